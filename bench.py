@@ -1,0 +1,418 @@
+#!/usr/bin/env python
+"""GatedDeltaNet chunked forward benchmark (B200, one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload per rank: B=1, T=4096, H=16, Dk=Dv=128, chunk 64, bf16 q/k/v
+(q,k ~ N(0,1) then L2-normalised, v ~ N(0,1)), fp32 g = -softplus(N(0,1)),
+beta = sigmoid(N(0,1)), initial state ~ N(0, 0.02), l2norm in the kernel,
+final state returned.  With N GPUs every rank runs its own shard of a global
+batch of N sequences (batch x head sharding, no collective): weak scaling.
+
+A step is one call of ``fast_chunk_gated_delta_rule`` over that batch.  Device
+time per step comes from CUDA events on the launching stream; a 256 MiB buffer
+(2x L2) is written between timed steps so every step starts with a cold L2.
+rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU
+algorithm (the oracle port; the reference is Python/PyTorch and has no
+compiled CPU code) on rank 0 with all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "GDN chunk-fwd tok/s @B=1,T=4096 (1/2/4/8 GPU) + % roofline; 0.8B decode tok/s"
+UNIT = "tok/s"
+D = 128
+CHUNK = 64
+# algorithmic bytes (fused I/O, intermediates excluded) per token per head:
+# q, k, v, o in bf16 (4 x 128 x 2) + g, beta in fp32
+BYTES_PER_TOKEN_HEAD = 4 * D * 2 + 8
+STATE_BYTES = D * D * 4
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--B", type=int, default=1, help="sequences per rank")
+    ap.add_argument("--T", type=int, default=4096)
+    ap.add_argument("--H", type=int, default=16)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget (rank 0, N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--soak-seconds", type=float, default=1.0, help="untimed load before timing (clock sampling)")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch from a committed ncu summary (profiles/traffic.json), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            t = json.load(f)
+        return t.get(workload, {}).get(kernel)
+    except Exception:
+        return None
+
+
+# --------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML every 50 ms."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples = []
+        self.ok = False
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML missing: report no clocks rather than guess
+            self.err = str(e)
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((time.perf_counter(), mhz, rs))
+            except Exception:
+                pass
+            time.sleep(0.05)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self, t0: float, t1: float):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        win = [s for s in self.samples if t0 <= s[0] <= t1] or self.samples
+        mhz = [s[1] for s in win]
+        bits = 0
+        for s in win:
+            bits |= s[2]
+        reasons = [n for b, n in self.REASONS.items() if bits & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(win)}
+
+
+# --------------------------------------------------------------------------- inputs
+
+def make_inputs(torch, B, T, H, seed, device):
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    q = torch.randn(B, T, H, D, device=device, generator=gen)
+    k = torch.randn(B, T, H, D, device=device, generator=gen)
+    q = (q / q.norm(dim=-1, keepdim=True)).bfloat16()
+    k = (k / k.norm(dim=-1, keepdim=True)).bfloat16()
+    v = torch.randn(B, T, H, D, device=device, generator=gen).bfloat16()
+    beta = torch.randn(B, T, H, device=device, generator=gen).sigmoid()
+    g = -torch.nn.functional.softplus(torch.randn(B, T, H, device=device, generator=gen))
+    s0 = torch.randn(B, H, D, D, device=device, generator=gen) * 0.02
+    return q, k, v, g, beta, s0
+
+
+# --------------------------------------------------------------------------- CPU (oracle port)
+
+def cpu_threads():
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        return max((i.get("num_threads", 1) for i in info), default=1)
+    except Exception:
+        return 1
+
+
+def time_oracle(T_sample, H, seconds=None, steps=None, warmup=0):
+    """Time the oracle port of torch_chunk_gated_delta_rule on a B=1, T_sample, H sample."""
+    import numpy as np
+
+    from oracle import gdn_oracle as O
+    q, k, v, g, beta, s0 = O.make_inputs(1, T_sample, H, seed=0, in_dtype="bf16", init_state_std=0.02)
+
+    def one():
+        O.chunk_gated_delta_rule(q, k, v, g, beta, initial_state=s0, output_final_state=True,
+                                 use_qk_l2norm_in_kernel=True, in_dtype="bf16")
+
+    for _ in range(warmup):
+        one()
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t)
+        if steps is not None and len(times) >= steps:
+            break
+        if seconds is not None and time.perf_counter() - t_start >= seconds and len(times) >= 2:
+            break
+    return times
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    T_sample = min(1024, args.T)
+    times = time_oracle(T_sample, args.H, steps=max(1, args.steps), warmup=max(0, args.warmup))
+    mean_s = statistics.mean(times)
+    value = args.B * T_sample / mean_s  # tok/s of the sample (the algorithm's cost is linear in T)
+    sample = f"B=1, first {T_sample} of T={args.T} tokens, H={args.H}, bf16 inputs (numpy oracle port)"
+    cores = cpu_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": len(times), "warmup": args.warmup, "ms_per_step": mean_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": f"gdn_chunk_fwd B={args.B} T={args.T} H={args.H} Dk=Dv=128 chunk=64 (CPU sample)",
+                   "global_batch": args.B, "seq_len": args.T, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is Python/PyTorch with no compiled CPU code; its algorithm runs as the numpy "
+                "port in oracle/gdn_oracle.py (pinned to the reference's own outputs)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from llms_from_scratch_b200 import _lib, fast_chunk_gated_delta_rule, fast_recurrent_gated_delta_rule
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    lib = _lib.load()
+    B, T, H = args.B, args.T, args.H
+    q, k, v, g, beta, s0 = make_inputs(torch, B, T, H, seed=1234 + rank, device=device)
+    ws = torch.empty(lib.gdn_chunk_workspace_bytes(B, T, H, D, D, _lib.GDN_BF16), dtype=torch.uint8, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def step():
+        return fast_chunk_gated_delta_rule(q, k, v, g, beta, chunk_size=CHUNK, initial_state=s0,
+                                           output_final_state=True, use_qk_l2norm_in_kernel=True, workspace=ws)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < args.soak_seconds:
+        for _ in range(10):
+            step()
+        torch.cuda.synchronize()
+
+    # ---- timed region: K steps, cold L2 before each
+    K = args.steps
+    n_phase = 3
+    outer = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    phase = [[torch.cuda.Event(enable_timing=True) for _ in range(n_phase)] for _ in range(K)]
+    for evs in phase:
+        for e in evs:
+            e.record()
+    for a, b in outer:
+        a.record()
+        b.record()
+    torch.cuda.synchronize()
+    phase_arrays = [(ctypes.c_void_p * n_phase)(*[e.cuda_event for e in evs]) for evs in phase]
+
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.gdn_launch_count()
+    t_timed0 = time.perf_counter()
+    for i in range(K):
+        flush.fill_(i & 0xFF)
+        lib.gdn_set_phase_events(phase_arrays[i], n_phase)
+        outer[i][0].record()
+        step()
+        outer[i][1].record()
+    lib.gdn_set_phase_events(None, 0)
+    torch.cuda.synchronize()
+    barrier()
+    t_timed1 = time.perf_counter()
+    launches = lib.gdn_launch_count() - launches0
+    step_ms = [a.elapsed_time(b) for a, b in outer]
+    prep_ms = [evs[0].elapsed_time(evs[1]) for evs in phase]
+    scan_ms = [evs[1].elapsed_time(evs[2]) for evs in phase]
+    ms_local = statistics.mean(step_ms)
+    ms = max_over_ranks(ms_local)
+    tokens_job = world * B * T
+    value = tokens_job / (ms / 1e3)
+
+    # ---- end to end through the public API with host buffers
+    hq, hk, hv, hg, hb, hs = (x.cpu().pin_memory() for x in (q, k, v, g, beta, s0))
+    ho = torch.empty((B, T, H, D), dtype=torch.bfloat16).pin_memory()
+    hst = torch.empty((B, H, D, D), dtype=torch.float32).pin_memory()
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hg, hb, hs))
+    d2h = ho.numel() * ho.element_size() + hst.numel() * hst.element_size()
+
+    def e2e_step():
+        dq, dk, dv, dg, db, ds = (x.to(device, non_blocking=True) for x in (hq, hk, hv, hg, hb, hs))
+        o, st = fast_chunk_gated_delta_rule(dq, dk, dv, dg, db, chunk_size=CHUNK, initial_state=ds,
+                                            output_final_state=True, use_qk_l2norm_in_kernel=True, workspace=ws)
+        ho.copy_(o, non_blocking=True)
+        hst.copy_(st, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(K):
+        flush.fill_(i & 0xFF)
+        e2e_ev[i][0].record()
+        e2e_step()
+        e2e_ev[i][1].record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in e2e_ev))
+    t_end = time.perf_counter()
+    clocks.stop()
+
+    # ---- decode step kernel (config 4 shape, one GatedDeltaNet layer at batch 32)
+    Bd = 32
+    dq_, dk_, dv_, dg_, db_, dst = make_inputs(torch, Bd, 1, H, seed=99 + rank, device=device)
+    dstate = dst.clone()
+    for _ in range(5):
+        fast_recurrent_gated_delta_rule(dq_, dk_, dv_, dg_, db_, dstate, True, use_qk_l2norm_in_kernel=True,
+                                        out_state=dstate)
+    dec_ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for e in dec_ev:
+        e.record()
+    torch.cuda.synchronize()
+    dec_arr = (ctypes.c_void_p * 2)(*[e.cuda_event for e in dec_ev])
+    dec_times = []
+    for i in range(20):
+        flush.fill_(i & 0xFF)
+        lib.gdn_set_phase_events(dec_arr, 2)
+        fast_recurrent_gated_delta_rule(dq_, dk_, dv_, dg_, db_, dstate, True, use_qk_l2norm_in_kernel=True,
+                                        out_state=dstate)
+        lib.gdn_set_phase_events(None, 0)
+        torch.cuda.synchronize()
+        dec_times.append(dec_ev[0].elapsed_time(dec_ev[1]))
+    dec_ms = statistics.median(dec_times)
+    dec_bytes = Bd * H * (2 * STATE_BYTES + 4 * D * 2 + 8)
+
+    # ---- roofline of the dominant kernel
+    peak, peak_kind = load_peaks()
+    prep_avg, scan_avg = statistics.mean(prep_ms), statistics.mean(scan_ms)
+    kernels = {
+        "gdn_prep": (prep_avg, B * H * T * (3 * D * 2 + 8)),                    # reads q, k, v, g, beta
+        "gdn_scan": (scan_avg, B * H * T * D * 2 + 2 * B * H * STATE_BYTES),  # writes o; state in + out
+    }
+    dom = max(kernels, key=lambda n: kernels[n][0])
+    dom_ms, dom_bytes = kernels[dom]
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    workload = f"B{B}_T{T}_H{H}_bf16"
+    traffic = load_traffic(dom, workload)
+    step_bytes = B * H * T * BYTES_PER_TOKEN_HEAD + 2 * B * H * STATE_BYTES
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        T_sample = min(1024, T)
+        times = time_oracle(T_sample, H, seconds=args.cpu_seconds, warmup=1)
+        cpu = {"value": T_sample / statistics.mean(times), "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+               "sample": f"B=1, first {T_sample} of T={T} tokens, H={H}, bf16 inputs, {len(times)} runs "
+                         f"(numpy oracle port of torch_chunk_gated_delta_rule)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": f"gdn_chunk_fwd B={B} T={T} H={H} Dk=Dv=128 chunk=64 bf16 q/k/v, fp32 g/beta/"
+                                   "state, l2norm in kernel, final state out",
+                       "global_batch": world * B, "seq_len": T, "heads": H,
+                       "parallelism": f"batch-shard x{world} (no collective)",
+                       "l2": "256 MiB buffer written between timed steps (cold L2)"},
+            "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms},
+            "step_roofline": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_bytes / (ms / 1e3) / 1e9,
+                              "frac": step_bytes / (ms / 1e3) / 1e9 / peak},
+            "kernels_ms": {"gdn_prep": prep_avg, "gdn_scan": scan_avg},
+            "e2e": {"value": tokens_job / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": launches,
+            "clocks": clocks.summary(t_soak, t_end),
+            "decode_step": {"workload": f"recurrent step B={Bd} H={H} (one GatedDeltaNet layer)",
+                            "ms": dec_ms, "achieved_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
+                            "frac_hbm": dec_bytes / (dec_ms / 1e3) / 1e9 / peak},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,120 @@
+/*
+ * gdn_b200.h - C ABI of the B200 (sm_100a) GatedDeltaNet kernels.
+ *
+ * The reference (pbanavara/llms_from_scratch) exposes this path as two Python
+ * callables; every entry point below names the reference interface it replaces:
+ *
+ *   fast_chunk_gated_delta_rule      qwen3_5_cutedsl_kernels.py:462-473
+ *   torch_chunk_gated_delta_rule     qwen3_5_transformers.py:110-120
+ *   torch_recurrent_gated_delta_rule qwen3_5_transformers.py:190-192
+ *
+ * Conventions (same as the reference):
+ *   query, key   [B, T, H, Dk]      value, out  [B, T, H, Dv]
+ *   g, beta      [B, T, H]          g is the per-token log-decay (not cumsummed)
+ *   states       [B, H, Dk, Dv]     float32, row-major, contiguous
+ * `out` has query's dtype.  Dk = Dv = 128 and chunk_size = 64 are required.
+ * Tensors may be strided in B, T and H; the innermost (head) dimension must be
+ * contiguous.  All calls are asynchronous on `stream` (a cudaStream_t; NULL is
+ * the legacy default stream) and allocate no device memory: the chunked
+ * forward takes a caller-owned workspace of gdn_chunk_workspace_bytes() bytes.
+ *
+ * Every function returns a gdn_status; gdn_last_error() gives a message for
+ * the most recent failure on the calling host thread.
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+typedef enum {
+    GDN_OK = 0,
+    GDN_ERR_INVALID_ARGUMENT = 1, /* shape, stride, dtype or flag not supported (Python: ValueError) */
+    GDN_ERR_UNSUPPORTED = 2,      /* valid request this build cannot run (Python: RuntimeError)    */
+    GDN_ERR_WORKSPACE = 3,        /* workspace missing, too small or misaligned                    */
+    GDN_ERR_CUDA = 4,             /* a CUDA runtime call or kernel launch failed                   */
+    GDN_ERR_DEVICE = 5            /* the current device is not an sm_100 GPU                       */
+} gdn_status;
+
+typedef enum { GDN_F32 = 0, GDN_BF16 = 1, GDN_F16 = 2 } gdn_dtype;
+
+/* A strided view of device memory.  Unused trailing dims have size 1. */
+typedef struct {
+    void* data;        /* device pointer                                   */
+    int32_t dtype;     /* gdn_dtype                                        */
+    int32_t ndim;      /* 3 for g/beta, 4 for q/k/v/out                     */
+    int64_t shape[4];
+    int64_t stride[4]; /* in elements                                      */
+} gdn_tensor;
+
+/* Chunked gated delta rule forward (prefill).
+ *
+ * Replaces fast_chunk_gated_delta_rule(query, key, value, g, beta, chunk_size,
+ * initial_state, output_final_state, use_qk_l2norm_in_kernel)
+ * (qwen3_5_cutedsl_kernels.py:462-473) and its oracle
+ * torch_chunk_gated_delta_rule (qwen3_5_transformers.py:110-187).
+ *   initial_state  NULL for a zero state (qwen3_5_transformers.py:161-165)
+ *   final_state    written when output_final_state != 0; may alias initial_state
+ *   workspace      >= gdn_chunk_workspace_bytes(...) bytes, 256-byte aligned
+ */
+GDN_API int gdn_chunk_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
+                               const gdn_tensor* g, const gdn_tensor* beta, int chunk_size,
+                               const float* initial_state, int output_final_state,
+                               int use_qk_l2norm_in_kernel, gdn_tensor* out, float* final_state,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes gdn_chunk_gated_delta_rule needs for this problem. */
+GDN_API size_t gdn_chunk_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int qkv_dtype);
+
+/* Token-by-token recurrent rule (decode step when T == 1).
+ *
+ * Replaces torch_recurrent_gated_delta_rule(query, key, value, g, beta,
+ * initial_state, output_final_state, use_qk_l2norm_in_kernel)
+ * (qwen3_5_transformers.py:190-229).  final_state may alias initial_state
+ * (in-place decode).  No workspace.
+ */
+GDN_API int gdn_recurrent_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
+                                   const gdn_tensor* g, const gdn_tensor* beta, const float* initial_state,
+                                   int output_final_state, int use_qk_l2norm_in_kernel, gdn_tensor* out,
+                                   float* final_state, void* stream);
+
+/* Instrumentation (no counterpart in the reference, which times whole calls
+ * with CUDA events, benchmark.py:82-100).
+ *
+ * gdn_launch_count: number of kernels this library has launched in this
+ * process (all devices, all threads).
+ *
+ * gdn_set_phase_events: when `events` is non-NULL, every later call on this
+ * host thread records events[0] on its stream before its first kernel and
+ * events[i] after its i-th kernel (i = 1..n-1 must cover the kernels of the
+ * call: 2 for the chunked forward, 1 for the recurrent rule).  Entries are
+ * cudaEvent_t handles.  Pass NULL to stop. */
+GDN_API uint64_t gdn_launch_count(void);
+GDN_API void gdn_set_phase_events(void* const* events, int n);
+
+/* Message for the most recent failure on this host thread ("" if none). */
+GDN_API const char* gdn_last_error(void);
+
+/* Name of a gdn_status value. */
+GDN_API const char* gdn_status_name(int status);
+
+/* GDN_ABI_VERSION of the loaded library. */
+GDN_API int gdn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */

@@ -1,0 +1,261 @@
+// C ABI: argument validation, dispatch and error reporting.
+//
+// Mirrors the reference's Python contract for this path
+// (fast_chunk_gated_delta_rule, qwen3_5_cutedsl_kernels.py:462-567;
+//  torch_recurrent_gated_delta_rule, qwen3_5_transformers.py:190-229):
+// same argument meaning, output in the query dtype, final state in fp32,
+// inputs never modified.  Where the reference raises, this returns
+// GDN_ERR_INVALID_ARGUMENT / GDN_ERR_UNSUPPORTED with a message.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "gdn_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local void* const* g_phase_events = nullptr;
+thread_local int g_phase_event_count = 0;
+std::atomic<uint64_t> g_launches{0};
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(GDN_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool valid_dtype(int d) { return d == GDN_F32 || d == GDN_BF16 || d == GDN_F16; }
+
+// The kernels are compiled for sm_100a only; anything else cannot load them.
+int check_device() {
+    static int major_of[64];
+    static bool known[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(GDN_ERR_DEVICE, "device ordinal %d out of range", dev);
+    if (!known[dev]) {
+        int major = 0;
+        e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        major_of[dev] = major;
+        known[dev] = true;
+    }
+    if (major_of[dev] != 10)
+        return fail(GDN_ERR_DEVICE, "device %d has compute capability %d.x; this library is built for sm_100a (B200)",
+                    dev, major_of[dev]);
+    return GDN_OK;
+}
+
+int check4(const char* name, const gdn_tensor* t, int64_t B, int64_t T, int64_t H, int64_t D) {
+    if (!t) return fail(GDN_ERR_INVALID_ARGUMENT, "%s is NULL", name);
+    if (t->ndim != 4) return fail(GDN_ERR_INVALID_ARGUMENT, "%s must be 4-D [B,T,H,D], got ndim=%d", name, t->ndim);
+    if (!valid_dtype(t->dtype)) return fail(GDN_ERR_INVALID_ARGUMENT, "%s has unsupported dtype code %d", name, t->dtype);
+    const int64_t want[4] = {B, T, H, D};
+    for (int i = 0; i < 4; ++i)
+        if (t->shape[i] != want[i])
+            return fail(GDN_ERR_INVALID_ARGUMENT, "%s has shape [%lld,%lld,%lld,%lld], expected [%lld,%lld,%lld,%lld]", name,
+                        (long long)t->shape[0], (long long)t->shape[1], (long long)t->shape[2], (long long)t->shape[3],
+                        (long long)B, (long long)T, (long long)H, (long long)D);
+    if (t->stride[3] != 1)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "%s: the head dimension must be contiguous (stride %lld)", name,
+                    (long long)t->stride[3]);
+    if (B * T * H > 0 && !t->data) return fail(GDN_ERR_INVALID_ARGUMENT, "%s has a NULL data pointer", name);
+    return GDN_OK;
+}
+
+int check3(const char* name, const gdn_tensor* t, int64_t B, int64_t T, int64_t H) {
+    if (!t) return fail(GDN_ERR_INVALID_ARGUMENT, "%s is NULL", name);
+    if (t->ndim != 3) return fail(GDN_ERR_INVALID_ARGUMENT, "%s must be 3-D [B,T,H], got ndim=%d", name, t->ndim);
+    if (!valid_dtype(t->dtype)) return fail(GDN_ERR_INVALID_ARGUMENT, "%s has unsupported dtype code %d", name, t->dtype);
+    if (t->shape[0] != B || t->shape[1] != T || t->shape[2] != H)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "%s has shape [%lld,%lld,%lld], expected [%lld,%lld,%lld]", name,
+                    (long long)t->shape[0], (long long)t->shape[1], (long long)t->shape[2], (long long)B, (long long)T,
+                    (long long)H);
+    if (B * T * H > 0 && !t->data) return fail(GDN_ERR_INVALID_ARGUMENT, "%s has a NULL data pointer", name);
+    return GDN_OK;
+}
+
+gdn::View4 view4(const gdn_tensor* t) { return {t->data, t->stride[0], t->stride[1], t->stride[2], t->dtype}; }
+gdn::View3 view3(const gdn_tensor* t) { return {t->data, t->stride[0], t->stride[1], t->stride[2], t->dtype}; }
+
+// Shared checks of the two entry points; fills B, T, H.
+int check_common(const gdn_tensor* q, const gdn_tensor* k, const gdn_tensor* v, const gdn_tensor* g,
+                 const gdn_tensor* beta, const gdn_tensor* out, const float* h0, int output_final_state,
+                 const float* hT, int64_t* B, int64_t* T, int64_t* H) {
+    if (!q) return fail(GDN_ERR_INVALID_ARGUMENT, "query is NULL");
+    if (q->ndim != 4) return fail(GDN_ERR_INVALID_ARGUMENT, "query must be 4-D [B,T,H,Dk], got ndim=%d", q->ndim);
+    *B = q->shape[0];
+    *T = q->shape[1];
+    *H = q->shape[2];
+    if (*B < 0 || *T < 0 || *H < 0) return fail(GDN_ERR_INVALID_ARGUMENT, "negative dimension in query");
+    if (q->shape[3] != gdn::kDk)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "key head dim must be %d, got %lld", gdn::kDk, (long long)q->shape[3]);
+    if (!v) return fail(GDN_ERR_INVALID_ARGUMENT, "value is NULL");
+    if (v->ndim == 4 && v->shape[3] != gdn::kDv)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "value head dim must be %d, got %lld", gdn::kDv, (long long)v->shape[3]);
+    int rc;
+    if ((rc = check4("query", q, *B, *T, *H, gdn::kDk))) return rc;
+    if ((rc = check4("key", k, *B, *T, *H, gdn::kDk))) return rc;
+    if ((rc = check4("value", v, *B, *T, *H, gdn::kDv))) return rc;
+    if ((rc = check3("g", g, *B, *T, *H))) return rc;
+    if ((rc = check3("beta", beta, *B, *T, *H))) return rc;
+    if ((rc = check4("out", out, *B, *T, *H, gdn::kDv))) return rc;
+    if (*B * *H > 0x7fffffffLL) return fail(GDN_ERR_INVALID_ARGUMENT, "B*H too large");
+    if (h0 && (reinterpret_cast<uintptr_t>(h0) & 15))
+        return fail(GDN_ERR_INVALID_ARGUMENT, "initial_state must be 16-byte aligned");
+    if (output_final_state && !hT && *B * *H > 0)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "output_final_state is set but final_state is NULL");
+    if (hT && (reinterpret_cast<uintptr_t>(hT) & 15))
+        return fail(GDN_ERR_INVALID_ARGUMENT, "final_state must be 16-byte aligned");
+    return GDN_OK;
+}
+
+// T == 0: no tokens; the final state is the initial state (or zeros).
+int empty_sequence(int64_t B, int64_t H, const float* h0, float* hT, cudaStream_t stream) {
+    if (!hT) return GDN_OK;
+    const size_t bytes = (size_t)B * H * gdn::kDk * gdn::kDv * sizeof(float);
+    cudaError_t e = cudaSuccess;
+    if (!h0) e = cudaMemsetAsync(hT, 0, bytes, stream);
+    else if (h0 != hT) e = cudaMemcpyAsync(hT, h0, bytes, cudaMemcpyDeviceToDevice, stream);
+    return e == cudaSuccess ? GDN_OK : cuda_fail(e, "final state copy");
+}
+
+}  // namespace
+
+namespace gdn {
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+cudaError_t phase_event(int index, cudaStream_t stream) {
+    if (!g_phase_events || index >= g_phase_event_count || !g_phase_events[index]) return cudaSuccess;
+    return cudaEventRecord(reinterpret_cast<cudaEvent_t>(g_phase_events[index]), stream);
+}
+
+}  // namespace gdn
+
+extern "C" {
+
+uint64_t gdn_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+void gdn_set_phase_events(void* const* events, int n) {
+    g_phase_events = events;
+    g_phase_event_count = events ? n : 0;
+}
+
+size_t gdn_chunk_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int qkv_dtype) {
+    (void)Dk;
+    (void)Dv;
+    (void)qkv_dtype;
+    if (B <= 0 || T <= 0 || H <= 0) return 0;
+    const int64_t NC = (T + gdn::kChunk - 1) / gdn::kChunk;
+    return (size_t)(B * H * NC) * (size_t)gdn::kWsChunkFloats * sizeof(float);
+}
+
+int gdn_chunk_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
+                               const gdn_tensor* g, const gdn_tensor* beta, int chunk_size,
+                               const float* initial_state, int output_final_state, int use_qk_l2norm_in_kernel,
+                               gdn_tensor* out, float* final_state, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+    g_last_error.clear();
+    if (chunk_size != gdn::kChunk)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "chunk_size must be %d, got %d", gdn::kChunk, chunk_size);
+    int64_t B, T, H;
+    int rc = check_common(query, key, value, g, beta, out, initial_state, output_final_state, final_state, &B, &T, &H);
+    if (rc) return rc;
+    if ((rc = check_device())) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    float* hT = output_final_state ? final_state : nullptr;
+    if (B * H == 0) return GDN_OK;
+    if (T == 0) return empty_sequence(B, H, initial_state, hT, st);
+
+    const size_t need = gdn_chunk_workspace_bytes(B, T, H, gdn::kDk, gdn::kDv, query->dtype);
+    if (!workspace || workspace_bytes < need)
+        return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace ? workspace_bytes : 0);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(GDN_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+
+    gdn::ChunkParams p{};
+    p.q = view4(query);
+    p.k = view4(key);
+    p.v = view4(value);
+    p.g = view3(g);
+    p.beta = view3(beta);
+    p.out = out->data;
+    p.out_sb = out->stride[0];
+    p.out_st = out->stride[1];
+    p.out_sh = out->stride[2];
+    p.out_dtype = out->dtype;
+    p.h0 = initial_state;
+    p.hT = hT;
+    p.ws = reinterpret_cast<float*>(workspace);
+    p.B = (int)B;
+    p.H = (int)H;
+    p.T = T;
+    p.NC = (int)((T + gdn::kChunk - 1) / gdn::kChunk);
+    p.l2norm = use_qk_l2norm_in_kernel ? 1 : 0;
+    cudaError_t e = gdn::launch_chunk_simt(p, st);
+    return e == cudaSuccess ? GDN_OK : cuda_fail(e, "chunk kernels launch");
+}
+
+int gdn_recurrent_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
+                                   const gdn_tensor* g, const gdn_tensor* beta, const float* initial_state,
+                                   int output_final_state, int use_qk_l2norm_in_kernel, gdn_tensor* out,
+                                   float* final_state, void* stream) {
+    g_last_error.clear();
+    int64_t B, T, H;
+    int rc = check_common(query, key, value, g, beta, out, initial_state, output_final_state, final_state, &B, &T, &H);
+    if (rc) return rc;
+    if ((rc = check_device())) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    float* hT = output_final_state ? final_state : nullptr;
+    if (B * H == 0) return GDN_OK;
+    if (T == 0) return empty_sequence(B, H, initial_state, hT, st);
+
+    gdn::RecurrentParams p{};
+    p.q = view4(query);
+    p.k = view4(key);
+    p.v = view4(value);
+    p.g = view3(g);
+    p.beta = view3(beta);
+    p.out = out->data;
+    p.out_sb = out->stride[0];
+    p.out_st = out->stride[1];
+    p.out_sh = out->stride[2];
+    p.out_dtype = out->dtype;
+    p.h0 = initial_state;
+    p.hT = hT;
+    p.B = (int)B;
+    p.H = (int)H;
+    p.T = T;
+    p.l2norm = use_qk_l2norm_in_kernel ? 1 : 0;
+    cudaError_t e = gdn::launch_recurrent(p, st);
+    return e == cudaSuccess ? GDN_OK : cuda_fail(e, "recurrent kernel launch");
+}
+
+const char* gdn_last_error(void) { return g_last_error.c_str(); }
+
+const char* gdn_status_name(int status) {
+    switch (status) {
+        case GDN_OK: return "GDN_OK";
+        case GDN_ERR_INVALID_ARGUMENT: return "GDN_ERR_INVALID_ARGUMENT";
+        case GDN_ERR_UNSUPPORTED: return "GDN_ERR_UNSUPPORTED";
+        case GDN_ERR_WORKSPACE: return "GDN_ERR_WORKSPACE";
+        case GDN_ERR_CUDA: return "GDN_ERR_CUDA";
+        case GDN_ERR_DEVICE: return "GDN_ERR_DEVICE";
+        default: return "GDN_UNKNOWN_STATUS";
+    }
+}
+
+int gdn_abi_version(void) { return GDN_ABI_VERSION; }
+
+}  // extern "C"

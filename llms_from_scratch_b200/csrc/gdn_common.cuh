@@ -1,0 +1,70 @@
+// Shared device helpers for the GatedDeltaNet kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gdn_b200.h"
+
+namespace gdn {
+
+constexpr int kChunk = 64;   // tokens per chunk (the reference's chunk_size)
+constexpr int kDk = 128;     // key head dim
+constexpr int kDv = 128;     // value head dim
+
+// Strided view handed to kernels: element pointer + strides in elements.
+struct View4 {
+    const void* p;
+    int64_t sb, st, sh;  // batch, time, head strides; the head dim is contiguous
+    int dtype;
+};
+struct View3 {
+    const void* p;
+    int64_t sb, st, sh;
+    int dtype;
+};
+
+__device__ __forceinline__ float load_elem(const void* base, int64_t idx, int dtype) {
+    if (dtype == GDN_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+    if (dtype == GDN_F16) return __half2float(reinterpret_cast<const __half*>(base)[idx]);
+    return reinterpret_cast<const float*>(base)[idx];
+}
+
+__device__ __forceinline__ void store_elem(void* base, int64_t idx, int dtype, float x) {
+    if (dtype == GDN_BF16) reinterpret_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(x);
+    else if (dtype == GDN_F16) reinterpret_cast<__half*>(base)[idx] = __float2half_rn(x);
+    else reinterpret_cast<float*>(base)[idx] = x;
+}
+
+// Round an fp32 value to `dtype` and back (identity for fp32): reproduces the
+// roundings a torch op in that dtype would do.
+__device__ __forceinline__ float round_to(float x, int dtype) {
+    if (dtype == GDN_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+    if (dtype == GDN_F16) return __half2float(__float2half_rn(x));
+    return x;
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
+// Inverse L2 norm of a 128-vector spread 4 elements per lane over one warp,
+// evaluated the way `x * rsqrt((x*x).sum(-1) + 1e-6)` runs in `dtype`
+// (qwen3_5_transformers.py:104-107): for 16-bit inputs every elementwise
+// result is rounded to that dtype and the sum accumulates in fp32.
+__device__ __forceinline__ float l2norm_inv(const float (&x)[4], int dtype) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s += round_to(x[i] * x[i], dtype);
+    s = warp_sum(s);
+    if (dtype == GDN_F32) return 1.0f / sqrtf(s + 1e-6f);
+    s = round_to(s, dtype);
+    s = round_to(s + 1e-6f, dtype);
+    return round_to(1.0f / sqrtf(s), dtype);
+}
+
+}  // namespace gdn

@@ -1,0 +1,191 @@
+"""Drop-in GatedDeltaNet ops backed by the sm_100a CUDA library.
+
+``fast_chunk_gated_delta_rule`` keeps the reference's exact signature
+(qwen3_5_cutedsl_kernels.py:462-473) and return convention
+(``(out [B,T,H,Dv] in query.dtype, final_state [B,H,Dk,Dv] fp32 or None)``).
+``fast_recurrent_gated_delta_rule`` keeps the signature of
+``torch_recurrent_gated_delta_rule`` (qwen3_5_transformers.py:190-192).
+
+Both allocate their outputs (the caller owns them), never modify inputs, run
+asynchronously on the current CUDA stream, and raise ``RuntimeError`` (a
+``GDNError``) on bad arguments, as the reference's torch ops do.  CPU tensors
+raise: there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.GDN_F32, torch.bfloat16: _lib.GDN_BF16, torch.float16: _lib.GDN_F16}
+
+# backend names accepted for drop-in compatibility; all run this package's CUDA kernels
+_CUDA_BACKENDS = ("auto", "cuda", "b200", "triton", "cute")
+
+
+def l2norm(x: torch.Tensor, dim: int = -1, eps: float = 1e-6) -> torch.Tensor:
+    """Same as the reference helper (qwen3_5_cutedsl_kernels.py:100-101)."""
+    return x * torch.rsqrt((x * x).sum(dim=dim, keepdim=True) + eps)
+
+
+def get_backend() -> str:
+    """The backend ``backend="auto"`` resolves to (qwen3_5_cutedsl_kernels.py:104-109)."""
+    return "cuda"
+
+
+def _as_kernel_tensor(x: torch.Tensor, name: str, ndim: int) -> torch.Tensor:
+    if not isinstance(x, torch.Tensor):
+        raise RuntimeError(f"{name} must be a torch.Tensor")
+    if x.dim() != ndim:
+        raise RuntimeError(f"{name} must have {ndim} dims, got shape {tuple(x.shape)}")
+    if x.device.type != "cuda":
+        raise RuntimeError(f"{name} is on {x.device}; the GatedDeltaNet kernels need CUDA tensors (no CPU path)")
+    if x.dtype not in _DTYPES:
+        x = x.float()
+    if ndim == 4 and x.shape[-1] > 1 and x.stride(-1) != 1:
+        x = x.contiguous()
+    return x
+
+
+def _desc(x: torch.Tensor) -> _lib.GdnTensor:
+    d = _lib.GdnTensor()
+    d.data = x.data_ptr() if x.numel() > 0 else 0
+    d.dtype = _DTYPES[x.dtype]
+    d.ndim = x.dim()
+    for i in range(4):
+        d.shape[i] = x.shape[i] if i < x.dim() else 1
+        d.stride[i] = x.stride(i) if i < x.dim() else 1
+    return d
+
+
+def _state_in(initial_state: Optional[torch.Tensor], B, H, Dk, Dv, device) -> Optional[torch.Tensor]:
+    if initial_state is None:
+        return None
+    if tuple(initial_state.shape) != (B, H, Dk, Dv):
+        raise RuntimeError(f"initial_state must have shape {(B, H, Dk, Dv)}, got {tuple(initial_state.shape)}")
+    if initial_state.device != device:
+        raise RuntimeError(f"initial_state is on {initial_state.device}, expected {device}")
+    return initial_state.to(torch.float32).contiguous()
+
+
+def _check_backend(backend: str) -> None:
+    if backend == "torch":
+        raise RuntimeError("backend 'torch' is the reference's pure-PyTorch path; this package runs only its "
+                           "CUDA kernels (use backend='auto')")
+    if backend not in _CUDA_BACKENDS:
+        raise RuntimeError(f"Requested backend '{backend}' is not available.")
+
+
+def fast_chunk_gated_delta_rule(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    g: torch.Tensor,
+    beta: torch.Tensor,
+    chunk_size: int = 64,
+    initial_state: Optional[torch.Tensor] = None,
+    output_final_state: bool = False,
+    use_qk_l2norm_in_kernel: bool = False,
+    backend: str = "auto",
+    workspace: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Chunked gated delta rule forward on the GPU.
+
+    Drop-in for the reference's ``fast_chunk_gated_delta_rule``: same
+    arguments, layouts (``[B,T,H,D]``) and outputs.  ``workspace`` optionally
+    supplies a reusable uint8 CUDA buffer of at least
+    ``chunk_workspace_bytes(...)`` bytes (allocated per call otherwise).
+    """
+    _check_backend(backend)
+    q = _as_kernel_tensor(query, "query", 4)
+    k = _as_kernel_tensor(key, "key", 4)
+    v = _as_kernel_tensor(value, "value", 4)
+    gg = _as_kernel_tensor(g, "g", 3)
+    bb = _as_kernel_tensor(beta, "beta", 3)
+    B, T, H, Dk = q.shape
+    Dv = v.shape[-1]
+    dev = q.device
+    for name, x in (("key", k), ("value", v), ("g", gg), ("beta", bb)):
+        if x.device != dev:
+            raise RuntimeError(f"{name} is on {x.device}, query on {dev}")
+    h0 = _state_in(initial_state, B, H, Dk, Dv, dev)
+    out_dtype = query.dtype
+    out = torch.empty((B, T, H, Dv), dtype=q.dtype, device=dev)
+    final = torch.empty((B, H, Dk, Dv), dtype=torch.float32, device=dev) if output_final_state else None
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        ws_bytes = lib.gdn_chunk_workspace_bytes(B, T, H, Dk, Dv, _DTYPES[q.dtype])
+        if workspace is None or workspace.numel() < ws_bytes:
+            workspace = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+        dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.gdn_chunk_gated_delta_rule(
+            ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(dg), ctypes.byref(db),
+            int(chunk_size), h0.data_ptr() if h0 is not None else None, int(bool(output_final_state)),
+            int(bool(use_qk_l2norm_in_kernel)), ctypes.byref(do),
+            final.data_ptr() if final is not None else None, workspace.data_ptr(), workspace.numel(), stream)
+        _lib.check(rc)
+    if out.dtype != out_dtype:
+        out = out.to(out_dtype)
+    return out, final
+
+
+def chunk_workspace_bytes(B: int, T: int, H: int, Dk: int = 128, Dv: int = 128,
+                          dtype: torch.dtype = torch.bfloat16) -> int:
+    return int(_lib.load().gdn_chunk_workspace_bytes(B, T, H, Dk, Dv, _DTYPES.get(dtype, _lib.GDN_F32)))
+
+
+def fast_recurrent_gated_delta_rule(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    g: torch.Tensor,
+    beta: torch.Tensor,
+    initial_state: Optional[torch.Tensor],
+    output_final_state: bool,
+    use_qk_l2norm_in_kernel: bool = False,
+    out_state: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Token-recurrent gated delta rule (the decode step) on the GPU.
+
+    Same contract as ``torch_recurrent_gated_delta_rule``.  ``out_state``
+    optionally names an fp32 ``[B,H,Dk,Dv]`` tensor to receive the final state;
+    it may be ``initial_state`` itself for an in-place decode update.
+    """
+    q = _as_kernel_tensor(query, "query", 4)
+    k = _as_kernel_tensor(key, "key", 4)
+    v = _as_kernel_tensor(value, "value", 4)
+    gg = _as_kernel_tensor(g, "g", 3)
+    bb = _as_kernel_tensor(beta, "beta", 3)
+    B, T, H, Dk = q.shape
+    Dv = v.shape[-1]
+    dev = q.device
+    h0 = _state_in(initial_state, B, H, Dk, Dv, dev)
+    out_dtype = query.dtype
+    out = torch.empty((B, T, H, Dv), dtype=q.dtype, device=dev)
+    final = None
+    if output_final_state:
+        if out_state is not None:
+            if (out_state.dtype != torch.float32 or tuple(out_state.shape) != (B, H, Dk, Dv)
+                    or not out_state.is_contiguous() or out_state.device != dev):
+                raise RuntimeError("out_state must be a contiguous fp32 [B,H,Dk,Dv] tensor on the query's device")
+            final = out_state
+        else:
+            final = torch.empty((B, H, Dk, Dv), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.gdn_recurrent_gated_delta_rule(
+            ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(dg), ctypes.byref(db),
+            h0.data_ptr() if h0 is not None else None, int(bool(output_final_state)),
+            int(bool(use_qk_l2norm_in_kernel)), ctypes.byref(do),
+            final.data_ptr() if final is not None else None, stream)
+        _lib.check(rc)
+    if out.dtype != out_dtype:
+        out = out.to(out_dtype)
+    return out, final

@@ -1,0 +1,150 @@
+"""The C-ABI library loads, exports every symbol include/*.h declares, and
+rejects bad arguments with the reference's error behaviour -- all without a GPU
+(validation runs before any CUDA call)."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from llms_from_scratch_b200 import _lib
+from llms_from_scratch_b200.build import build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _lib.load()
+
+
+def _declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        names.update(re.findall(r"GDN_API\s+[\w\s\*]+?\b(gdn_\w+)\s*\(", src))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = _declared_symbols()
+    assert {"gdn_chunk_gated_delta_rule", "gdn_recurrent_gated_delta_rule", "gdn_chunk_workspace_bytes"} <= names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in sorted(_declared_symbols()):
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+    # and the Python binding types every one of them
+    assert _declared_symbols() <= set(_lib.SIGNATURES)
+
+
+def test_abi_version_and_status_names(lib):
+    assert lib.gdn_abi_version() == 1
+    assert lib.gdn_status_name(0) == b"GDN_OK"
+    assert lib.gdn_status_name(1) == b"GDN_ERR_INVALID_ARGUMENT"
+    assert lib.gdn_status_name(99) == b"GDN_UNKNOWN_STATUS"
+
+
+def test_workspace_size(lib):
+    assert lib.gdn_chunk_workspace_bytes(0, 10, 1, 128, 128, 1) == 0
+    a = lib.gdn_chunk_workspace_bytes(1, 64, 1, 128, 128, 1)
+    assert a > 0 and a % 256 == 0
+    assert lib.gdn_chunk_workspace_bytes(1, 65, 1, 128, 128, 1) == 2 * a
+    assert lib.gdn_chunk_workspace_bytes(3, 4096, 16, 128, 128, 1) == 3 * 16 * 64 * a
+
+
+def _t(shape, dtype=_lib.GDN_BF16, data=0x1000):
+    d = _lib.GdnTensor()
+    d.data = data
+    d.dtype = dtype
+    d.ndim = len(shape)
+    st = 1
+    strides = []
+    for s in reversed(shape):
+        strides.append(st)
+        st *= s
+    strides = list(reversed(strides))
+    for i in range(4):
+        d.shape[i] = shape[i] if i < len(shape) else 1
+        d.stride[i] = strides[i] if i < len(shape) else 1
+    return d
+
+
+def _call_chunk(lib, q, k, v, g, b, out, chunk=64, ws=0x100000, ws_bytes=1 << 40):
+    return lib.gdn_chunk_gated_delta_rule(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v), ctypes.byref(g),
+                                          ctypes.byref(b), chunk, None, 0, 1, ctypes.byref(out), None, ws,
+                                          ws_bytes, None)
+
+
+@pytest.mark.parametrize("case,needle", [
+    ("chunk", "chunk_size must be 64"),
+    ("dk", "key head dim must be 128"),
+    ("dv", "value head dim must be 128"),
+    ("gshape", "g has shape"),
+    ("stride", "head dimension must be contiguous"),
+    ("dtype", "unsupported dtype"),
+])
+def test_invalid_arguments_are_rejected_before_any_cuda_call(lib, case, needle):
+    B, T, H = 1, 70, 2
+    q, k, v = _t([B, T, H, 128]), _t([B, T, H, 128]), _t([B, T, H, 128])
+    g, b = _t([B, T, H], _lib.GDN_F32), _t([B, T, H], _lib.GDN_F32)
+    out = _t([B, T, H, 128])
+    chunk = 64
+    if case == "chunk":
+        chunk = 32
+    elif case == "dk":
+        q, k = _t([B, T, H, 64]), _t([B, T, H, 64])
+    elif case == "dv":
+        v, out = _t([B, T, H, 64]), _t([B, T, H, 64])
+    elif case == "gshape":
+        g = _t([B, T + 1, H], _lib.GDN_F32)
+    elif case == "stride":
+        k.stride[3] = 2
+    elif case == "dtype":
+        v.dtype = 7
+    rc = _call_chunk(lib, q, k, v, g, b, out, chunk=chunk)
+    assert rc == _lib.GDN_ERR_INVALID_ARGUMENT
+    assert needle in lib.gdn_last_error().decode()
+    with pytest.raises(_lib.GDNError, match="GDN_ERR_INVALID_ARGUMENT"):
+        _lib.check(rc)
+
+
+def test_final_state_pointer_required(lib):
+    B, T, H = 1, 8, 1
+    q, k, v, out = (_t([B, T, H, 128]) for _ in range(4))
+    g, b = _t([B, T, H], _lib.GDN_F32), _t([B, T, H], _lib.GDN_F32)
+    rc = lib.gdn_recurrent_gated_delta_rule(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v), ctypes.byref(g),
+                                            ctypes.byref(b), None, 1, 1, ctypes.byref(out), None, None)
+    assert rc == _lib.GDN_ERR_INVALID_ARGUMENT
+    assert "final_state" in lib.gdn_last_error().decode()
+
+
+def test_python_op_refuses_cpu_tensors_and_torch_backend():
+    import torch
+
+    from llms_from_scratch_b200 import fast_chunk_gated_delta_rule, fast_recurrent_gated_delta_rule
+    q = torch.zeros(1, 4, 1, 128)
+    g = torch.zeros(1, 4, 1)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        fast_chunk_gated_delta_rule(q, q, q, g, g)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        fast_recurrent_gated_delta_rule(q, q, q, g, g, None, False)
+    with pytest.raises(RuntimeError, match="pure-PyTorch"):
+        fast_chunk_gated_delta_rule(q, q, q, g, g, backend="torch")
+    with pytest.raises(RuntimeError, match="not available"):
+        fast_chunk_gated_delta_rule(q, q, q, g, g, backend="nope")
+
+
+def test_compat_module_exports_reference_names():
+    import importlib
+    import sys
+    sys.path.insert(0, os.path.join(ROOT, "llms_from_scratch_b200", "compat"))
+    try:
+        m = importlib.import_module("qwen3_5_cutedsl_kernels")
+        for name in ("fast_chunk_gated_delta_rule", "get_backend", "_TRITON_OK", "_CUTE_OK", "l2norm"):
+            assert hasattr(m, name)
+        assert m.get_backend() in ("cuda",)
+    finally:
+        sys.path.pop(0)
