@@ -85,13 +85,28 @@ def test_against_reference_golden_vectors(path):
     d = {k: z[k] for k in z.files}
     kind, in_dtype = str(d["kind"]), str(d["in_dtype"])
     fn = run_chunk if kind == "chunk" else run_rec
+    ref_o = O.from_bf16_bits(d["out"]) if in_dtype == "bf16" else d["out"]
+    if "q_l2" in d:
+        # 16-bit fixture: start from the reference's own normalised q/k (torch's CPU
+        # bf16 rsqrt is a hardware estimate), which pins the rest of the arithmetic
+        # at the full tolerance ...
+        o, s = fn(d["q_l2"], d["k_l2"], d["v"], d["g"], d["beta"], d.get("initial_state"), in_dtype,
+                  l2=False, ofs=bool(d["output_final_state"]))
+        assert_parity(o, ref_o, in_dtype, "out (reference-normalised q/k)")
+        if "final_state" in d:
+            assert_parity(s, d["final_state"], in_dtype, "final_state (reference-normalised q/k)")
+    # ... and end to end with the in-kernel l2norm
     o, s = fn(d["q"], d["k"], d["v"], d["g"], d["beta"], d.get("initial_state"), in_dtype,
               l2=bool(d["l2norm"]), ofs=bool(d["output_final_state"]))
-    ref_o = O.from_bf16_bits(d["out"]) if in_dtype == "bf16" else d["out"]
     assert_parity(o, ref_o, in_dtype, "out")
     if "final_state" in d:
-        # the final state is fp32 in every case; bf16 inputs bound it by the bf16 class
-        assert_parity(s, d["final_state"], in_dtype, "final_state")
+        if "q_l2" in d:
+            # A one-ulp difference in the inverse norm of one recent key (the rsqrt
+            # estimate above) moves the final state by up to ~0.5% rel-L2 when q/k
+            # are far from unit norm; the oracle sees the same gap.
+            assert rel_l2(s, d["final_state"]) < 1e-2
+        else:
+            assert_parity(s, d["final_state"], in_dtype, "final_state")
     else:
         assert s is None
 
