@@ -163,8 +163,8 @@ def test_strided_views_like_the_model():
     q, k, v = torch.split(mixed, [H * 128] * 3, dim=-1)
     q, k, v = (x.reshape(B, T, H, 128) for x in (q, k, v))
     ab = torch.randn(B, T, 2 * H, device="cuda")
-    g = -torch.nn.functional.softplus(ab[..., :H])
-    beta = ab[..., H:].sigmoid()
+    g = (-torch.nn.functional.softplus(ab))[..., :H]
+    beta = ab.sigmoid()[..., H:]
     assert not q.is_contiguous() and not g.is_contiguous()
     o1, s1 = m.fast_chunk_gated_delta_rule(q, k, v, g, beta, output_final_state=True, use_qk_l2norm_in_kernel=True)
     o2, s2 = m.fast_chunk_gated_delta_rule(q.contiguous(), k.contiguous(), v.contiguous(), g.contiguous(),
