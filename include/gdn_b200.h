@@ -78,6 +78,32 @@ GDN_API int gdn_chunk_gated_delta_rule(const gdn_tensor* query, const gdn_tensor
 /* Workspace bytes gdn_chunk_gated_delta_rule needs for this problem. */
 GDN_API size_t gdn_chunk_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int qkv_dtype);
 
+/* Chunked forward for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference (its Python op allocates freely).  Same
+ * arguments and results as gdn_chunk_gated_delta_rule, minus the workspace:
+ * for callers that cannot call cudaMalloc when they run the op -- runtimes that
+ * plan every device buffer ahead of time, plugins whose host framework owns all
+ * allocations, code running while other components hold the free memory.
+ * Scratch comes from a fixed array of GDN_NOALLOC_SCRATCH_BYTES (64 MiB)
+ * compiled into the library, which every GPU that loads it holds until exit.
+ *   - Problems whose workspace (gdn_chunk_workspace_bytes) exceeds that return
+ *     GDN_ERR_WORKSPACE without launching anything.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current) and caches it; make that
+ *     first call before any stream capture.
+ *   - All calls share the array and it keeps the last call's contents; nothing
+ *     in it needs to start at zero.  Calls that overlap on the GPU (other
+ *     streams or host threads) race on it: order them on one stream.
+ *   - Calls no cudaMalloc, cudaFree or other allocating routine. */
+#define GDN_NOALLOC_SCRATCH_BYTES (64ull << 20)
+GDN_API int gdn_chunk_gated_delta_rule_noalloc(const gdn_tensor* query, const gdn_tensor* key,
+                                               const gdn_tensor* value, const gdn_tensor* g,
+                                               const gdn_tensor* beta, int chunk_size,
+                                               const float* initial_state, int output_final_state,
+                                               int use_qk_l2norm_in_kernel, gdn_tensor* out,
+                                               float* final_state, void* stream);
+
 /* Token-by-token recurrent rule (decode step when T == 1).
  *
  * Replaces torch_recurrent_gated_delta_rule(query, key, value, g, beta,

@@ -21,6 +21,7 @@ GDN_ERR_CUDA = 4
 GDN_ERR_DEVICE = 5
 
 GDN_F32, GDN_BF16, GDN_F16 = 0, 1, 2
+GDN_NOALLOC_SCRATCH_BYTES = 64 << 20  # include/gdn_b200.h
 
 # Every symbol include/gdn_b200.h declares, with its ctypes signature.
 c_void_p, c_int, c_int64, c_size_t, c_char_p = (ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
@@ -43,6 +44,8 @@ SIGNATURES = {
     "gdn_chunk_gated_delta_rule": (c_int, [_P, _P, _P, _P, _P, c_int, c_void_p, c_int, c_int, _P, c_void_p,
                                            c_void_p, c_size_t, c_void_p]),
     "gdn_chunk_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int64, c_int]),
+    "gdn_chunk_gated_delta_rule_noalloc": (c_int, [_P, _P, _P, _P, _P, c_int, c_void_p, c_int, c_int, _P,
+                                                   c_void_p, c_void_p]),
     "gdn_recurrent_gated_delta_rule": (c_int, [_P, _P, _P, _P, _P, c_void_p, c_int, c_int, _P, c_void_p, c_void_p]),
     "gdn_launch_count": (ctypes.c_uint64, []),
     "gdn_set_phase_events": (None, [ctypes.POINTER(c_void_p), c_int]),

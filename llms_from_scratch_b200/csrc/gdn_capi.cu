@@ -137,6 +137,16 @@ namespace gdn {
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+int set_last_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
 cudaError_t phase_event(int index, cudaStream_t stream) {
     if (!g_phase_events || index >= g_phase_event_count || !g_phase_events[index]) return cudaSuccess;
     return cudaEventRecord(reinterpret_cast<cudaEvent_t>(g_phase_events[index]), stream);

@@ -44,6 +44,9 @@ struct RecurrentParams {
     int l2norm;
 };
 
+// Records `fmt` as the message gdn_last_error() returns on this host thread; returns `code`.
+int set_last_error(int code, const char* fmt, ...);
+
 // Launch bookkeeping shared by all launchers: counts kernels and records the
 // phase events requested through gdn_set_phase_events on this host thread.
 void note_launch();
