@@ -130,6 +130,12 @@ GDN_API int gdn_recurrent_gated_delta_rule(const gdn_tensor* query, const gdn_te
 GDN_API uint64_t gdn_launch_count(void);
 GDN_API void gdn_set_phase_events(void* const* events, int n);
 
+/* Sticky error bits of the current device.  A kernel whose bounded wait on an
+ * internal barrier gives up (a bug, never expected) sets a bit here and exits
+ * cleanly instead of hanging: 1 = chunk prep, 2 = chunk scan.  Synchronous;
+ * `clear` != 0 resets the word. */
+GDN_API unsigned int gdn_device_error(int clear);
+
 /* Message for the most recent failure on this host thread ("" if none). */
 GDN_API const char* gdn_last_error(void);
 

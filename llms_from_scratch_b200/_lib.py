@@ -49,6 +49,7 @@ SIGNATURES = {
     "gdn_recurrent_gated_delta_rule": (c_int, [_P, _P, _P, _P, _P, c_void_p, c_int, c_int, _P, c_void_p, c_void_p]),
     "gdn_launch_count": (ctypes.c_uint64, []),
     "gdn_set_phase_events": (None, [ctypes.POINTER(c_void_p), c_int]),
+    "gdn_device_error": (ctypes.c_uint, [c_int]),
     "gdn_last_error": (c_char_p, []),
     "gdn_status_name": (c_char_p, [c_int]),
     "gdn_abi_version": (c_int, []),

@@ -16,6 +16,37 @@
 namespace {
 
 thread_local std::string g_last_error;
+
+// Sticky device error word: bounded waits inside the kernels that give up OR a
+// bit in here (gdn_internal.h) instead of hanging or trapping.
+__device__ unsigned int g_device_error;
+void* g_device_error_addr[64];
+
+unsigned int* device_error_word(int dev) {
+    if (dev < 0 || dev >= 64) return nullptr;
+    if (!g_device_error_addr[dev]) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
+        g_device_error_addr[dev] = ptr;
+    }
+    return reinterpret_cast<unsigned int*>(g_device_error_addr[dev]);
+}
+
+// The tensor-core chunk path takes bf16 q/k/v/out whose rows are 8-byte (inputs)
+// and 16-byte (output) aligned; everything else runs on the CUDA-core path.
+bool tc_eligible(const gdn_tensor* q, const gdn_tensor* k, const gdn_tensor* v, const gdn_tensor* out) {
+    const gdn_tensor* in[3] = {q, k, v};
+    for (const gdn_tensor* t : in) {
+        if (t->dtype != GDN_BF16) return false;
+        if ((reinterpret_cast<uintptr_t>(t->data) & 7) || (t->stride[0] & 3) || (t->stride[1] & 3) || (t->stride[2] & 3))
+            return false;
+    }
+    if (out->dtype != GDN_BF16) return false;
+    if ((reinterpret_cast<uintptr_t>(out->data) & 15) || (out->stride[0] & 7) || (out->stride[1] & 7) ||
+        (out->stride[2] & 7))
+        return false;
+    return true;
+}
 thread_local void* const* g_phase_events = nullptr;
 thread_local int g_phase_event_count = 0;
 std::atomic<uint64_t> g_launches{0};
@@ -169,7 +200,10 @@ size_t gdn_chunk_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Dk, in
     (void)qkv_dtype;
     if (B <= 0 || T <= 0 || H <= 0) return 0;
     const int64_t NC = (T + gdn::kChunk - 1) / gdn::kChunk;
-    return (size_t)(B * H * NC) * (size_t)gdn::kWsChunkFloats * sizeof(float);
+    const size_t per_chunk = (size_t)gdn::kWsChunkFloats * sizeof(float) > (size_t)gdn::kTcChunkBytes
+                                 ? (size_t)gdn::kWsChunkFloats * sizeof(float)
+                                 : (size_t)gdn::kTcChunkBytes;
+    return (size_t)(B * H * NC) * per_chunk;
 }
 
 int gdn_chunk_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
@@ -189,6 +223,8 @@ int gdn_chunk_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* key, c
     if (B * H == 0) return GDN_OK;
     if (T == 0) return empty_sequence(B, H, initial_state, hT, st);
 
+    int dev = 0;
+    cudaGetDevice(&dev);
     const size_t need = gdn_chunk_workspace_bytes(B, T, H, gdn::kDk, gdn::kDv, query->dtype);
     if (!workspace || workspace_bytes < need)
         return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace ? workspace_bytes : 0);
@@ -213,7 +249,8 @@ int gdn_chunk_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* key, c
     p.T = T;
     p.NC = (int)((T + gdn::kChunk - 1) / gdn::kChunk);
     p.l2norm = use_qk_l2norm_in_kernel ? 1 : 0;
-    cudaError_t e = gdn::launch_chunk_simt(p, st);
+    p.err = device_error_word(dev);
+    cudaError_t e = tc_eligible(query, key, value, out) ? gdn::launch_chunk_tc(p, st) : gdn::launch_chunk_simt(p, st);
     return e == cudaSuccess ? GDN_OK : cuda_fail(e, "chunk kernels launch");
 }
 
@@ -250,6 +287,20 @@ int gdn_recurrent_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* ke
     p.l2norm = use_qk_l2norm_in_kernel ? 1 : 0;
     cudaError_t e = gdn::launch_recurrent(p, st);
     return e == cudaSuccess ? GDN_OK : cuda_fail(e, "recurrent kernel launch");
+}
+
+unsigned int gdn_device_error(int clear) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    unsigned int* w = device_error_word(dev);
+    if (!w) return 0;
+    unsigned int v = 0;
+    if (cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
+    if (clear && v) {
+        const unsigned int zero = 0;
+        cudaMemcpy(w, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    }
+    return v;
 }
 
 const char* gdn_last_error(void) { return g_last_error.c_str(); }

@@ -1,0 +1,660 @@
+// Chunked gated delta rule on the sm_100a tensor cores (tcgen05 + TMEM).
+//
+// The reference's chunk loop (qwen3_5_transformers.py:170-180) is rewritten as
+// an affine recurrence on the chunk-start state S_c (Dk x Dv, fp32):
+//
+//   S_{c+1} = M_c S_c + b_c          M_c = e^{gc_last} I - kd^T w,   b_c = kd^T u
+//   o_c     = Q'_c S_c + o0_c        Q'_c = q e^{gc} Dk^-1/2 - Aqk w,  o0_c = Aqk u
+//
+// with u = T beta v, w = T beta e^{gc} k (T the unit-lower-triangular WY inverse,
+// :154-160), kd = k e^{gc_last - gc} (:179) and Aqk the causal decayed q k^T
+// (:172).  Everything that does not depend on S is computed for all chunks in
+// parallel (gdn_prep_tc); the sequential part shrinks to one 128x128x128 and
+// one 64x128x128 product per chunk (gdn_scan_tc).
+//
+// Precision.  Only q^, k^ (the l2-normalised inputs, bf16 exactly as the
+// reference rounds them) and v are exact bf16 MMA operands.  Every other
+// operand of the prep is a derived fp32 quantity and enters its MMA as a
+// hi + lo pair of bf16 (two MMAs), so the prep is fp32-accurate.  The scan
+// feeds M_c, Q'_c and S_c to the MMA in bf16 and keeps S, b and o0 in fp32.
+//
+// gdn_prep_tc: one CTA (8 warps) per (batch, head, 64-token chunk).
+//   1. rows of q, k, v -> l2norm (16-bit rounding as the reference) -> bf16
+//      128B-swizzled tiles Qh, Kh, V in shared memory
+//   2. G_k = Kh Kh^T, G_q = Qh Kh^T on the tensor cores (M=64, N=64, K=128)
+//   3. L = -(beta G_k e^(gc_i-gc_j)) strictly lower, Aqk = Dk^-1/2 G_q e^(gc_i-gc_j) causal
+//   4. T = (I - L)^-1 by forward substitution (64 threads, one column each)
+//   5. X = E_d T B_e, Y = E_d T B, W = Aqk T B, Z = Aqk T B_e  (64x64, fp32)
+//   6. P_X = X k^, P_Y = Y v, Zk = Z k^, o0 = W v (M=64, N=128, K=64, hi+lo)
+//   7. Q' = q^ e^gc Dk^-1/2 - Zk, o0 -> workspace; P_X, P_Y -> hi+lo B tiles
+//   8. M' = k^T P_X, b = k^T P_Y (M=128, N=128, K=64, hi+lo)
+//   9. M = e^gc_last I - M', b -> workspace
+// gdn_scan_tc: one CTA per (batch, head, 32-column slice of Dv); warp 4
+//   bulk-copies each chunk's workspace record (double-buffered), warp 5 issues
+//   the two MMAs, warps 0-3 turn the accumulators into the next state and the
+//   output rows.
+#include <cuda_bf16.h>
+
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+#include "gdn_tc.cuh"
+
+namespace gdn {
+namespace {
+
+using namespace tc;
+
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s; a healthy wait here takes microseconds
+
+__device__ __forceinline__ void report(unsigned int* err, unsigned int bit) {
+    if (err) atomicOr(err, bit);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// bf16 hi/lo split: x ~= hi + lo with |x - hi - lo| <= 2^-16 |x|.
+__device__ __forceinline__ void split_bf16(float x, float& hi, float& lo) {
+    hi = __bfloat162float(__float2bfloat16_rn(x));
+    lo = x - hi;
+}
+
+// ============================================================================ prep
+
+constexpr int kPrepThreads = 256;
+constexpr uint32_t P_KH = 0;           // k^ bf16 [64 tok][128], swizzled, 16 KiB
+constexpr uint32_t P_QH = 16384;       // q^
+constexpr uint32_t P_V = 32768;        // v
+constexpr uint32_t P_L = 49152;        // fp32 [64][64]
+constexpr uint32_t P_AQK = 65536;      // fp32 [64][68]
+constexpr int kAqkLd = 68;
+constexpr uint32_t P_T = 82944;        // fp32 [64][64]
+constexpr uint32_t P_SPLIT = 99328;    // X,Y,W,Z hi/lo (8 x 8 KiB), later PX/PY hi/lo (4 x 16 KiB)
+constexpr uint32_t P_MISC = 164864;
+constexpr uint32_t P_SMEM = P_MISC + 2048 + 1024;
+
+struct PrepMisc {
+    float gc[64];
+    float beta[64];
+    float egc[64];
+    float ekd[64];
+    uint64_t bar;
+    uint32_t tmem;
+};
+
+__device__ __forceinline__ void load_bf16x4(const View4& v, int b, int64_t t, int h, int lane, float (&x)[4]) {
+    const __nv_bfloat16* p =
+        reinterpret_cast<const __nv_bfloat16*>(v.p) + (int64_t)b * v.sb + t * v.st + (int64_t)h * v.sh + 4 * lane;
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+    const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+    x[0] = __low2float(lo);
+    x[1] = __high2float(lo);
+    x[2] = __low2float(hi);
+    x[3] = __high2float(hi);
+}
+
+__device__ __forceinline__ void store_bf16x4(unsigned char* tile, int row, int col, const float (&x)[4]) {
+    uint2 u;
+    u.x = pack_bf16x2(x[0], x[1]);
+    u.y = pack_bf16x2(x[2], x[3]);
+    *reinterpret_cast<uint2*>(tile + sw128_offset(row, col, 64)) = u;
+}
+
+// 8 consecutive values -> one 16-byte chunk of a swizzled bf16 tile (global or shared).
+__device__ __forceinline__ void store_bf16x8(unsigned char* tile, uint32_t off, const float* x) {
+    uint4 u;
+    u.x = pack_bf16x2(x[0], x[1]);
+    u.y = pack_bf16x2(x[2], x[3]);
+    u.z = pack_bf16x2(x[4], x[5]);
+    u.w = pack_bf16x2(x[6], x[7]);
+    *reinterpret_cast<uint4*>(tile + off) = u;
+}
+
+// hi/lo halves of 8 consecutive values into two swizzled bf16 tiles.
+__device__ __forceinline__ void store_split8(unsigned char* hi_tile, unsigned char* lo_tile, uint32_t off,
+                                             const float* x) {
+    float h[8], l[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) split_bf16(x[e], h[e], l[e]);
+    store_bf16x8(hi_tile, off, h);
+    store_bf16x8(lo_tile, off, l);
+}
+
+// fp32 row of 32 values in a [rows][32] block whose 16-byte chunks are swizzled by row % 8.
+__device__ __forceinline__ uint32_t f32blk_offset(int row, int chunk4) {
+    return (uint32_t)row * 128u + (uint32_t)((chunk4 ^ (row & 7)) * 16);
+}
+
+__global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    PrepMisc& ms = *reinterpret_cast<PrepMisc*>(sm + P_MISC);
+    float(*sL)[64] = reinterpret_cast<float(*)[64]>(sm + P_L);
+    float(*sA)[kAqkLd] = reinterpret_cast<float(*)[kAqkLd]>(sm + P_AQK);
+    float(*sT)[64] = reinterpret_cast<float(*)[64]>(sm + P_T);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t chunk = blockIdx.x;
+    const int c = (int)(chunk % p.NC);
+    const int bh = (int)(chunk / p.NC);
+    const int b = bh / p.H, h = bh % p.H;
+    const int64_t t0 = (int64_t)c * kChunk;
+    const float scale = rsqrtf((float)kDk);
+    unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
+
+    // ---- 1. normalised rows -> swizzled bf16 tiles (qwen3_5_transformers.py:122-137)
+    for (int r = warp; r < kChunk; r += kPrepThreads / 32) {
+        const int64_t t = t0 + r;
+        float q[4] = {0.f, 0.f, 0.f, 0.f}, k[4] = {0.f, 0.f, 0.f, 0.f}, v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (t < p.T) {
+            load_bf16x4(p.q, b, t, h, lane, q);
+            load_bf16x4(p.k, b, t, h, lane, k);
+            load_bf16x4(p.v, b, t, h, lane, v);
+            if (p.l2norm) {
+                const float iq = l2norm_inv(q, GDN_BF16), ik = l2norm_inv(k, GDN_BF16);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    q[e] = round_to(q[e] * iq, GDN_BF16);
+                    k[e] = round_to(k[e] * ik, GDN_BF16);
+                }
+            }
+        }
+        store_bf16x4(sm + P_QH, r, 4 * lane, q);
+        store_bf16x4(sm + P_KH, r, 4 * lane, k);
+        store_bf16x4(sm + P_V, r, 4 * lane, v);
+    }
+    if (tid < kChunk) {
+        const int64_t t = t0 + tid;
+        float gv = 0.f, bv = 0.f;
+        if (t < p.T) {
+            gv = load_elem(p.g.p, (int64_t)b * p.g.sb + t * p.g.st + (int64_t)h * p.g.sh, p.g.dtype);
+            bv = load_elem(p.beta.p, (int64_t)b * p.beta.sb + t * p.beta.st + (int64_t)h * p.beta.sh, p.beta.dtype);
+        }
+        ms.gc[tid] = gv;
+        ms.beta[tid] = bv;
+    }
+    if (warp == 0) {
+        tmem_alloc(&ms.tmem, 512);
+        tmem_relinquish();
+    }
+    if (tid == 32) {
+        mbar_init(&ms.bar, 1);
+        fence_mbar_init();
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = ms.tmem;
+    const uint32_t sbase = smem_u32(sm);
+
+    // ---- 2. G_k = k^ k^T -> TMEM cols [0,64), G_q = q^ k^T -> [64,128); cumsum of g (:151)
+    if (tid == 0) {
+        const uint32_t id = make_idesc_f16(64, 64, false, false, true);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t koff = (ks >> 2) * 64 * 128 + (ks & 3) * 32;
+            const uint64_t bk = make_sdesc(sbase + P_KH + koff, 16, 1024, kSwizzle128B);
+            mma_f16(tm + 0, make_sdesc(sbase + P_KH + koff, 16, 1024, kSwizzle128B), bk, id, ks > 0);
+            mma_f16(tm + 64, make_sdesc(sbase + P_QH + koff, 16, 1024, kSwizzle128B), bk, id, ks > 0);
+        }
+        mma_commit(&ms.bar);
+        float acc = 0.f;
+        for (int i = 0; i < kChunk; ++i) {
+            acc += ms.gc[i];
+            ms.gc[i] = acc;
+        }
+    }
+    __syncthreads();
+    if (tid < kChunk) {
+        ms.egc[tid] = expf(ms.gc[tid]);
+        ms.ekd[tid] = expf(ms.gc[kChunk - 1] - ms.gc[tid]);
+    }
+    bool ok = mbar_wait(&ms.bar, 0, kWaitNs);
+    tc_fence_after();
+
+    const int quad = warp & 3, half = warp >> 2;
+    // ---- 3. L and Aqk from the accumulators (:152-153, :172)
+    if (!__syncthreads_or(!ok)) {
+        float gk[32], gq[32];
+        tmem_ld32(tmem_addr(tm, 32 * quad, 32 * half), gk);
+        tmem_ld32(tmem_addr(tm, 32 * quad, 64 + 32 * half), gq);
+        tmem_ld_wait();
+        if (lane < 16) {
+            const int i = 16 * quad + lane;
+            const float gci = ms.gc[i], bi = ms.beta[i];
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) {
+                const int j = 32 * half + jj;
+                const float dec = (j <= i) ? expf(gci - ms.gc[j]) : 0.f;
+                sL[i][j] = (j < i) ? -(bi * gk[jj]) * dec : 0.f;
+                sA[i][j] = (j <= i) ? (scale * gq[jj]) * dec : 0.f;
+            }
+        }
+    } else {
+        ok = false;
+    }
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- 4. T = (I - L)^-1: thread j solves column j (the loop at :154-158)
+    if (ok && tid < kChunk) {
+        const int j = tid;
+        float x[kChunk];
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) x[i] = (i == j) ? 1.f : 0.f;
+#pragma unroll
+        for (int i = 1; i < kChunk; ++i) {
+            float s = 0.f;
+#pragma unroll
+            for (int m4 = 0; m4 < (i + 3) / 4; ++m4) {
+                const float4 l4 = *reinterpret_cast<const float4*>(&sL[i][4 * m4]);
+                s += l4.x * x[4 * m4] + l4.y * x[4 * m4 + 1] + l4.z * x[4 * m4 + 2] + l4.w * x[4 * m4 + 3];
+            }
+            x[i] = (i == j) ? 1.f : s;
+        }
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) sT[i][j] = x[i];
+    }
+    __syncthreads();
+
+    // ---- 5. the four 64x64 coefficient matrices, hi/lo bf16 A tiles
+    if (ok) {
+        const int i = tid >> 2, j0 = (tid & 3) * 16;
+        float at[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) at[e] = 0.f;
+        for (int m = j0; m <= i; ++m) {  // (Aqk T)[i][j] = sum_{m=j..i} Aqk[i][m] T[m][j]
+            const float a = sA[i][m];
+#pragma unroll
+            for (int e4 = 0; e4 < 4; ++e4) {
+                const float4 t4 = *reinterpret_cast<const float4*>(&sT[m][j0 + 4 * e4]);
+                at[4 * e4] += a * t4.x;
+                at[4 * e4 + 1] += a * t4.y;
+                at[4 * e4 + 2] += a * t4.z;
+                at[4 * e4 + 3] += a * t4.w;
+            }
+        }
+        const float ekdi = ms.ekd[i];
+        float X[16], Y[16], W[16], Z[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const int j = j0 + e;
+            const float bj = ms.beta[j], bej = ms.beta[j] * ms.egc[j];
+            const float tij = sT[i][j];
+            X[e] = ekdi * tij * bej;
+            Y[e] = ekdi * tij * bj;
+            W[e] = at[e] * bj;
+            Z[e] = at[e] * bej;
+        }
+        unsigned char* sp = sm + P_SPLIT;
+#pragma unroll
+        for (int h8 = 0; h8 < 2; ++h8) {
+            const uint32_t off = sw128_offset(i, j0 + 8 * h8, 64);
+            store_split8(sp + 0 * 8192, sp + 1 * 8192, off, X + 8 * h8);
+            store_split8(sp + 2 * 8192, sp + 3 * 8192, off, Y + 8 * h8);
+            store_split8(sp + 4 * 8192, sp + 5 * 8192, off, W + 8 * h8);
+            store_split8(sp + 6 * 8192, sp + 7 * 8192, off, Z + 8 * h8);
+        }
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    // ---- 6. P_X = X k^ [0,128), P_Y = Y v [128,256), Zk = Z k^ [256,384), o0 = W v [384,512)
+    if (ok && tid == 0) {
+        tc_fence_after();
+        const uint32_t id = make_idesc_f16(64, 128, false, true, true);
+        const uint32_t sp = sbase + P_SPLIT;
+        const uint32_t a_tiles[4] = {sp + 0 * 8192, sp + 2 * 8192, sp + 6 * 8192, sp + 4 * 8192};
+        const uint32_t b_tiles[4] = {sbase + P_KH, sbase + P_V, sbase + P_KH, sbase + P_V};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {  // hi, lo
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint64_t ad = make_sdesc(a_tiles[r] + s * 8192 + ks * 32, 16, 1024, kSwizzle128B);
+                    const uint64_t bd = make_sdesc(b_tiles[r] + ks * 2048, 8192, 1024, kSwizzle128B);
+                    mma_f16(tm + 128 * r, ad, bd, id, (s | ks) != 0);
+                }
+            }
+        }
+        mma_commit(&ms.bar);
+    }
+    if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);
+    tc_fence_after();
+
+    // ---- 7. epilogue: P_X/P_Y -> hi/lo B tiles, Q' and o0 -> workspace
+    if (!__syncthreads_or(!ok)) {
+        const int i = 16 * quad + lane;  // valid for lane < 16
+        unsigned char* sp = sm + P_SPLIT;
+        // P_X -> PXh/PXl at +0/+16K, P_Y -> PYh/PYl at +32K/+48K (MN-major B: rows = tokens)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                float v[32];
+                tmem_ld32(tmem_addr(tm, 32 * quad, 128 * r + 64 * half + 32 * cc), v);
+                tmem_ld_wait();
+                if (lane < 16) {
+#pragma unroll
+                    for (int q8 = 0; q8 < 4; ++q8) {
+                        const int d = 64 * half + 32 * cc + 8 * q8;
+                        store_split8(sp + r * 32768, sp + r * 32768 + 16384, sw128_offset(i, d, 64), v + 8 * q8);
+                    }
+                }
+            }
+        }
+        // Q' = q^ Dk^-1/2 e^gc - Zk  (the q e^gc S term of :175 and -Aqk w S of :176 combined)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+            float v[32];
+            tmem_ld32(tmem_addr(tm, 32 * quad, 256 + 64 * half + 32 * cc), v);
+            tmem_ld_wait();
+            if (lane < 16) {
+                const float qs = scale * ms.egc[i];
+#pragma unroll
+                for (int q8 = 0; q8 < 4; ++q8) {
+                    const int d = 64 * half + 32 * cc + 8 * q8;
+                    const uint32_t off = sw128_offset(i, d, 64);
+                    const uint4 qu = *reinterpret_cast<const uint4*>(sm + P_QH + off);
+                    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(&qu);
+                    float o[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o[e] = qs * __bfloat162float(qb[e]) - v[8 * q8 + e];
+                    store_bf16x8(wrec + kTcQ, off, o);
+                }
+            }
+        }
+        // o0 = Aqk u, fp32 column tiles of 32
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+            float v[32];
+            tmem_ld32(tmem_addr(tm, 32 * quad, 384 + 64 * half + 32 * cc), v);
+            tmem_ld_wait();
+            if (lane < 16) {
+                unsigned char* blk = wrec + kTcO0 + (2 * half + cc) * (64 * 128);
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4)
+                    *reinterpret_cast<float4*>(blk + f32blk_offset(i, q4)) =
+                        make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+            }
+        }
+    } else {
+        ok = false;
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    // ---- 8. M' = k^T P_X -> [0,128), b = k^T P_Y -> [128,256)  (M=128 over Dk)
+    if (ok && tid == 0) {
+        const uint32_t id = make_idesc_f16(128, 128, true, true, true);
+        const uint32_t sp = sbase + P_SPLIT;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint64_t ad = make_sdesc(sbase + P_KH + ks * 2048, 8192, 1024, kSwizzle128B);
+                    const uint64_t bd = make_sdesc(sp + r * 32768 + s * 16384 + ks * 2048, 8192, 1024, kSwizzle128B);
+                    mma_f16(tm + 128 * r, ad, bd, id, (s | ks) != 0);
+                }
+            }
+        }
+        mma_commit(&ms.bar);
+    }
+    if (ok) ok = mbar_wait(&ms.bar, 0, kWaitNs);
+    tc_fence_after();
+
+    // ---- 9. M = e^gc_last I - M' (bf16 image), b (fp32 column tiles)
+    if (!__syncthreads_or(!ok)) {
+        const int dk = 32 * quad + lane;
+        const float gamma = ms.egc[kChunk - 1];
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+            float v[32];
+            tmem_ld32(tmem_addr(tm, 32 * quad, 64 * half + 32 * cc), v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q8 = 0; q8 < 4; ++q8) {
+                const int col = 64 * half + 32 * cc + 8 * q8;
+                float m[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) m[e] = ((col + e) == dk ? gamma : 0.f) - v[8 * q8 + e];
+                store_bf16x8(wrec + kTcM, sw128_offset(dk, col, 128), m);
+            }
+        }
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+            float v[32];
+            tmem_ld32(tmem_addr(tm, 32 * quad, 128 + 64 * half + 32 * cc), v);
+            tmem_ld_wait();
+            unsigned char* blk = wrec + kTcB + (2 * half + cc) * (128 * 128);
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4)
+                *reinterpret_cast<float4*>(blk + f32blk_offset(dk, q4)) =
+                    make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+        }
+    } else {
+        ok = false;
+    }
+    if (!ok && tid == 0) report(p.err, kErrTimeoutPrep);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tm, 512);
+}
+
+// ============================================================================ scan
+
+constexpr int kScanThreads = 192;          // warps 0-3: epilogue, 4: bulk copies, 5: MMA
+constexpr uint32_t S_STAGE = 73728;        // M image 32K | Q image 16K | b slice 16K | o0 slice 8K
+constexpr uint32_t S_OFF_Q = 32768, S_OFF_B = 49152, S_OFF_O0 = 65536;
+constexpr uint32_t S_STILE = 2 * S_STAGE;  // state operand: bf16 [128 dk][64] swizzled (32 columns used)
+constexpr uint32_t S_MISC = S_STILE + 16384;
+constexpr uint32_t S_SMEM = S_MISC + 256 + 1024;
+
+struct ScanMisc {
+    uint64_t full[2];
+    uint64_t empty[2];
+    uint64_t mma_done;
+    uint64_t s_ready;
+    uint32_t tmem;
+    int abort;
+};
+
+__global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    ScanMisc& ms = *reinterpret_cast<ScanMisc*>(sm + S_MISC);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int bh = blockIdx.x;
+    const int b = bh / p.H, h = bh % p.H;
+    const int dvt = blockIdx.y;
+    const int dv0 = dvt * kTcDvTile;
+    const unsigned char* wbase = reinterpret_cast<const unsigned char*>(p.ws) + (int64_t)bh * p.NC * kTcChunkBytes;
+
+    if (tid == 0) {
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&ms.full[s], 1);
+            mbar_init(&ms.empty[s], 128);
+        }
+        mbar_init(&ms.mma_done, 1);
+        mbar_init(&ms.s_ready, 128);
+        ms.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&ms.tmem, 64);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = ms.tmem;
+    const uint32_t sbase = smem_u32(sm);
+    bool ok = true;
+
+    if (warp == 4) {
+        // ---------------- producer: one chunk record per stage
+        if (lane == 0) {
+            int issued = 0;
+            for (int c = 0; c < p.NC; ++c) {
+                const int s = c & 1;
+                if (c >= 2 && !mbar_wait(&ms.empty[s], ((c >> 1) - 1) & 1, kWaitNs)) {
+                    ok = false;
+                    break;
+                }
+                if (ms.abort) break;
+                const unsigned char* rec = wbase + (int64_t)c * kTcChunkBytes;
+                unsigned char* st = sm + s * S_STAGE;
+                mbar_arrive_expect_tx(&ms.full[s], S_STAGE);
+                bulk_g2s(st, rec + kTcM, 32768, &ms.full[s]);
+                bulk_g2s(st + S_OFF_Q, rec + kTcQ, 16384, &ms.full[s]);
+                bulk_g2s(st + S_OFF_B, rec + kTcB + dvt * 16384, 16384, &ms.full[s]);
+                bulk_g2s(st + S_OFF_O0, rec + kTcO0 + dvt * 8192, 8192, &ms.full[s]);
+                ++issued;
+            }
+            // leave no copy in flight: wait for the last record of each stage to land
+            for (int c = (issued > 2 ? issued - 2 : 0); c < issued; ++c)
+                if (!mbar_wait(&ms.full[c & 1], (c >> 1) & 1, kWaitNs)) ok = false;
+        }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idS = make_idesc_f16(128, kTcDvTile, false, true, true);
+            const uint32_t idO = make_idesc_f16(64, kTcDvTile, false, true, true);
+            for (int c = 0; c < p.NC; ++c) {
+                const int s = c & 1;
+                if (!mbar_wait(&ms.full[s], (c >> 1) & 1, kWaitNs) || !mbar_wait(&ms.s_ready, c & 1, kWaitNs)) {
+                    ok = false;
+                    break;
+                }
+                if (ms.abort) break;
+                tc_fence_after();
+                const uint32_t st = sbase + s * S_STAGE;
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint64_t bd = make_sdesc(sbase + S_STILE + ks * 2048, 16384, 1024, kSwizzle128B);
+                    const uint64_t am = make_sdesc(st + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSwizzle128B);
+                    const uint64_t aq =
+                        make_sdesc(st + S_OFF_Q + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024, kSwizzle128B);
+                    mma_f16(tm + 0, am, bd, idS, ks > 0);
+                    mma_f16(tm + kTcDvTile, aq, bd, idO, ks > 0);
+                }
+                mma_commit(&ms.mma_done);
+            }
+        }
+    } else {
+        // ---------------- epilogue: thread = state row dk (TMEM lane), warp w also owns output rows 16w..16w+15
+        const int dk = tid;
+        float S[kTcDvTile];
+        const int64_t srow = ((int64_t)bh * kDk + dk) * kDv + dv0;
+#pragma unroll
+        for (int q4 = 0; q4 < kTcDvTile / 4; ++q4) {
+            const float4 v = p.h0 ? *reinterpret_cast<const float4*>(p.h0 + srow + 4 * q4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            S[4 * q4] = v.x;
+            S[4 * q4 + 1] = v.y;
+            S[4 * q4 + 2] = v.z;
+            S[4 * q4 + 3] = v.w;
+        }
+        unsigned char* stile = sm + S_STILE;
+#pragma unroll
+        for (int q8 = 0; q8 < kTcDvTile / 8; ++q8) store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
+        fence_proxy_async_smem();
+        mbar_arrive(&ms.s_ready);
+
+        for (int c = 0; c < p.NC; ++c) {
+            const int s = c & 1;
+            if (!mbar_wait(&ms.mma_done, c & 1, kWaitNs)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float d[32], o[32];
+            tmem_ld32(tmem_addr(tm, 32 * warp, 0), d);
+            tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile), o);
+            tmem_ld_wait();
+            const unsigned char* st = sm + s * S_STAGE;
+            // S_{c+1} = M_c S_c + b_c
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4) {
+                const float4 bb = *reinterpret_cast<const float4*>(st + S_OFF_B + f32blk_offset(dk, q4));
+                S[4 * q4] = d[4 * q4] + bb.x;
+                S[4 * q4 + 1] = d[4 * q4 + 1] + bb.y;
+                S[4 * q4 + 2] = d[4 * q4 + 2] + bb.z;
+                S[4 * q4 + 3] = d[4 * q4 + 3] + bb.w;
+            }
+            // o_c = Q'_c S_c + o0_c for tokens 16w + lane (M=64 accumulator rows)
+            if (lane < 16) {
+                const int tok = 16 * warp + lane;
+                const int64_t t = (int64_t)c * kChunk + tok;
+                if (t < p.T) {
+                    float ov[32];
+#pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        const float4 oo = *reinterpret_cast<const float4*>(st + S_OFF_O0 + f32blk_offset(tok, q4));
+                        ov[4 * q4] = o[4 * q4] + oo.x;
+                        ov[4 * q4 + 1] = o[4 * q4 + 1] + oo.y;
+                        ov[4 * q4 + 2] = o[4 * q4 + 2] + oo.z;
+                        ov[4 * q4 + 3] = o[4 * q4 + 3] + oo.w;
+                    }
+                    unsigned char* dst = reinterpret_cast<unsigned char*>(p.out) +
+                                         2 * ((int64_t)b * p.out_sb + t * p.out_st + (int64_t)h * p.out_sh + dv0);
+#pragma unroll
+                    for (int q8 = 0; q8 < 4; ++q8) store_bf16x8(dst, 16 * q8, ov + 8 * q8);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&ms.empty[s]);
+            if (c + 1 < p.NC) {
+#pragma unroll
+                for (int q8 = 0; q8 < kTcDvTile / 8; ++q8)
+                    store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
+                fence_proxy_async_smem();
+                mbar_arrive(&ms.s_ready);
+            }
+        }
+        if (ok && p.hT) {
+#pragma unroll
+            for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
+                *reinterpret_cast<float4*>(p.hT + srow + 4 * q4) =
+                    make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
+        }
+    }
+    if (!ok) {
+        ms.abort = 1;
+        report(p.err, kErrTimeoutScan);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tm, 64);
+}
+
+}  // namespace
+
+cudaError_t launch_chunk_tc(const ChunkParams& p, cudaStream_t stream) {
+    static_assert(P_SMEM <= 227 * 1024 && S_SMEM <= 227 * 1024, "shared memory budget");
+    cudaError_t e = cudaFuncSetAttribute(gdn_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(gdn_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
+    if (e != cudaSuccess) return e;
+    const int64_t nchunks = (int64_t)p.B * p.H * p.NC;
+    if ((e = phase_event(0, stream)) != cudaSuccess) return e;
+    gdn_prep_tc<<<(unsigned)nchunks, kPrepThreads, P_SMEM, stream>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    note_launch();
+    if ((e = phase_event(1, stream)) != cudaSuccess) return e;
+    dim3 grid((unsigned)(p.B * p.H), kDv / kTcDvTile);
+    gdn_scan_tc<<<grid, kScanThreads, S_SMEM, stream>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    note_launch();
+    return phase_event(2, stream);
+}
+
+}  // namespace gdn

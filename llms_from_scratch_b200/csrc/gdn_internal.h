@@ -17,6 +17,16 @@ constexpr int64_t kWsAqk = kWsKd + kChunk * kDk;     // (q k^T * decay) causal [
 constexpr int64_t kWsGamma = kWsAqk + kChunk * kChunk;  // e^gc_last
 constexpr int64_t kWsChunkFloats = kWsGamma + 64;       // keeps every chunk 256-byte aligned
 
+// Workspace record of one (batch, head, chunk) for the tensor-core path.  The
+// scan kernel bulk-copies these straight into shared memory, so the bf16 images
+// are stored already in the swizzled UMMA operand layout.
+constexpr int64_t kTcM = 0;             // M_c = e^gc_last I - kd^T w, bf16 K-major image [128][128]   32 KiB
+constexpr int64_t kTcQ = 32768;         // Q'_c = q e^gc Dk^-1/2 - Aqk w, bf16 K-major image [64][128] 16 KiB
+constexpr int64_t kTcB = 49152;         // b_c = kd^T u, fp32 [4 column tiles][128][32], rows swizzled   64 KiB
+constexpr int64_t kTcO0 = 114688;       // o0_c = Aqk u, fp32 [4 column tiles][64][32], rows swizzled    32 KiB
+constexpr int64_t kTcChunkBytes = 147456;
+constexpr int kTcDvTile = 32;           // state columns per scan CTA
+
 struct ChunkParams {
     View4 q, k, v;
     View3 g, beta;
@@ -29,6 +39,7 @@ struct ChunkParams {
     int B, H, NC;
     int64_t T;
     int l2norm;
+    unsigned int* err;  // device error word (bounded waits that gave up set bits here)
 };
 
 struct RecurrentParams {
@@ -52,7 +63,11 @@ int set_last_error(int code, const char* fmt, ...);
 void note_launch();
 cudaError_t phase_event(int index, cudaStream_t stream);
 
+// Error bits a kernel ORs into the device error word.
+enum : unsigned int { kErrTimeoutPrep = 1u, kErrTimeoutScan = 2u };
+
 cudaError_t launch_chunk_simt(const ChunkParams& p, cudaStream_t stream);
+cudaError_t launch_chunk_tc(const ChunkParams& p, cudaStream_t stream);
 cudaError_t launch_recurrent(const RecurrentParams& p, cudaStream_t stream);
 
 }  // namespace gdn

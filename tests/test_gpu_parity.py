@@ -293,3 +293,48 @@ def test_launch_counter_and_phase_events():
     torch.cuda.synchronize()
     assert lib.gdn_launch_count() - n0 >= 2
     assert evs[0].elapsed_time(evs[1]) > 0 and evs[1].elapsed_time(evs[2]) > 0
+
+
+def test_tensor_core_and_cuda_core_paths_agree():
+    """bf16 inputs with 8-byte-aligned rows take the tcgen05 path; the same values
+    behind a 2-byte offset take the CUDA-core path.  Both match the oracle."""
+    m = ops()
+    q, k, v, g, beta, s0 = O.make_inputs(2, 300, 4, seed=21, in_dtype="bf16", init_state_std=0.02,
+                                         normalize_qk=False)
+    ro, rs = O.chunk_gated_delta_rule(q, k, v, g, beta, initial_state=s0, output_final_state=True,
+                                      use_qk_l2norm_in_kernel=True, in_dtype="bf16")
+
+    def shifted(x):
+        buf = torch.zeros(x.size + 1, dtype=torch.bfloat16, device="cuda")
+        view = buf[1:].view(x.shape)
+        view.copy_(torch.from_numpy(x).to(torch.bfloat16))
+        assert view.data_ptr() % 8 != 0
+        return view
+
+    outs = {}
+    for name, mk in (("tc", lambda x: dev(x, torch.bfloat16)), ("simt", shifted)):
+        o, s = m.fast_chunk_gated_delta_rule(mk(q), mk(k), mk(v), dev(g), dev(beta), initial_state=dev(s0),
+                                             output_final_state=True, use_qk_l2norm_in_kernel=True)
+        outs[name] = (o.float().cpu().numpy(), s.cpu().numpy())
+        assert_parity(outs[name][0], ro, "bf16", f"{name} out")
+        assert_parity(outs[name][1], rs, "bf16", f"{name} state")
+    assert_parity(outs["tc"][0], outs["simt"][0], "bf16", "tc vs simt out")
+
+
+@pytest.mark.parametrize("gscale", [0.05, 1.0, 4.0])
+def test_decay_range_vs_oracle(gscale):
+    """Weak (g*0.05) to strong (g*4) decay: the inter-chunk state matters most when decay is weak."""
+    q, k, v, g, beta, s0 = O.make_inputs(1, 512, 4, seed=31, in_dtype="bf16", init_state_std=0.02,
+                                         normalize_qk=False)
+    g = (g * gscale).astype(np.float32)
+    o, s = run_chunk(q, k, v, g, beta, s0, "bf16")
+    ro, rs = O.chunk_gated_delta_rule(q, k, v, g, beta, initial_state=s0, output_final_state=True,
+                                      use_qk_l2norm_in_kernel=True, in_dtype="bf16")
+    assert_parity(o, ro, "bf16", "out")
+    assert_parity(s, rs, "bf16", "state")
+
+
+def test_device_error_word_is_clear():
+    from llms_from_scratch_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.load().gdn_device_error(1) == 0
