@@ -388,7 +388,7 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp32", "data": "synthetic",
+            "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"gdn_chunk_fwd B={B} T={T} H={H} Dk=Dv=128 chunk=64 bf16 q/k/v, fp32 g/beta/"
                                    "state, l2norm in kernel, final state out",
                        "global_batch": world * B, "seq_len": T, "heads": H,
