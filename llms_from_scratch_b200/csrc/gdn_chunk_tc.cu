@@ -67,12 +67,13 @@ constexpr int kPrepThreads = 256;
 constexpr uint32_t P_KH = 0;           // k^ bf16 [64 tok][128], swizzled, 16 KiB
 constexpr uint32_t P_QH = 16384;       // q^
 constexpr uint32_t P_V = 32768;        // v
-constexpr uint32_t P_L = 49152;        // fp32 [64][64]
-constexpr uint32_t P_AQK = 65536;      // fp32 [64][68]
-constexpr int kAqkLd = 68;
-constexpr uint32_t P_T = 82944;        // fp32 [64][64]
-constexpr uint32_t P_SPLIT = 99328;    // X,Y,W,Z hi/lo (8 x 8 KiB), later PX/PY hi/lo (4 x 16 KiB)
-constexpr uint32_t P_MISC = 164864;
+constexpr int kLd = 68;                // fp32 row stride of the 64x64 scratch matrices (16-byte rows, few conflicts)
+constexpr int kAqkLd = 65;             // Aqk is only read/written as scalars: odd stride, conflict-free
+constexpr uint32_t P_L = 49152;        // fp32 [64][68]
+constexpr uint32_t P_AQK = 66560;      // fp32 [64][65]
+constexpr uint32_t P_T = 83200;        // fp32 [64][68]
+constexpr uint32_t P_SPLIT = 101376;   // X,Y,W,Z hi/lo (8 x 8 KiB), later PX/PY hi/lo (4 x 16 KiB)
+constexpr uint32_t P_MISC = 166912;
 constexpr uint32_t P_SMEM = P_MISC + 2048 + 1024;
 
 struct PrepMisc {
@@ -132,9 +133,9 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     PrepMisc& ms = *reinterpret_cast<PrepMisc*>(sm + P_MISC);
-    float(*sL)[64] = reinterpret_cast<float(*)[64]>(sm + P_L);
+    float(*sL)[kLd] = reinterpret_cast<float(*)[kLd]>(sm + P_L);
     float(*sA)[kAqkLd] = reinterpret_cast<float(*)[kAqkLd]>(sm + P_AQK);
-    float(*sT)[64] = reinterpret_cast<float(*)[64]>(sm + P_T);
+    float(*sT)[kLd] = reinterpret_cast<float(*)[kLd]>(sm + P_T);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t chunk = blockIdx.x;
@@ -145,26 +146,38 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     const float scale = rsqrtf((float)kDk);
     unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
 
-    // ---- 1. normalised rows -> swizzled bf16 tiles (qwen3_5_transformers.py:122-137)
-    for (int r = warp; r < kChunk; r += kPrepThreads / 32) {
-        const int64_t t = t0 + r;
-        float q[4] = {0.f, 0.f, 0.f, 0.f}, k[4] = {0.f, 0.f, 0.f, 0.f}, v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (t < p.T) {
-            load_bf16x4(p.q, b, t, h, lane, q);
-            load_bf16x4(p.k, b, t, h, lane, k);
-            load_bf16x4(p.v, b, t, h, lane, v);
-            if (p.l2norm) {
-                const float iq = l2norm_inv(q, GDN_BF16), ik = l2norm_inv(k, GDN_BF16);
+    // ---- 1. normalised rows -> swizzled bf16 tiles (qwen3_5_transformers.py:122-137).
+    //      Each warp owns 8 rows; all 24 row loads are issued before the first reduction.
+    {
+        constexpr int kRows = kChunk / (kPrepThreads / 32);
+        float q[kRows][4], k[kRows][4], v[kRows][4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    q[e] = round_to(q[e] * iq, GDN_BF16);
-                    k[e] = round_to(k[e] * ik, GDN_BF16);
-                }
+        for (int rr = 0; rr < kRows; ++rr) {
+            const int64_t t = t0 + warp + 8 * rr;
+            if (t < p.T) {
+                load_bf16x4(p.q, b, t, h, lane, q[rr]);
+                load_bf16x4(p.k, b, t, h, lane, k[rr]);
+                load_bf16x4(p.v, b, t, h, lane, v[rr]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) q[rr][e] = k[rr][e] = v[rr][e] = 0.f;
             }
         }
-        store_bf16x4(sm + P_QH, r, 4 * lane, q);
-        store_bf16x4(sm + P_KH, r, 4 * lane, k);
-        store_bf16x4(sm + P_V, r, 4 * lane, v);
+#pragma unroll
+        for (int rr = 0; rr < kRows; ++rr) {
+            const int r = warp + 8 * rr;
+            if (p.l2norm && t0 + r < p.T) {
+                const float iq = l2norm_inv(q[rr], GDN_BF16), ik = l2norm_inv(k[rr], GDN_BF16);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    q[rr][e] = round_to(q[rr][e] * iq, GDN_BF16);
+                    k[rr][e] = round_to(k[rr][e] * ik, GDN_BF16);
+                }
+            }
+            store_bf16x4(sm + P_QH, r, 4 * lane, q[rr]);
+            store_bf16x4(sm + P_KH, r, 4 * lane, k[rr]);
+            store_bf16x4(sm + P_V, r, 4 * lane, v[rr]);
+        }
     }
     if (tid < kChunk) {
         const int64_t t = t0 + tid;
@@ -202,11 +215,17 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
             mma_f16(tm + 64, make_sdesc(sbase + P_QH + koff, 16, 1024, kSwizzle128B), bk, id, ks > 0);
         }
         mma_commit(&ms.bar);
-        float acc = 0.f;
-        for (int i = 0; i < kChunk; ++i) {
-            acc += ms.gc[i];
-            ms.gc[i] = acc;
+    }
+    if (warp == 1) {  // inclusive scan of g over the chunk (:151), two values per lane
+        const float g0 = ms.gc[2 * lane], g1 = ms.gc[2 * lane + 1];
+        float x = g0 + g1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
         }
+        ms.gc[2 * lane] = x - g1;
+        ms.gc[2 * lane + 1] = x;
     }
     __syncthreads();
     if (tid < kChunk) {
@@ -248,13 +267,16 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         for (int i = 0; i < kChunk; ++i) x[i] = (i == j) ? 1.f : 0.f;
 #pragma unroll
         for (int i = 1; i < kChunk; ++i) {
-            float s = 0.f;
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;  // independent chains: latency, not count, bounds this loop
 #pragma unroll
             for (int m4 = 0; m4 < (i + 3) / 4; ++m4) {
                 const float4 l4 = *reinterpret_cast<const float4*>(&sL[i][4 * m4]);
-                s += l4.x * x[4 * m4] + l4.y * x[4 * m4 + 1] + l4.z * x[4 * m4 + 2] + l4.w * x[4 * m4 + 3];
+                s0 += l4.x * x[4 * m4];
+                s1 += l4.y * x[4 * m4 + 1];
+                s2 += l4.z * x[4 * m4 + 2];
+                s3 += l4.w * x[4 * m4 + 3];
             }
-            x[i] = (i == j) ? 1.f : s;
+            x[i] = (i == j) ? 1.f : (s0 + s1) + (s2 + s3);
         }
 #pragma unroll
         for (int i = 0; i < kChunk; ++i) sT[i][j] = x[i];
@@ -263,7 +285,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
 
     // ---- 5. the four 64x64 coefficient matrices, hi/lo bf16 A tiles
     if (ok) {
-        const int i = tid >> 2, j0 = (tid & 3) * 16;
+        const int i = tid & 63, j0 = (tid >> 6) * 16;
         float at[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) at[e] = 0.f;
@@ -279,12 +301,20 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
             }
         }
         const float ekdi = ms.ekd[i];
-        float X[16], Y[16], W[16], Z[16];
+        float X[16], Y[16], W[16], Z[16], ti[16];
+#pragma unroll
+        for (int e4 = 0; e4 < 4; ++e4) {
+            const float4 t4 = *reinterpret_cast<const float4*>(&sT[i][j0 + 4 * e4]);
+            ti[4 * e4] = t4.x;
+            ti[4 * e4 + 1] = t4.y;
+            ti[4 * e4 + 2] = t4.z;
+            ti[4 * e4 + 3] = t4.w;
+        }
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
             const int j = j0 + e;
             const float bj = ms.beta[j], bej = ms.beta[j] * ms.egc[j];
-            const float tij = sT[i][j];
+            const float tij = ti[e];
             X[e] = ekdi * tij * bej;
             Y[e] = ekdi * tij * bj;
             W[e] = at[e] * bj;
@@ -590,6 +620,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                 S[4 * q4 + 2] = d[4 * q4 + 2] + bb.z;
                 S[4 * q4 + 3] = d[4 * q4 + 3] + bb.w;
             }
+            // hand S_{c+1} to the MMA warp first: it is the only thing on the sequential path
+            tc_fence_before();
+            if (c + 1 < p.NC) {
+#pragma unroll
+                for (int q8 = 0; q8 < kTcDvTile / 8; ++q8)
+                    store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
+                fence_proxy_async_smem();
+                mbar_arrive(&ms.s_ready);
+            }
             // o_c = Q'_c S_c + o0_c for tokens 16w + lane (M=64 accumulator rows)
             if (lane < 16) {
                 const int tok = 16 * warp + lane;
@@ -610,15 +649,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                     for (int q8 = 0; q8 < 4; ++q8) store_bf16x8(dst, 16 * q8, ov + 8 * q8);
                 }
             }
-            tc_fence_before();
             mbar_arrive(&ms.empty[s]);
-            if (c + 1 < p.NC) {
-#pragma unroll
-                for (int q8 = 0; q8 < kTcDvTile / 8; ++q8)
-                    store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
-                fence_proxy_async_smem();
-                mbar_arrive(&ms.s_ready);
-            }
         }
         if (ok && p.hT) {
 #pragma unroll
