@@ -18,14 +18,17 @@
 // hi + lo pair of bf16 (two MMAs), so the prep is fp32-accurate.  The scan
 // feeds M_c, Q'_c and S_c to the MMA in bf16 and keeps S, b and o0 in fp32.
 //
-// gdn_prep_tc: one CTA (8 warps) per (batch, head, 64-token chunk).
+// gdn_prep_tc: one CTA (16 warps) per (batch, head, 64-token chunk).  Operands
+// that share a B matrix are stacked into M=128 MMAs so every accumulator fills
+// all 128 TMEM lanes.
 //   1. rows of q, k, v -> l2norm (16-bit rounding as the reference) -> bf16
-//      128B-swizzled tiles Qh, Kh, V in shared memory
-//   2. G_k = Kh Kh^T, G_q = Qh Kh^T on the tensor cores (M=64, N=64, K=128)
+//      128B-swizzled tiles [k^; q^] and v in shared memory
+//   2. [k^; q^] k^T on the tensor cores -> G_k (lanes 0-63) and G_q (64-127)
 //   3. L = -(beta G_k e^(gc_i-gc_j)) strictly lower, Aqk = Dk^-1/2 G_q e^(gc_i-gc_j) causal
-//   4. T = (I - L)^-1 by forward substitution (64 threads, one column each)
+//   4. T = (I - L)^-1 in 16x16 blocks (diagonal blocks by substitution, then
+//      the off-diagonal blocks by distance)
 //   5. X = E_d T B_e, Y = E_d T B, W = Aqk T B, Z = Aqk T B_e  (64x64, fp32)
-//   6. P_X = X k^, P_Y = Y v, Zk = Z k^, o0 = W v (M=64, N=128, K=64, hi+lo)
+//   6. [X; Z] k^ -> P_X | Zk and [Y; W] v -> P_Y | o0  (M=128, N=128, K=64, hi+lo)
 //   7. Q' = q^ e^gc Dk^-1/2 - Zk, o0 -> workspace; P_X, P_Y -> hi+lo B tiles
 //   8. M' = k^T P_X, b = k^T P_Y (M=128, N=128, K=64, hi+lo)
 //   9. M = e^gc_last I - M', b -> workspace
@@ -63,18 +66,19 @@ __device__ __forceinline__ void split_bf16(float x, float& hi, float& lo) {
 
 // ============================================================================ prep
 
-constexpr int kPrepThreads = 256;
-constexpr uint32_t P_KH = 0;           // k^ bf16 [64 tok][128], swizzled, 16 KiB
-constexpr uint32_t P_QH = 16384;       // q^
-constexpr uint32_t P_V = 32768;        // v
-constexpr int kLd = 68;                // fp32 row stride of the 64x64 scratch matrices (16-byte rows, few conflicts)
-constexpr int kAqkLd = 65;             // Aqk is only read/written as scalars: odd stride, conflict-free
+constexpr int kPrepThreads = 512;
+constexpr uint32_t P_KQ = 0;           // bf16 [128 rows][128] swizzled: rows 0-63 k^, 64-127 q^ (atom columns 16 KiB apart)
+constexpr uint32_t P_V = 32768;        // bf16 [64 rows][128] swizzled v (atom columns 8 KiB apart)
+constexpr int kLd = 68;                // fp32 row stride of L and T (16-byte rows)
+constexpr int kAqkLd = 65;             // Aqk is only accessed as scalars: odd stride
 constexpr uint32_t P_L = 49152;        // fp32 [64][68]
 constexpr uint32_t P_AQK = 66560;      // fp32 [64][65]
 constexpr uint32_t P_T = 83200;        // fp32 [64][68]
-constexpr uint32_t P_SPLIT = 101376;   // X,Y,W,Z hi/lo (8 x 8 KiB), later PX/PY hi/lo (4 x 16 KiB)
-constexpr uint32_t P_MISC = 166912;
+constexpr uint32_t P_Y3 = 100608;      // fp32 [3][16][16], scratch of the blocked inverse
+constexpr uint32_t P_SPLIT = 104448;   // [X;Z] and [Y;W] hi/lo A tiles (4 x 16 KiB), later PX/PY hi/lo B tiles
+constexpr uint32_t P_MISC = 169984;
 constexpr uint32_t P_SMEM = P_MISC + 2048 + 1024;
+constexpr uint32_t kPrepTmemCols = 256;
 
 struct PrepMisc {
     float gc[64];
@@ -97,11 +101,11 @@ __device__ __forceinline__ void load_bf16x4(const View4& v, int b, int64_t t, in
     x[3] = __high2float(hi);
 }
 
-__device__ __forceinline__ void store_bf16x4(unsigned char* tile, int row, int col, const float (&x)[4]) {
+__device__ __forceinline__ void store_bf16x4(unsigned char* tile, uint32_t off, const float (&x)[4]) {
     uint2 u;
     u.x = pack_bf16x2(x[0], x[1]);
     u.y = pack_bf16x2(x[2], x[3]);
-    *reinterpret_cast<uint2*>(tile + sw128_offset(row, col, 64)) = u;
+    *reinterpret_cast<uint2*>(tile + off) = u;
 }
 
 // 8 consecutive values -> one 16-byte chunk of a swizzled bf16 tile (global or shared).
@@ -136,8 +140,10 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     float(*sL)[kLd] = reinterpret_cast<float(*)[kLd]>(sm + P_L);
     float(*sA)[kAqkLd] = reinterpret_cast<float(*)[kAqkLd]>(sm + P_AQK);
     float(*sT)[kLd] = reinterpret_cast<float(*)[kLd]>(sm + P_T);
+    float(*sY)[16][16] = reinterpret_cast<float(*)[16][16]>(sm + P_Y3);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int quad = warp & 3, cq = warp >> 2;  // TMEM lane quadrant, column quarter
     const int64_t chunk = blockIdx.x;
     const int c = (int)(chunk % p.NC);
     const int bh = (int)(chunk / p.NC);
@@ -147,13 +153,13 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
 
     // ---- 1. normalised rows -> swizzled bf16 tiles (qwen3_5_transformers.py:122-137).
-    //      Each warp owns 8 rows; all 24 row loads are issued before the first reduction.
+    //      Each warp owns 4 rows; all 12 row loads are issued before the first reduction.
     {
         constexpr int kRows = kChunk / (kPrepThreads / 32);
         float q[kRows][4], k[kRows][4], v[kRows][4];
 #pragma unroll
         for (int rr = 0; rr < kRows; ++rr) {
-            const int64_t t = t0 + warp + 8 * rr;
+            const int64_t t = t0 + warp + 16 * rr;
             if (t < p.T) {
                 load_bf16x4(p.q, b, t, h, lane, q[rr]);
                 load_bf16x4(p.k, b, t, h, lane, k[rr]);
@@ -165,7 +171,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         }
 #pragma unroll
         for (int rr = 0; rr < kRows; ++rr) {
-            const int r = warp + 8 * rr;
+            const int r = warp + 16 * rr;
             if (p.l2norm && t0 + r < p.T) {
                 const float iq = l2norm_inv(q[rr], GDN_BF16), ik = l2norm_inv(k[rr], GDN_BF16);
 #pragma unroll
@@ -174,9 +180,9 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
                     k[rr][e] = round_to(k[rr][e] * ik, GDN_BF16);
                 }
             }
-            store_bf16x4(sm + P_QH, r, 4 * lane, q[rr]);
-            store_bf16x4(sm + P_KH, r, 4 * lane, k[rr]);
-            store_bf16x4(sm + P_V, r, 4 * lane, v[rr]);
+            store_bf16x4(sm + P_KQ, sw128_offset(r, 4 * lane, 128), k[rr]);
+            store_bf16x4(sm + P_KQ, sw128_offset(64 + r, 4 * lane, 128), q[rr]);
+            store_bf16x4(sm + P_V, sw128_offset(r, 4 * lane, 64), v[rr]);
         }
     }
     if (tid < kChunk) {
@@ -190,7 +196,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         ms.beta[tid] = bv;
     }
     if (warp == 0) {
-        tmem_alloc(&ms.tmem, 512);
+        tmem_alloc(&ms.tmem, kPrepTmemCols);
         tmem_relinquish();
     }
     if (tid == 32) {
@@ -204,15 +210,13 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     const uint32_t tm = ms.tmem;
     const uint32_t sbase = smem_u32(sm);
 
-    // ---- 2. G_k = k^ k^T -> TMEM cols [0,64), G_q = q^ k^T -> [64,128); cumsum of g (:151)
+    // ---- 2. [k^; q^] k^T -> TMEM cols [0,64): lanes 0-63 G_k = k^ k^T, lanes 64-127 G_q = q^ k^T
     if (tid == 0) {
-        const uint32_t id = make_idesc_f16(64, 64, false, false, true);
+        const uint32_t id = make_idesc_f16(128, 64, false, false, true);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
-            const uint32_t koff = (ks >> 2) * 64 * 128 + (ks & 3) * 32;
-            const uint64_t bk = make_sdesc(sbase + P_KH + koff, 16, 1024, kSwizzle128B);
-            mma_f16(tm + 0, make_sdesc(sbase + P_KH + koff, 16, 1024, kSwizzle128B), bk, id, ks > 0);
-            mma_f16(tm + 64, make_sdesc(sbase + P_QH + koff, 16, 1024, kSwizzle128B), bk, id, ks > 0);
+            const uint64_t d = make_sdesc(sbase + P_KQ + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSwizzle128B);
+            mma_f16(tm, d, d, id, ks > 0);  // B reads only rows 0-63 (k^) of the same tile
         }
         mma_commit(&ms.bar);
     }
@@ -229,28 +233,31 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     }
     __syncthreads();
     if (tid < kChunk) {
-        ms.egc[tid] = expf(ms.gc[tid]);
-        ms.ekd[tid] = expf(ms.gc[kChunk - 1] - ms.gc[tid]);
+        ms.egc[tid] = __expf(ms.gc[tid]);
+        ms.ekd[tid] = __expf(ms.gc[kChunk - 1] - ms.gc[tid]);
     }
     bool ok = mbar_wait(&ms.bar, 0, kWaitNs);
     tc_fence_after();
 
-    const int quad = warp & 3, half = warp >> 2;
-    // ---- 3. L and Aqk from the accumulators (:152-153, :172)
+    // ---- 3. L = -(beta_i G_k e^(gc_i-gc_j)) strictly lower (:152-153), Aqk = Dk^-1/2 G_q e^(gc_i-gc_j) causal (:172)
     if (!__syncthreads_or(!ok)) {
-        float gk[32], gq[32];
-        tmem_ld32(tmem_addr(tm, 32 * quad, 32 * half), gk);
-        tmem_ld32(tmem_addr(tm, 32 * quad, 64 + 32 * half), gq);
+        float gv[16];
+        tmem_ld16(tmem_addr(tm, 32 * quad, 16 * cq), gv);
         tmem_ld_wait();
-        if (lane < 16) {
-            const int i = 16 * quad + lane;
-            const float gci = ms.gc[i], bi = ms.beta[i];
+        const int r = 32 * quad + lane, i = r & 63;
+        const float gci = ms.gc[i];
+        if (r < 64) {
+            const float bi = ms.beta[i];
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-                const int j = 32 * half + jj;
-                const float dec = (j <= i) ? expf(gci - ms.gc[j]) : 0.f;
-                sL[i][j] = (j < i) ? -(bi * gk[jj]) * dec : 0.f;
-                sA[i][j] = (j <= i) ? (scale * gq[jj]) * dec : 0.f;
+            for (int e = 0; e < 16; ++e) {
+                const int j = 16 * cq + e;
+                sL[i][j] = (j < i) ? -(bi * gv[e]) * __expf(gci - ms.gc[j]) : 0.f;
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const int j = 16 * cq + e;
+                sA[i][j] = (j <= i) ? (scale * gv[e]) * __expf(gci - ms.gc[j]) : 0.f;
             }
         }
     } else {
@@ -259,96 +266,167 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     tc_fence_before();
     __syncthreads();
 
-    // ---- 4. T = (I - L)^-1: thread j solves column j (the loop at :154-158)
-    if (ok && tid < kChunk) {
-        const int j = tid;
-        float x[kChunk];
+    // ---- 4. T = (I - L)^-1 in 16x16 blocks (the forward substitution of :154-158):
+    //      diagonal blocks by substitution, then T_rc = T_rr sum_{k=c}^{r-1} L_rk T_kc by block distance.
+    if (ok) {
+        if (tid < 64) {
+            const int blk = tid >> 4, j = tid & 15, o = 16 * blk;
+            float x[16];
 #pragma unroll
-        for (int i = 0; i < kChunk; ++i) x[i] = (i == j) ? 1.f : 0.f;
+            for (int i = 0; i < 16; ++i) x[i] = (i == j) ? 1.f : 0.f;
 #pragma unroll
-        for (int i = 1; i < kChunk; ++i) {
-            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;  // independent chains: latency, not count, bounds this loop
+            for (int i = 1; i < 16; ++i) {
+                float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-            for (int m4 = 0; m4 < (i + 3) / 4; ++m4) {
-                const float4 l4 = *reinterpret_cast<const float4*>(&sL[i][4 * m4]);
-                s0 += l4.x * x[4 * m4];
-                s1 += l4.y * x[4 * m4 + 1];
-                s2 += l4.z * x[4 * m4 + 2];
-                s3 += l4.w * x[4 * m4 + 3];
+                for (int m = 0; m < i; m += 2) {
+                    s0 += sL[o + i][o + m] * x[m];
+                    if (m + 1 < i) s1 += sL[o + i][o + m + 1] * x[m + 1];
+                }
+                x[i] = (i == j) ? 1.f : s0 + s1;
             }
-            x[i] = (i == j) ? 1.f : (s0 + s1) + (s2 + s3);
-        }
 #pragma unroll
-        for (int i = 0; i < kChunk; ++i) sT[i][j] = x[i];
+            for (int i = 0; i < 16; ++i) sT[o + i][o + j] = x[i];
+        } else {  // zero the strictly upper blocks
+            for (int idx = tid - 64; idx < 6 * 256; idx += kPrepThreads - 64) {
+                const int blkid = idx >> 8, e = idx & 255;
+                const int rb = blkid < 3 ? 0 : (blkid < 5 ? 1 : 2);
+                const int cb = blkid < 3 ? blkid + 1 : (blkid < 5 ? blkid - 1 : 3);
+                sT[16 * rb + (e >> 4)][16 * cb + (e & 15)] = 0.f;
+            }
+        }
+    }
+    __syncthreads();
+    if (ok) {  // distance 1: Y_c = L_{c+1,c} T_cc
+        for (int o = tid; o < 768; o += kPrepThreads) {
+            const int cb = o >> 8, i = (o >> 4) & 15, j = o & 15;
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int m = 0; m < 16; m += 2) {
+                s0 += sL[16 * (cb + 1) + i][16 * cb + m] * sT[16 * cb + m][16 * cb + j];
+                s1 += sL[16 * (cb + 1) + i][16 * cb + m + 1] * sT[16 * cb + m + 1][16 * cb + j];
+            }
+            sY[cb][i][j] = s0 + s1;
+        }
+    }
+    __syncthreads();
+    if (ok) {  // T_{c+1,c} = T_{c+1,c+1} Y_c
+        for (int o = tid; o < 768; o += kPrepThreads) {
+            const int cb = o >> 8, i = (o >> 4) & 15, j = o & 15, rb = 16 * (cb + 1);
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int m = 0; m < 16; m += 2) {
+                s0 += sT[rb + i][rb + m] * sY[cb][m][j];
+                s1 += sT[rb + i][rb + m + 1] * sY[cb][m + 1][j];
+            }
+            sT[rb + i][16 * cb + j] = s0 + s1;
+        }
+    }
+    __syncthreads();
+    if (ok) {  // distance 2: Y_c = L_{c+2,c} T_cc + L_{c+2,c+1} T_{c+1,c}
+        const int cb = tid >> 8, i = (tid >> 4) & 15, j = tid & 15, rb = 16 * (cb + 2);
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            s0 += sL[rb + i][16 * cb + m] * sT[16 * cb + m][16 * cb + j];
+            s1 += sL[rb + i][16 * (cb + 1) + m] * sT[16 * (cb + 1) + m][16 * cb + j];
+        }
+        sY[cb][i][j] = s0 + s1;
+    }
+    __syncthreads();
+    if (ok) {  // T_{c+2,c} = T_{c+2,c+2} Y_c
+        const int cb = tid >> 8, i = (tid >> 4) & 15, j = tid & 15, rb = 16 * (cb + 2);
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; m += 2) {
+            s0 += sT[rb + i][rb + m] * sY[cb][m][j];
+            s1 += sT[rb + i][rb + m + 1] * sY[cb][m + 1][j];
+        }
+        sT[rb + i][16 * cb + j] = s0 + s1;
+    }
+    __syncthreads();
+    if (ok && tid < 256) {  // distance 3: Y = sum_{k<3} L_{3,k} T_{k,0}
+        const int i = tid >> 4, j = tid & 15;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            s0 += sL[48 + i][m] * sT[m][j];
+            s1 += sL[48 + i][16 + m] * sT[16 + m][j];
+            s2 += sL[48 + i][32 + m] * sT[32 + m][j];
+        }
+        sY[0][i][j] = s0 + s1 + s2;
+    }
+    __syncthreads();
+    if (ok && tid < 256) {  // T_{3,0} = T_33 Y
+        const int i = tid >> 4, j = tid & 15;
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; m += 2) {
+            s0 += sT[48 + i][48 + m] * sY[0][m][j];
+            s1 += sT[48 + i][48 + m + 1] * sY[0][m + 1][j];
+        }
+        sT[48 + i][j] = s0 + s1;
     }
     __syncthreads();
 
-    // ---- 5. the four 64x64 coefficient matrices, hi/lo bf16 A tiles
+    // ---- 5. the four 64x64 coefficient matrices, hi/lo bf16 A tiles [X;Z] and [Y;W]
+    //      X = E_d T B_e, Y = E_d T B, W = (Aqk T) B, Z = (Aqk T) B_e
     if (ok) {
-        const int i = tid & 63, j0 = (tid >> 6) * 16;
-        float at[16];
+        const int i = tid & 63, j0 = (tid >> 6) * 8;
+        float at[8];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) at[e] = 0.f;
+        for (int e = 0; e < 8; ++e) at[e] = 0.f;
         for (int m = j0; m <= i; ++m) {  // (Aqk T)[i][j] = sum_{m=j..i} Aqk[i][m] T[m][j]
             const float a = sA[i][m];
-#pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-                const float4 t4 = *reinterpret_cast<const float4*>(&sT[m][j0 + 4 * e4]);
-                at[4 * e4] += a * t4.x;
-                at[4 * e4 + 1] += a * t4.y;
-                at[4 * e4 + 2] += a * t4.z;
-                at[4 * e4 + 3] += a * t4.w;
-            }
+            const float4 t0v = *reinterpret_cast<const float4*>(&sT[m][j0]);
+            const float4 t1v = *reinterpret_cast<const float4*>(&sT[m][j0 + 4]);
+            at[0] += a * t0v.x;
+            at[1] += a * t0v.y;
+            at[2] += a * t0v.z;
+            at[3] += a * t0v.w;
+            at[4] += a * t1v.x;
+            at[5] += a * t1v.y;
+            at[6] += a * t1v.z;
+            at[7] += a * t1v.w;
         }
+        const float4 ta = *reinterpret_cast<const float4*>(&sT[i][j0]);
+        const float4 tb = *reinterpret_cast<const float4*>(&sT[i][j0 + 4]);
+        const float ti[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
         const float ekdi = ms.ekd[i];
-        float X[16], Y[16], W[16], Z[16], ti[16];
+        float X[8], Y[8], W[8], Z[8];
 #pragma unroll
-        for (int e4 = 0; e4 < 4; ++e4) {
-            const float4 t4 = *reinterpret_cast<const float4*>(&sT[i][j0 + 4 * e4]);
-            ti[4 * e4] = t4.x;
-            ti[4 * e4 + 1] = t4.y;
-            ti[4 * e4 + 2] = t4.z;
-            ti[4 * e4 + 3] = t4.w;
-        }
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
+        for (int e = 0; e < 8; ++e) {
             const int j = j0 + e;
             const float bj = ms.beta[j], bej = ms.beta[j] * ms.egc[j];
-            const float tij = ti[e];
-            X[e] = ekdi * tij * bej;
-            Y[e] = ekdi * tij * bj;
+            X[e] = ekdi * ti[e] * bej;
+            Y[e] = ekdi * ti[e] * bj;
             W[e] = at[e] * bj;
             Z[e] = at[e] * bej;
         }
         unsigned char* sp = sm + P_SPLIT;
-#pragma unroll
-        for (int h8 = 0; h8 < 2; ++h8) {
-            const uint32_t off = sw128_offset(i, j0 + 8 * h8, 64);
-            store_split8(sp + 0 * 8192, sp + 1 * 8192, off, X + 8 * h8);
-            store_split8(sp + 2 * 8192, sp + 3 * 8192, off, Y + 8 * h8);
-            store_split8(sp + 4 * 8192, sp + 5 * 8192, off, W + 8 * h8);
-            store_split8(sp + 6 * 8192, sp + 7 * 8192, off, Z + 8 * h8);
-        }
+        store_split8(sp + 0 * 16384, sp + 1 * 16384, sw128_offset(i, j0, 128), X);
+        store_split8(sp + 0 * 16384, sp + 1 * 16384, sw128_offset(64 + i, j0, 128), Z);
+        store_split8(sp + 2 * 16384, sp + 3 * 16384, sw128_offset(i, j0, 128), Y);
+        store_split8(sp + 2 * 16384, sp + 3 * 16384, sw128_offset(64 + i, j0, 128), W);
     }
     fence_proxy_async_smem();
     __syncthreads();
 
-    // ---- 6. P_X = X k^ [0,128), P_Y = Y v [128,256), Zk = Z k^ [256,384), o0 = W v [384,512)
+    // ---- 6. [X;Z] k^ -> cols [0,128) (P_X | Zk), [Y;W] v -> cols [128,256) (P_Y | o0); M=128, N=128, K=64, hi+lo
     if (ok && tid == 0) {
         tc_fence_after();
-        const uint32_t id = make_idesc_f16(64, 128, false, true, true);
+        const uint32_t id = make_idesc_f16(128, 128, false, true, true);
         const uint32_t sp = sbase + P_SPLIT;
-        const uint32_t a_tiles[4] = {sp + 0 * 8192, sp + 2 * 8192, sp + 6 * 8192, sp + 4 * 8192};
-        const uint32_t b_tiles[4] = {sbase + P_KH, sbase + P_V, sbase + P_KH, sbase + P_V};
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
+        for (int r = 0; r < 2; ++r) {
+            const uint32_t bt = r == 0 ? sbase + P_KQ : sbase + P_V;
+            const uint32_t blbo = r == 0 ? 16384 : 8192;
 #pragma unroll
-            for (int s = 0; s < 2; ++s) {  // hi, lo
+            for (int s2 = 0; s2 < 2; ++s2) {  // hi, lo
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks) {
-                    const uint64_t ad = make_sdesc(a_tiles[r] + s * 8192 + ks * 32, 16, 1024, kSwizzle128B);
-                    const uint64_t bd = make_sdesc(b_tiles[r] + ks * 2048, 8192, 1024, kSwizzle128B);
-                    mma_f16(tm + 128 * r, ad, bd, id, (s | ks) != 0);
+                    const uint64_t ad = make_sdesc(sp + (2 * r + s2) * 16384 + ks * 32, 16, 1024, kSwizzle128B);
+                    const uint64_t bd = make_sdesc(bt + ks * 2048, blbo, 1024, kSwizzle128B);
+                    mma_f16(tm + 128 * r, ad, bd, id, (s2 | ks) != 0);
                 }
             }
         }
@@ -357,61 +435,42 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);
     tc_fence_after();
 
-    // ---- 7. epilogue: P_X/P_Y -> hi/lo B tiles, Q' and o0 -> workspace
+    // ---- 7. rows 0-63: P_X, P_Y -> hi/lo B tiles; rows 64-127: Q' and o0 -> workspace
     if (!__syncthreads_or(!ok)) {
-        const int i = 16 * quad + lane;  // valid for lane < 16
+        const int r = 32 * quad + lane, i = r & 63;
         unsigned char* sp = sm + P_SPLIT;
-        // P_X -> PXh/PXl at +0/+16K, P_Y -> PYh/PYl at +32K/+48K (MN-major B: rows = tokens)
+        float v[32];
+        tmem_ld32(tmem_addr(tm, 32 * quad, 32 * cq), v);
+        tmem_ld_wait();
+        if (r < 64) {  // P_X (MN-major B tile: rows = tokens)
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+            for (int q8 = 0; q8 < 4; ++q8)
+                store_split8(sp, sp + 16384, sw128_offset(i, 32 * cq + 8 * q8, 64), v + 8 * q8);
+        } else {  // Q' = q^ Dk^-1/2 e^gc - Zk (the q e^gc S of :175 and -Aqk w S of :176 combined)
+            const float qs = scale * ms.egc[i];
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                float v[32];
-                tmem_ld32(tmem_addr(tm, 32 * quad, 128 * r + 64 * half + 32 * cc), v);
-                tmem_ld_wait();
-                if (lane < 16) {
+            for (int q8 = 0; q8 < 4; ++q8) {
+                const int d = 32 * cq + 8 * q8;
+                const uint4 qu = *reinterpret_cast<const uint4*>(sm + P_KQ + sw128_offset(64 + i, d, 128));
+                const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(&qu);
+                float o[8];
 #pragma unroll
-                    for (int q8 = 0; q8 < 4; ++q8) {
-                        const int d = 64 * half + 32 * cc + 8 * q8;
-                        store_split8(sp + r * 32768, sp + r * 32768 + 16384, sw128_offset(i, d, 64), v + 8 * q8);
-                    }
-                }
+                for (int e = 0; e < 8; ++e) o[e] = qs * __bfloat162float(qb[e]) - v[8 * q8 + e];
+                store_bf16x8(wrec + kTcQ, sw128_offset(i, d, 64), o);
             }
         }
-        // Q' = q^ Dk^-1/2 e^gc - Zk  (the q e^gc S term of :175 and -Aqk w S of :176 combined)
+        tmem_ld32(tmem_addr(tm, 32 * quad, 128 + 32 * cq), v);
+        tmem_ld_wait();
+        if (r < 64) {  // P_Y
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-            float v[32];
-            tmem_ld32(tmem_addr(tm, 32 * quad, 256 + 64 * half + 32 * cc), v);
-            tmem_ld_wait();
-            if (lane < 16) {
-                const float qs = scale * ms.egc[i];
+            for (int q8 = 0; q8 < 4; ++q8)
+                store_split8(sp + 32768, sp + 49152, sw128_offset(i, 32 * cq + 8 * q8, 64), v + 8 * q8);
+        } else {  // o0 = Aqk u, fp32 column tile cq
+            unsigned char* blk = wrec + kTcO0 + cq * (64 * 128);
 #pragma unroll
-                for (int q8 = 0; q8 < 4; ++q8) {
-                    const int d = 64 * half + 32 * cc + 8 * q8;
-                    const uint32_t off = sw128_offset(i, d, 64);
-                    const uint4 qu = *reinterpret_cast<const uint4*>(sm + P_QH + off);
-                    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(&qu);
-                    float o[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) o[e] = qs * __bfloat162float(qb[e]) - v[8 * q8 + e];
-                    store_bf16x8(wrec + kTcQ, off, o);
-                }
-            }
-        }
-        // o0 = Aqk u, fp32 column tiles of 32
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-            float v[32];
-            tmem_ld32(tmem_addr(tm, 32 * quad, 384 + 64 * half + 32 * cc), v);
-            tmem_ld_wait();
-            if (lane < 16) {
-                unsigned char* blk = wrec + kTcO0 + (2 * half + cc) * (64 * 128);
-#pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4)
-                    *reinterpret_cast<float4*>(blk + f32blk_offset(i, q4)) =
-                        make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
-            }
+            for (int q4 = 0; q4 < 8; ++q4)
+                *reinterpret_cast<float4*>(blk + f32blk_offset(i, q4)) =
+                    make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
         }
     } else {
         ok = false;
@@ -421,19 +480,19 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     __syncthreads();
     tc_fence_after();
 
-    // ---- 8. M' = k^T P_X -> [0,128), b = k^T P_Y -> [128,256)  (M=128 over Dk)
+    // ---- 8. M' = k^T P_X -> [0,128), b = k^T P_Y -> [128,256)  (M=128 over Dk, K = tokens)
     if (ok && tid == 0) {
         const uint32_t id = make_idesc_f16(128, 128, true, true, true);
         const uint32_t sp = sbase + P_SPLIT;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
 #pragma unroll
-            for (int s = 0; s < 2; ++s) {
+            for (int s2 = 0; s2 < 2; ++s2) {
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks) {
-                    const uint64_t ad = make_sdesc(sbase + P_KH + ks * 2048, 8192, 1024, kSwizzle128B);
-                    const uint64_t bd = make_sdesc(sp + r * 32768 + s * 16384 + ks * 2048, 8192, 1024, kSwizzle128B);
-                    mma_f16(tm + 128 * r, ad, bd, id, (s | ks) != 0);
+                    const uint64_t ad = make_sdesc(sbase + P_KQ + ks * 2048, 16384, 1024, kSwizzle128B);
+                    const uint64_t bd = make_sdesc(sp + (2 * r + s2) * 16384 + ks * 2048, 8192, 1024, kSwizzle128B);
+                    mma_f16(tm + 128 * r, ad, bd, id, (s2 | ks) != 0);
                 }
             }
         }
@@ -446,38 +505,31 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     if (!__syncthreads_or(!ok)) {
         const int dk = 32 * quad + lane;
         const float gamma = ms.egc[kChunk - 1];
+        float v[32];
+        tmem_ld32(tmem_addr(tm, 32 * quad, 32 * cq), v);
+        tmem_ld_wait();
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-            float v[32];
-            tmem_ld32(tmem_addr(tm, 32 * quad, 64 * half + 32 * cc), v);
-            tmem_ld_wait();
+        for (int q8 = 0; q8 < 4; ++q8) {
+            const int col = 32 * cq + 8 * q8;
+            float m[8];
 #pragma unroll
-            for (int q8 = 0; q8 < 4; ++q8) {
-                const int col = 64 * half + 32 * cc + 8 * q8;
-                float m[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) m[e] = ((col + e) == dk ? gamma : 0.f) - v[8 * q8 + e];
-                store_bf16x8(wrec + kTcM, sw128_offset(dk, col, 128), m);
-            }
+            for (int e = 0; e < 8; ++e) m[e] = ((col + e) == dk ? gamma : 0.f) - v[8 * q8 + e];
+            store_bf16x8(wrec + kTcM, sw128_offset(dk, col, 128), m);
         }
+        tmem_ld32(tmem_addr(tm, 32 * quad, 128 + 32 * cq), v);
+        tmem_ld_wait();
+        unsigned char* blk = wrec + kTcB + cq * (128 * 128);
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-            float v[32];
-            tmem_ld32(tmem_addr(tm, 32 * quad, 128 + 64 * half + 32 * cc), v);
-            tmem_ld_wait();
-            unsigned char* blk = wrec + kTcB + (2 * half + cc) * (128 * 128);
-#pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4)
-                *reinterpret_cast<float4*>(blk + f32blk_offset(dk, q4)) =
-                    make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
-        }
+        for (int q4 = 0; q4 < 8; ++q4)
+            *reinterpret_cast<float4*>(blk + f32blk_offset(dk, q4)) =
+                make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
     } else {
         ok = false;
     }
     if (!ok && tid == 0) report(p.err, kErrTimeoutPrep);
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tm, 512);
+    if (warp == 0) tmem_dealloc(tm, kPrepTmemCols);
 }
 
 // ============================================================================ scan
