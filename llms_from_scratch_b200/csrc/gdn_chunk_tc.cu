@@ -33,9 +33,10 @@
 //   8. M' = k^T P_X, b = k^T P_Y (M=128, N=128, K=64, hi+lo)
 //   9. M = e^gc_last I - M', b -> workspace
 // gdn_scan_tc: one CTA per (batch, head, 32-column slice of Dv); warp 4
-//   bulk-copies each chunk's workspace record (double-buffered), warp 5 issues
-//   the two MMAs, warps 0-3 turn the accumulators into the next state and the
-//   output rows.
+//   bulk-copies each chunk's workspace record (double-buffered); warps 0-3 turn
+//   the accumulators into the next state, thread 0 issues the next chunk's two
+//   MMAs as soon as the state is in shared memory, and the output rows of a
+//   chunk are written while the next chunk's MMAs run.
 #include <cuda_bf16.h>
 
 #include "gdn_common.cuh"
@@ -534,7 +535,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
 
 // ============================================================================ scan
 
-constexpr int kScanThreads = 192;          // warps 0-3: epilogue, 4: bulk copies, 5: MMA
+constexpr int kScanThreads = 160;          // warps 0-3: state/output epilogue (thread 0 issues the MMAs), 4: bulk copies
 constexpr uint32_t S_STAGE = 73728;        // M image 32K | Q image 16K | b slice 16K | o0 slice 8K
 constexpr uint32_t S_OFF_Q = 32768, S_OFF_B = 49152, S_OFF_O0 = 65536;
 constexpr uint32_t S_STILE = 2 * S_STAGE;  // state operand: bf16 [128 dk][64] swizzled (32 columns used)
@@ -545,10 +546,46 @@ struct ScanMisc {
     uint64_t full[2];
     uint64_t empty[2];
     uint64_t mma_done;
-    uint64_t s_ready;
     uint32_t tmem;
     int abort;
 };
+
+// Named barrier over `nthreads` threads that also returns whether any of them passed `flag` != 0,
+// so a failure seen by one thread ends the loop of all of them together.
+__device__ __forceinline__ bool named_barrier_any(uint32_t id, uint32_t nthreads, bool flag) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)flag), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
+// o_c rows 16w..16w+15 of this CTA's 32 columns: o = Q'S (accumulator) + o0 (stage smem).
+__device__ __forceinline__ void scan_store_output(const ChunkParams& p, const unsigned char* st, const float (&o)[32],
+                                                  int c, int warp, int lane, int b, int h, int dv0) {
+    if (lane >= 16) return;
+    const int tok = 16 * warp + lane;
+    const int64_t t = (int64_t)c * kChunk + tok;
+    if (t >= p.T) return;
+    float ov[32];
+#pragma unroll
+    for (int q4 = 0; q4 < 8; ++q4) {
+        const float4 oo = *reinterpret_cast<const float4*>(st + S_OFF_O0 + f32blk_offset(tok, q4));
+        ov[4 * q4] = o[4 * q4] + oo.x;
+        ov[4 * q4 + 1] = o[4 * q4 + 1] + oo.y;
+        ov[4 * q4 + 2] = o[4 * q4 + 2] + oo.z;
+        ov[4 * q4 + 3] = o[4 * q4 + 3] + oo.w;
+    }
+    unsigned char* dst = reinterpret_cast<unsigned char*>(p.out) +
+                         2 * ((int64_t)b * p.out_sb + t * p.out_st + (int64_t)h * p.out_sh + dv0);
+#pragma unroll
+    for (int q8 = 0; q8 < 4; ++q8) store_bf16x8(dst, 16 * q8, ov + 8 * q8);
+}
 
 __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -567,7 +604,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             mbar_init(&ms.empty[s], 128);
         }
         mbar_init(&ms.mma_done, 1);
-        mbar_init(&ms.s_ready, 128);
         ms.abort = 0;
         fence_mbar_init();
     }
@@ -606,34 +642,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             for (int c = (issued > 2 ? issued - 2 : 0); c < issued; ++c)
                 if (!mbar_wait(&ms.full[c & 1], (c >> 1) & 1, kWaitNs)) ok = false;
         }
-    } else if (warp == 5) {
-        // ---------------- MMA issuer
-        if (lane == 0) {
-            const uint32_t idS = make_idesc_f16(128, kTcDvTile, false, true, true);
-            const uint32_t idO = make_idesc_f16(64, kTcDvTile, false, true, true);
-            for (int c = 0; c < p.NC; ++c) {
-                const int s = c & 1;
-                if (!mbar_wait(&ms.full[s], (c >> 1) & 1, kWaitNs) || !mbar_wait(&ms.s_ready, c & 1, kWaitNs)) {
-                    ok = false;
-                    break;
-                }
-                if (ms.abort) break;
-                tc_fence_after();
-                const uint32_t st = sbase + s * S_STAGE;
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks) {
-                    const uint64_t bd = make_sdesc(sbase + S_STILE + ks * 2048, 16384, 1024, kSwizzle128B);
-                    const uint64_t am = make_sdesc(st + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSwizzle128B);
-                    const uint64_t aq =
-                        make_sdesc(st + S_OFF_Q + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024, kSwizzle128B);
-                    mma_f16(tm + 0, am, bd, idS, ks > 0);
-                    mma_f16(tm + kTcDvTile, aq, bd, idO, ks > 0);
-                }
-                mma_commit(&ms.mma_done);
-            }
-        }
     } else {
-        // ---------------- epilogue: thread = state row dk (TMEM lane), warp w also owns output rows 16w..16w+15
+        // ---------------- thread = state row dk (TMEM lane); warp w also owns output rows 16w..16w+15
         const int dk = tid;
         float S[kTcDvTile];
         const int64_t srow = ((int64_t)bh * kDk + dk) * kDv + dv0;
@@ -649,18 +659,52 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
 #pragma unroll
         for (int q8 = 0; q8 < kTcDvTile / 8; ++q8) store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
         fence_proxy_async_smem();
-        mbar_arrive(&ms.s_ready);
 
+        // descriptors of stage 0 / k-step 0; the others differ only in the start address
+        const uint32_t idS = make_idesc_f16(128, kTcDvTile, false, true, true);
+        const uint32_t idO = make_idesc_f16(64, kTcDvTile, false, true, true);
+        const uint64_t dM = make_sdesc(sbase, 16, 1024, kSwizzle128B);
+        const uint64_t dQ = make_sdesc(sbase + S_OFF_Q, 16, 1024, kSwizzle128B);
+        const uint64_t dS = make_sdesc(sbase + S_STILE, 16384, 1024, kSwizzle128B);
+
+        float o_prev[32];
         for (int c = 0; c < p.NC; ++c) {
             const int s = c & 1;
-            if (!mbar_wait(&ms.mma_done, c & 1, kWaitNs)) {
+            // every row of S_c is in the operand tile; leave together if any thread failed a wait
+            if (named_barrier_any(1, 128, !ok)) {
                 ok = false;
                 break;
             }
+            if (tid == 0) {
+                if (!mbar_wait(&ms.full[s], (c >> 1) & 1, kWaitNs)) {
+                    ms.abort = 1;  // no MMA this chunk: every thread's mma_done wait below gives up
+                } else {
+                    tc_fence_after();
+                    const uint64_t so = (uint64_t)((s * S_STAGE) >> 4);
+#pragma unroll
+                    for (int ks = 0; ks < 8; ++ks) {
+                        const uint64_t ao = so + (uint64_t)((((ks >> 2) * 16384) + (ks & 3) * 32) >> 4);
+                        const uint64_t aq = so + (uint64_t)((((ks >> 2) * 8192) + (ks & 3) * 32) >> 4);
+                        const uint64_t bd = dS + (uint64_t)((ks * 2048) >> 4);
+                        mma_f16(tm + 0, dM + ao, bd, idS, ks > 0);
+                        mma_f16(tm + kTcDvTile, dQ + aq, bd, idO, ks > 0);
+                    }
+                    mma_commit(&ms.mma_done);
+                }
+            }
+            // previous chunk's output rows, overlapping this chunk's MMAs
+            if (c > 0) {
+                scan_store_output(p, sm + ((c - 1) & 1) * S_STAGE, o_prev, c - 1, warp, lane, b, h, dv0);
+                mbar_arrive(&ms.empty[(c - 1) & 1]);
+            }
+            if (!mbar_wait(&ms.mma_done, c & 1, kWaitNs)) {
+                ok = false;
+                continue;  // the barrier at the top of the loop ends every thread's loop
+            }
             tc_fence_after();
-            float d[32], o[32];
+            float d[32];
             tmem_ld32(tmem_addr(tm, 32 * warp, 0), d);
-            tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile), o);
+            tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile), o_prev);
             tmem_ld_wait();
             const unsigned char* st = sm + s * S_STAGE;
             // S_{c+1} = M_c S_c + b_c
@@ -672,42 +716,23 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                 S[4 * q4 + 2] = d[4 * q4 + 2] + bb.z;
                 S[4 * q4 + 3] = d[4 * q4 + 3] + bb.w;
             }
-            // hand S_{c+1} to the MMA warp first: it is the only thing on the sequential path
-            tc_fence_before();
             if (c + 1 < p.NC) {
 #pragma unroll
                 for (int q8 = 0; q8 < kTcDvTile / 8; ++q8)
                     store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
                 fence_proxy_async_smem();
-                mbar_arrive(&ms.s_ready);
             }
-            // o_c = Q'_c S_c + o0_c for tokens 16w + lane (M=64 accumulator rows)
-            if (lane < 16) {
-                const int tok = 16 * warp + lane;
-                const int64_t t = (int64_t)c * kChunk + tok;
-                if (t < p.T) {
-                    float ov[32];
-#pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4) {
-                        const float4 oo = *reinterpret_cast<const float4*>(st + S_OFF_O0 + f32blk_offset(tok, q4));
-                        ov[4 * q4] = o[4 * q4] + oo.x;
-                        ov[4 * q4 + 1] = o[4 * q4 + 1] + oo.y;
-                        ov[4 * q4 + 2] = o[4 * q4 + 2] + oo.z;
-                        ov[4 * q4 + 3] = o[4 * q4 + 3] + oo.w;
-                    }
-                    unsigned char* dst = reinterpret_cast<unsigned char*>(p.out) +
-                                         2 * ((int64_t)b * p.out_sb + t * p.out_st + (int64_t)h * p.out_sh + dv0);
-#pragma unroll
-                    for (int q8 = 0; q8 < 4; ++q8) store_bf16x8(dst, 16 * q8, ov + 8 * q8);
-                }
-            }
-            mbar_arrive(&ms.empty[s]);
+            tc_fence_before();
         }
-        if (ok && p.hT) {
+        if (ok) {
+            scan_store_output(p, sm + ((p.NC - 1) & 1) * S_STAGE, o_prev, p.NC - 1, warp, lane, b, h, dv0);
+            mbar_arrive(&ms.empty[(p.NC - 1) & 1]);
+            if (p.hT) {
 #pragma unroll
-            for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
-                *reinterpret_cast<float4*>(p.hT + srow + 4 * q4) =
-                    make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
+                for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
+                    *reinterpret_cast<float4*>(p.hT + srow + 4 * q4) =
+                        make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
+            }
         }
     }
     if (!ok) {
