@@ -32,8 +32,10 @@
 //   7. Q' = q^ e^gc Dk^-1/2 - Zk, o0 -> workspace; P_X, P_Y -> hi+lo B tiles
 //   8. M' = k^T P_X, b = k^T P_Y (M=128, N=128, K=64, hi+lo)
 //   9. M = e^gc_last I - M', b -> workspace
-// gdn_scan_tc: one CTA per (batch, head, 32-column slice of Dv); warp 4
-//   bulk-copies each chunk's workspace record (double-buffered); warps 0-3 turn
+// gdn_scan_tc: one CTA per (batch, head, 32-column slice of Dv); warps 4-5
+//   bulk-copy each chunk's workspace record (double-buffered, the M/Q half freed
+//   as soon as the tensor core has read it, records pulled into L2 four chunks
+//   ahead); warps 0-3 turn
 //   the accumulators into the next state, thread 0 issues the next chunk's two
 //   MMAs as soon as the state is in shared memory, and the output rows of a
 //   chunk are written while the next chunk's MMAs run.
@@ -535,7 +537,9 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
 
 // ============================================================================ scan
 
-constexpr int kScanThreads = 160;          // warps 0-3: state/output epilogue (thread 0 issues the MMAs), 4: bulk copies
+constexpr int kScanThreads = 192;          // warps 0-3: state/output epilogue (thread 0 issues the MMAs),
+                                           // 4: M/Q bulk copies + L2 prefetch, 5: b/o0 bulk copies
+constexpr int kScanPrefetch = 4;           // chunks ahead that the producer pulls into L2
 constexpr uint32_t S_STAGE = 73728;        // M image 32K | Q image 16K | b slice 16K | o0 slice 8K
 constexpr uint32_t S_OFF_Q = 32768, S_OFF_B = 49152, S_OFF_O0 = 65536;
 constexpr uint32_t S_STILE = 2 * S_STAGE;  // state operand: bf16 [128 dk][64] swizzled (32 columns used)
@@ -543,8 +547,10 @@ constexpr uint32_t S_MISC = S_STILE + 16384;
 constexpr uint32_t S_SMEM = S_MISC + 256 + 1024;
 
 struct ScanMisc {
-    uint64_t full[2];
-    uint64_t empty[2];
+    uint64_t full_mq[2];   // M/Q images landed (tx)
+    uint64_t full_bo[2];   // b/o0 slices landed (tx)
+    uint64_t empty_mq[2];  // the MMAs that read M/Q completed (tcgen05.commit)
+    uint64_t empty_bo[2];  // the epilogue read b and o0 (128 arrivals)
     uint64_t mma_done;
     uint32_t tmem;
     int abort;
@@ -600,8 +606,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
 
     if (tid == 0) {
         for (int s = 0; s < 2; ++s) {
-            mbar_init(&ms.full[s], 1);
-            mbar_init(&ms.empty[s], 128);
+            mbar_init(&ms.full_mq[s], 1);
+            mbar_init(&ms.full_bo[s], 1);
+            mbar_init(&ms.empty_mq[s], 1);
+            mbar_init(&ms.empty_bo[s], 128);
         }
         mbar_init(&ms.mma_done, 1);
         ms.abort = 0;
@@ -618,29 +626,42 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     const uint32_t sbase = smem_u32(sm);
     bool ok = true;
 
-    if (warp == 4) {
-        // ---------------- producer: one chunk record per stage
+    if (warp >= 4) {
+        // ---------------- producers: warp 4 streams the M/Q images, warp 5 the b/o0 slices
         if (lane == 0) {
+            const bool mq = warp == 4;
+            uint64_t* full = mq ? ms.full_mq : ms.full_bo;
+            uint64_t* empty = mq ? ms.empty_mq : ms.empty_bo;
+            const uint32_t bytes = mq ? 32768 + 16384 : 16384 + 8192;
             int issued = 0;
             for (int c = 0; c < p.NC; ++c) {
                 const int s = c & 1;
-                if (c >= 2 && !mbar_wait(&ms.empty[s], ((c >> 1) - 1) & 1, kWaitNs)) {
+                if (mq && c + kScanPrefetch < p.NC) {
+                    const unsigned char* pre = wbase + (int64_t)(c + kScanPrefetch) * kTcChunkBytes;
+                    bulk_prefetch_l2(pre + kTcM, 32768 + 16384);
+                    bulk_prefetch_l2(pre + kTcB + dvt * 16384, 16384);
+                    bulk_prefetch_l2(pre + kTcO0 + dvt * 8192, 8192);
+                }
+                if (c >= 2 && !mbar_wait(&empty[s], ((c >> 1) - 1) & 1, kWaitNs)) {
                     ok = false;
                     break;
                 }
                 if (ms.abort) break;
                 const unsigned char* rec = wbase + (int64_t)c * kTcChunkBytes;
                 unsigned char* st = sm + s * S_STAGE;
-                mbar_arrive_expect_tx(&ms.full[s], S_STAGE);
-                bulk_g2s(st, rec + kTcM, 32768, &ms.full[s]);
-                bulk_g2s(st + S_OFF_Q, rec + kTcQ, 16384, &ms.full[s]);
-                bulk_g2s(st + S_OFF_B, rec + kTcB + dvt * 16384, 16384, &ms.full[s]);
-                bulk_g2s(st + S_OFF_O0, rec + kTcO0 + dvt * 8192, 8192, &ms.full[s]);
+                mbar_arrive_expect_tx(&full[s], bytes);
+                if (mq) {
+                    bulk_g2s(st, rec + kTcM, 32768, &full[s]);
+                    bulk_g2s(st + S_OFF_Q, rec + kTcQ, 16384, &full[s]);
+                } else {
+                    bulk_g2s(st + S_OFF_B, rec + kTcB + dvt * 16384, 16384, &full[s]);
+                    bulk_g2s(st + S_OFF_O0, rec + kTcO0 + dvt * 8192, 8192, &full[s]);
+                }
                 ++issued;
             }
             // leave no copy in flight: wait for the last record of each stage to land
             for (int c = (issued > 2 ? issued - 2 : 0); c < issued; ++c)
-                if (!mbar_wait(&ms.full[c & 1], (c >> 1) & 1, kWaitNs)) ok = false;
+                if (!mbar_wait(&full[c & 1], (c >> 1) & 1, kWaitNs)) ok = false;
         }
     } else {
         // ---------------- thread = state row dk (TMEM lane); warp w also owns output rows 16w..16w+15
@@ -676,7 +697,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                 break;
             }
             if (tid == 0) {
-                if (!mbar_wait(&ms.full[s], (c >> 1) & 1, kWaitNs)) {
+                if (!mbar_wait(&ms.full_mq[s], (c >> 1) & 1, kWaitNs)) {
                     ms.abort = 1;  // no MMA this chunk: every thread's mma_done wait below gives up
                 } else {
                     tc_fence_after();
@@ -690,14 +711,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                         mma_f16(tm + kTcDvTile, dQ + aq, bd, idO, ks > 0);
                     }
                     mma_commit(&ms.mma_done);
+                    mma_commit(&ms.empty_mq[s]);
                 }
             }
             // previous chunk's output rows, overlapping this chunk's MMAs
             if (c > 0) {
                 scan_store_output(p, sm + ((c - 1) & 1) * S_STAGE, o_prev, c - 1, warp, lane, b, h, dv0);
-                mbar_arrive(&ms.empty[(c - 1) & 1]);
+                mbar_arrive(&ms.empty_bo[(c - 1) & 1]);
             }
-            if (!mbar_wait(&ms.mma_done, c & 1, kWaitNs)) {
+            if (!mbar_wait(&ms.mma_done, c & 1, kWaitNs) || !mbar_wait(&ms.full_bo[s], (c >> 1) & 1, kWaitNs)) {
                 ok = false;
                 continue;  // the barrier at the top of the loop ends every thread's loop
             }
@@ -726,7 +748,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
         }
         if (ok) {
             scan_store_output(p, sm + ((p.NC - 1) & 1) * S_STAGE, o_prev, p.NC - 1, warp, lane, b, h, dv0);
-            mbar_arrive(&ms.empty[(p.NC - 1) & 1]);
+            mbar_arrive(&ms.empty_bo[(p.NC - 1) & 1]);
             if (p.hT) {
 #pragma unroll
                 for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
