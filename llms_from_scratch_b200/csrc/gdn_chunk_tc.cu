@@ -35,10 +35,10 @@
 // gdn_scan_tc: one CTA per (batch, head, 32-column slice of Dv); warps 4-5
 //   bulk-copy each chunk's workspace record (double-buffered, the M/Q half freed
 //   as soon as the tensor core has read it, records pulled into L2 four chunks
-//   ahead); warps 0-3 turn
-//   the accumulators into the next state, thread 0 issues the next chunk's two
-//   MMAs as soon as the state is in shared memory, and the output rows of a
-//   chunk are written while the next chunk's MMAs run.
+//   ahead); warps 0-3 turn the state accumulator into the next state, one lane
+//   issues the next chunk's state MMAs as soon as that state is in shared
+//   memory (then the output MMAs, into alternating TMEM columns), and a chunk's
+//   output rows are written while the next chunk's MMAs run.
 #include <cuda_bf16.h>
 
 #include "gdn_common.cuh"
@@ -540,6 +540,8 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
 constexpr int kScanThreads = 192;          // warps 0-3: state/output epilogue (thread 0 issues the MMAs),
                                            // 4: M/Q bulk copies + L2 prefetch, 5: b/o0 bulk copies
 constexpr int kScanPrefetch = 4;           // chunks ahead that the producer pulls into L2
+constexpr int kScanIssuer = 16;            // warp 0 lane 16: issues the MMAs (lanes 16-31 own no output rows)
+constexpr uint32_t kScanTmemCols = 128;    // cols [0,32) state accumulator, [32,64) / [64,96) output accumulators
 constexpr uint32_t S_STAGE = 73728;        // M image 32K | Q image 16K | b slice 16K | o0 slice 8K
 constexpr uint32_t S_OFF_Q = 32768, S_OFF_B = 49152, S_OFF_O0 = 65536;
 constexpr uint32_t S_STILE = 2 * S_STAGE;  // state operand: bf16 [128 dk][64] swizzled (32 columns used)
@@ -551,7 +553,8 @@ struct ScanMisc {
     uint64_t full_bo[2];   // b/o0 slices landed (tx)
     uint64_t empty_mq[2];  // the MMAs that read M/Q completed (tcgen05.commit)
     uint64_t empty_bo[2];  // the epilogue read b and o0 (128 arrivals)
-    uint64_t mma_done;
+    uint64_t mma_s;        // state accumulator of this chunk ready
+    uint64_t mma_o[2];     // output accumulator of chunk c ready, alternating by chunk parity
     uint32_t tmem;
     int abort;
 };
@@ -611,12 +614,14 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             mbar_init(&ms.empty_mq[s], 1);
             mbar_init(&ms.empty_bo[s], 128);
         }
-        mbar_init(&ms.mma_done, 1);
+        mbar_init(&ms.mma_s, 1);
+        mbar_init(&ms.mma_o[0], 1);
+        mbar_init(&ms.mma_o[1], 1);
         ms.abort = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
-        tmem_alloc(&ms.tmem, 64);
+        tmem_alloc(&ms.tmem, kScanTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -688,7 +693,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
         const uint64_t dQ = make_sdesc(sbase + S_OFF_Q, 16, 1024, kSwizzle128B);
         const uint64_t dS = make_sdesc(sbase + S_STILE, 16384, 1024, kSwizzle128B);
 
-        float o_prev[32];
         for (int c = 0; c < p.NC; ++c) {
             const int s = c & 1;
             // every row of S_c is in the operand tile; leave together if any thread failed a wait
@@ -696,37 +700,47 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                 ok = false;
                 break;
             }
-            if (tid == 0) {
+            if (tid == kScanIssuer) {
                 if (!mbar_wait(&ms.full_mq[s], (c >> 1) & 1, kWaitNs)) {
-                    ms.abort = 1;  // no MMA this chunk: every thread's mma_done wait below gives up
+                    ms.abort = 1;  // no MMA this chunk: every thread's wait below gives up
                 } else {
                     tc_fence_after();
                     const uint64_t so = (uint64_t)((s * S_STAGE) >> 4);
+                    // state first: it is the only product on the sequential path
 #pragma unroll
-                    for (int ks = 0; ks < 8; ++ks) {
-                        const uint64_t ao = so + (uint64_t)((((ks >> 2) * 16384) + (ks & 3) * 32) >> 4);
-                        const uint64_t aq = so + (uint64_t)((((ks >> 2) * 8192) + (ks & 3) * 32) >> 4);
-                        const uint64_t bd = dS + (uint64_t)((ks * 2048) >> 4);
-                        mma_f16(tm + 0, dM + ao, bd, idS, ks > 0);
-                        mma_f16(tm + kTcDvTile, dQ + aq, bd, idO, ks > 0);
-                    }
-                    mma_commit(&ms.mma_done);
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16(tm + 0, dM + so + (uint64_t)((((ks >> 2) * 16384) + (ks & 3) * 32) >> 4),
+                                dS + (uint64_t)((ks * 2048) >> 4), idS, ks > 0);
+                    mma_commit(&ms.mma_s);
+#pragma unroll
+                    for (int ks = 0; ks < 8; ++ks)
+                        mma_f16(tm + kTcDvTile * (1 + s), dQ + so + (uint64_t)((((ks >> 2) * 8192) + (ks & 3) * 32) >> 4),
+                                dS + (uint64_t)((ks * 2048) >> 4), idO, ks > 0);
+                    mma_commit(&ms.mma_o[s]);
                     mma_commit(&ms.empty_mq[s]);
                 }
             }
             // previous chunk's output rows, overlapping this chunk's MMAs
             if (c > 0) {
-                scan_store_output(p, sm + ((c - 1) & 1) * S_STAGE, o_prev, c - 1, warp, lane, b, h, dv0);
-                mbar_arrive(&ms.empty_bo[(c - 1) & 1]);
+                const int sp = (c - 1) & 1;
+                if (!mbar_wait(&ms.mma_o[sp], ((c - 1) >> 1) & 1, kWaitNs)) {
+                    ok = false;
+                    continue;
+                }
+                tc_fence_after();
+                float o[32];
+                tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + sp)), o);
+                tmem_ld_wait();
+                scan_store_output(p, sm + sp * S_STAGE, o, c - 1, warp, lane, b, h, dv0);
+                mbar_arrive(&ms.empty_bo[sp]);
             }
-            if (!mbar_wait(&ms.mma_done, c & 1, kWaitNs) || !mbar_wait(&ms.full_bo[s], (c >> 1) & 1, kWaitNs)) {
+            if (!mbar_wait(&ms.mma_s, c & 1, kWaitNs) || !mbar_wait(&ms.full_bo[s], (c >> 1) & 1, kWaitNs)) {
                 ok = false;
                 continue;  // the barrier at the top of the loop ends every thread's loop
             }
             tc_fence_after();
             float d[32];
             tmem_ld32(tmem_addr(tm, 32 * warp, 0), d);
-            tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile), o_prev);
             tmem_ld_wait();
             const unsigned char* st = sm + s * S_STAGE;
             // S_{c+1} = M_c S_c + b_c
@@ -747,9 +761,18 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             tc_fence_before();
         }
         if (ok) {
-            scan_store_output(p, sm + ((p.NC - 1) & 1) * S_STAGE, o_prev, p.NC - 1, warp, lane, b, h, dv0);
-            mbar_arrive(&ms.empty_bo[(p.NC - 1) & 1]);
-            if (p.hT) {
+            const int sp = (p.NC - 1) & 1;
+            if (mbar_wait(&ms.mma_o[sp], ((p.NC - 1) >> 1) & 1, kWaitNs)) {
+                tc_fence_after();
+                float o[32];
+                tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + sp)), o);
+                tmem_ld_wait();
+                scan_store_output(p, sm + sp * S_STAGE, o, p.NC - 1, warp, lane, b, h, dv0);
+                mbar_arrive(&ms.empty_bo[sp]);
+            } else {
+                ok = false;
+            }
+            if (ok && p.hT) {
 #pragma unroll
                 for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
                     *reinterpret_cast<float4*>(p.hT + srow + 4 * q4) =
@@ -763,7 +786,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tm, 64);
+    if (warp == 0) tmem_dealloc(tm, kScanTmemCols);
 }
 
 }  // namespace
