@@ -145,9 +145,12 @@ __device__ __forceinline__ uint32_t tmem_addr(uint32_t base, uint32_t lane, uint
 }
 
 // 32 lanes x 32 columns of 32-bit: thread i of the warp receives columns
-// [col, col+32) of lane (32 * (warp % 4) + i).
+// [col, col+32) of lane (32 * (warp % 4) + i).  tcgen05.ld is warp-collective
+// (.sync.aligned), so the warp is reconverged first: a lane may still be in a
+// divergent branch (an MMA issuer, a spin on an mbarrier).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
+    __syncwarp();
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -164,6 +167,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // 32 lanes x 16 columns of 32-bit (same lane mapping as tmem_ld32).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
+    __syncwarp();
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
