@@ -544,8 +544,9 @@ constexpr int kScanIssuer = 16;            // warp 0 lane 16: issues the MMAs (l
 constexpr uint32_t kScanTmemCols = 128;    // cols [0,32) state accumulator, [32,64) / [64,96) output accumulators
 constexpr uint32_t S_STAGE = 73728;        // M image 32K | Q image 16K | b slice 16K | o0 slice 8K
 constexpr uint32_t S_OFF_Q = 32768, S_OFF_B = 49152, S_OFF_O0 = 65536;
-constexpr uint32_t S_STILE = 2 * S_STAGE;  // state operand: bf16 [128 dk][64] swizzled (32 columns used)
-constexpr uint32_t S_MISC = S_STILE + 16384;
+constexpr uint32_t S_STILE = 2 * S_STAGE;  // state operand, two tiles by chunk parity: bf16 [128 dk][64] swizzled
+                                           // (32 columns used); chunk c's MMAs read tile c % 2
+constexpr uint32_t S_MISC = S_STILE + 2 * 16384;
 constexpr uint32_t S_SMEM = S_MISC + 256 + 1024;
 
 struct ScanMisc {
@@ -710,12 +711,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks)
                         mma_f16(tm + 0, dM + so + (uint64_t)((((ks >> 2) * 16384) + (ks & 3) * 32) >> 4),
-                                dS + (uint64_t)((ks * 2048) >> 4), idS, ks > 0);
+                                dS + (uint64_t)((s * 16384 + ks * 2048) >> 4), idS, ks > 0);
                     mma_commit(&ms.mma_s);
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks)
                         mma_f16(tm + kTcDvTile * (1 + s), dQ + so + (uint64_t)((((ks >> 2) * 8192) + (ks & 3) * 32) >> 4),
-                                dS + (uint64_t)((ks * 2048) >> 4), idO, ks > 0);
+                                dS + (uint64_t)((s * 16384 + ks * 2048) >> 4), idO, ks > 0);
                     mma_commit(&ms.mma_o[s]);
                     mma_commit(&ms.empty_mq[s]);
                 }
@@ -752,10 +753,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                 S[4 * q4 + 2] = d[4 * q4 + 2] + bb.z;
                 S[4 * q4 + 3] = d[4 * q4 + 3] + bb.w;
             }
-            if (c + 1 < p.NC) {
+            if (c + 1 < p.NC) {  // tile (c+1) % 2 was last read by chunk c-1's MMAs, all complete
 #pragma unroll
                 for (int q8 = 0; q8 < kTcDvTile / 8; ++q8)
-                    store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
+                    store_bf16x8(stile + (s ^ 1) * 16384, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
                 fence_proxy_async_smem();
             }
             tc_fence_before();
