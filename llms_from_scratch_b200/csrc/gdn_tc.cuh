@@ -85,14 +85,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
-// Waits for the phase of `bar` with parity `parity` to complete, for at most
-// `timeout_ns` of wall time; returns false if it gave up.
+// Waits for the phase of `bar` with parity `parity` to complete; gives up and
+// returns false after `timeout_ns` nanoseconds at 2 GHz worth of SM clock
+// cycles (the SM-local cycle counter is read, which is cheap; at lower clocks
+// the bound is proportionally longer in wall time, never shorter).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
+    const long long t0 = clock64();
+    const long long budget = (long long)(timeout_ns * 2);
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer_ns() - t0 > timeout_ns) return false;
+        if (clock64() - t0 > budget) return false;
     }
 }
 
