@@ -80,6 +80,12 @@ constexpr uint32_t P_T = 83200;        // fp32 [64][68]
 constexpr uint32_t P_Y3 = 100608;      // fp32 [3][16][16], scratch of the blocked inverse
 constexpr uint32_t P_SPLIT = 104448;   // [X;Z] and [Y;W] hi/lo A tiles (4 x 16 KiB), later PX/PY hi/lo B tiles
 constexpr uint32_t P_MISC = 169984;
+// Output staging in regions that are dead by then; each image leaves with one bulk copy.
+constexpr uint32_t P_STG_Q = P_L;           // Q' image (16 KiB), written in step 7 (L/Aqk/T are dead)
+constexpr uint32_t P_STG_O0 = P_L + 16384;  // o0 column tiles (32 KiB), step 7
+constexpr uint32_t P_STG_M = P_KQ;          // M image (32 KiB), step 9 (k^/q^ are dead after step 8)
+constexpr uint32_t P_STG_B = P_SPLIT;       // b column tiles (64 KiB), step 9 (P tiles are dead after step 8)
+static_assert(P_STG_O0 + 32768 <= P_SPLIT, "step-7 staging must not overlap the P tiles");
 constexpr uint32_t P_SMEM = P_MISC + 2048 + 1024;
 constexpr uint32_t kPrepTmemCols = 256;
 
@@ -459,7 +465,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
                 float o[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) o[e] = qs * __bfloat162float(qb[e]) - v[8 * q8 + e];
-                store_bf16x8(wrec + kTcQ, sw128_offset(i, d, 64), o);
+                store_bf16x8(sm + P_STG_Q, sw128_offset(i, d, 64), o);
             }
         }
         tmem_ld32(tmem_addr(tm, 32 * quad, 128 + 32 * cq), v);
@@ -469,7 +475,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
             for (int q8 = 0; q8 < 4; ++q8)
                 store_split8(sp + 32768, sp + 49152, sw128_offset(i, 32 * cq + 8 * q8, 64), v + 8 * q8);
         } else {  // o0 = Aqk u, fp32 column tile cq
-            unsigned char* blk = wrec + kTcO0 + cq * (64 * 128);
+            unsigned char* blk = sm + P_STG_O0 + cq * (64 * 128);
 #pragma unroll
             for (int q4 = 0; q4 < 8; ++q4)
                 *reinterpret_cast<float4*>(blk + f32blk_offset(i, q4)) =
@@ -482,6 +488,11 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (ok && tid == 32) {  // Q' and o0 leave while the tensor core works on step 8
+        bulk_s2g(wrec + kTcQ, sm + P_STG_Q, 16384);
+        bulk_s2g(wrec + kTcO0, sm + P_STG_O0, 32768);
+        bulk_commit();
+    }
 
     // ---- 8. M' = k^T P_X -> [0,128), b = k^T P_Y -> [128,256)  (M=128 over Dk, K = tokens)
     if (ok && tid == 0) {
@@ -517,11 +528,11 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
             float m[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) m[e] = ((col + e) == dk ? gamma : 0.f) - v[8 * q8 + e];
-            store_bf16x8(wrec + kTcM, sw128_offset(dk, col, 128), m);
+            store_bf16x8(sm + P_STG_M, sw128_offset(dk, col, 128), m);
         }
         tmem_ld32(tmem_addr(tm, 32 * quad, 128 + 32 * cq), v);
         tmem_ld_wait();
-        unsigned char* blk = wrec + kTcB + cq * (128 * 128);
+        unsigned char* blk = sm + P_STG_B + cq * (128 * 128);
 #pragma unroll
         for (int q4 = 0; q4 < 8; ++q4)
             *reinterpret_cast<float4*>(blk + f32blk_offset(dk, q4)) =
@@ -529,10 +540,20 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     } else {
         ok = false;
     }
-    if (!ok && tid == 0) report(p.err, kErrTimeoutPrep);
+    fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
+    if (tid == 32) {
+        if (ok) {
+            bulk_s2g(wrec + kTcM, sm + P_STG_M, 32768);
+            bulk_s2g(wrec + kTcB, sm + P_STG_B, 65536);
+            bulk_commit();
+        }
+        bulk_wait_read_all();  // shared memory must outlive every copy that reads it
+    }
+    if (!ok && tid == 0) report(p.err, kErrTimeoutPrep);
     if (warp == 0) tmem_dealloc(tm, kPrepTmemCols);
+    __syncthreads();
 }
 
 // ============================================================================ scan
