@@ -32,13 +32,14 @@ unsigned int* device_error_word(int dev) {
     return reinterpret_cast<unsigned int*>(g_device_error_addr[dev]);
 }
 
-// The tensor-core chunk path takes bf16 q/k/v/out whose rows are 8-byte (inputs)
-// and 16-byte (output) aligned; everything else runs on the CUDA-core path.
+// The tensor-core chunk path takes bf16 q/k/v/out whose rows are 16-byte aligned
+// (its 16-byte asynchronous row copies need that); everything else runs on the
+// CUDA-core path.
 bool tc_eligible(const gdn_tensor* q, const gdn_tensor* k, const gdn_tensor* v, const gdn_tensor* out) {
     const gdn_tensor* in[3] = {q, k, v};
     for (const gdn_tensor* t : in) {
         if (t->dtype != GDN_BF16) return false;
-        if ((reinterpret_cast<uintptr_t>(t->data) & 7) || (t->stride[0] & 3) || (t->stride[1] & 3) || (t->stride[2] & 3))
+        if ((reinterpret_cast<uintptr_t>(t->data) & 15) || (t->stride[0] & 7) || (t->stride[1] & 7) || (t->stride[2] & 7))
             return false;
     }
     if (out->dtype != GDN_BF16) return false;

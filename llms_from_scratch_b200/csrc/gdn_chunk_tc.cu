@@ -18,7 +18,9 @@
 // hi + lo pair of bf16 (two MMAs), so the prep is fp32-accurate.  The scan
 // feeds M_c, Q'_c and S_c to the MMA in bf16 and keeps S, b and o0 in fp32.
 //
-// gdn_prep_tc: one CTA (16 warps) per (batch, head, 64-token chunk).  Operands
+// gdn_prep_tc: persistent, one CTA (16 warps) per SM walking the (batch, head,
+// 64-token chunk) records; the next chunk's rows are prefetched with cp.async
+// and each output image leaves with an asynchronous bulk copy.  Operands
 // that share a B matrix are stacked into M=128 MMAs so every accumulator fills
 // all 128 TMEM lanes.
 //   1. rows of q, k, v -> l2norm (16-bit rounding as the reference) -> bf16
@@ -80,13 +82,14 @@ constexpr uint32_t P_T = 83200;        // fp32 [64][68]
 constexpr uint32_t P_Y3 = 100608;      // fp32 [3][16][16], scratch of the blocked inverse
 constexpr uint32_t P_SPLIT = 104448;   // [X;Z] and [Y;W] hi/lo A tiles (4 x 16 KiB), later PX/PY hi/lo B tiles
 constexpr uint32_t P_MISC = 169984;
+constexpr uint32_t P_RAW = 172032;     // raw bf16 rows [3][64][128] of the next chunk (cp.async prefetch, 48 KiB)
 // Output staging in regions that are dead by then; each image leaves with one bulk copy.
 constexpr uint32_t P_STG_Q = P_L;           // Q' image (16 KiB), written in step 7 (L/Aqk/T are dead)
 constexpr uint32_t P_STG_O0 = P_L + 16384;  // o0 column tiles (32 KiB), step 7
 constexpr uint32_t P_STG_M = P_KQ;          // M image (32 KiB), step 9 (k^/q^ are dead after step 8)
 constexpr uint32_t P_STG_B = P_SPLIT;       // b column tiles (64 KiB), step 9 (P tiles are dead after step 8)
 static_assert(P_STG_O0 + 32768 <= P_SPLIT, "step-7 staging must not overlap the P tiles");
-constexpr uint32_t P_SMEM = P_MISC + 2048 + 1024;
+constexpr uint32_t P_SMEM = P_RAW + 49152 + 1024;
 constexpr uint32_t kPrepTmemCols = 256;
 
 struct PrepMisc {
@@ -142,6 +145,35 @@ __device__ __forceinline__ uint32_t f32blk_offset(int row, int chunk4) {
     return (uint32_t)row * 128u + (uint32_t)((chunk4 ^ (row & 7)) * 16);
 }
 
+// Issue the row loads of `chunk` into the raw staging (q, k, v: [64 rows][128] bf16 each, rows
+// past T zero-filled) and load its g / beta into registers of threads 0-63.
+__device__ __forceinline__ void prep_prefetch(const ChunkParams& p, int64_t chunk, unsigned char* raw, int tid,
+                                              float& g_next, float& b_next) {
+    const int c = (int)(chunk % p.NC);
+    const int bh = (int)(chunk / p.NC);
+    const int b = bh / p.H, h = bh % p.H;
+    const int64_t t0 = (int64_t)c * kChunk;
+    for (int idx = tid; idx < 3 * kChunk * 16; idx += kPrepThreads) {
+        const int tsr = idx >> 10, r = (idx >> 4) & 63, j = idx & 15;
+        const View4& vw = tsr == 0 ? p.q : (tsr == 1 ? p.k : p.v);
+        const int64_t t = t0 + r;
+        const bool valid = t < p.T;
+        const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(vw.p);
+        const void* src = valid ? static_cast<const void*>(base + (int64_t)b * vw.sb + t * vw.st + (int64_t)h * vw.sh + 8 * j)
+                                : static_cast<const void*>(base);
+        cp_async16(raw + tsr * 16384 + r * 256 + j * 16, src, valid ? 16u : 0u);
+    }
+    cp_async_commit();
+    if (tid < kChunk) {
+        const int64_t t = t0 + tid;
+        g_next = b_next = 0.f;
+        if (t < p.T) {
+            g_next = load_elem(p.g.p, (int64_t)b * p.g.sb + t * p.g.st + (int64_t)h * p.g.sh, p.g.dtype);
+            b_next = load_elem(p.beta.p, (int64_t)b * p.beta.sb + t * p.beta.st + (int64_t)h * p.beta.sh, p.beta.dtype);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -153,57 +185,10 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int quad = warp & 3, cq = warp >> 2;  // TMEM lane quadrant, column quarter
-    const int64_t chunk = blockIdx.x;
-    const int c = (int)(chunk % p.NC);
-    const int bh = (int)(chunk / p.NC);
-    const int b = bh / p.H, h = bh % p.H;
-    const int64_t t0 = (int64_t)c * kChunk;
     const float scale = rsqrtf((float)kDk);
-    unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
+    const int64_t nchunks = (int64_t)p.B * p.H * p.NC;
+    unsigned char* raw = sm + P_RAW;
 
-    // ---- 1. normalised rows -> swizzled bf16 tiles (qwen3_5_transformers.py:122-137).
-    //      Each warp owns 4 rows; all 12 row loads are issued before the first reduction.
-    {
-        constexpr int kRows = kChunk / (kPrepThreads / 32);
-        float q[kRows][4], k[kRows][4], v[kRows][4];
-#pragma unroll
-        for (int rr = 0; rr < kRows; ++rr) {
-            const int64_t t = t0 + warp + 16 * rr;
-            if (t < p.T) {
-                load_bf16x4(p.q, b, t, h, lane, q[rr]);
-                load_bf16x4(p.k, b, t, h, lane, k[rr]);
-                load_bf16x4(p.v, b, t, h, lane, v[rr]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) q[rr][e] = k[rr][e] = v[rr][e] = 0.f;
-            }
-        }
-#pragma unroll
-        for (int rr = 0; rr < kRows; ++rr) {
-            const int r = warp + 16 * rr;
-            if (p.l2norm && t0 + r < p.T) {
-                const float iq = l2norm_inv(q[rr], GDN_BF16), ik = l2norm_inv(k[rr], GDN_BF16);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    q[rr][e] = round_to(q[rr][e] * iq, GDN_BF16);
-                    k[rr][e] = round_to(k[rr][e] * ik, GDN_BF16);
-                }
-            }
-            store_bf16x4(sm + P_KQ, sw128_offset(r, 4 * lane, 128), k[rr]);
-            store_bf16x4(sm + P_KQ, sw128_offset(64 + r, 4 * lane, 128), q[rr]);
-            store_bf16x4(sm + P_V, sw128_offset(r, 4 * lane, 64), v[rr]);
-        }
-    }
-    if (tid < kChunk) {
-        const int64_t t = t0 + tid;
-        float gv = 0.f, bv = 0.f;
-        if (t < p.T) {
-            gv = load_elem(p.g.p, (int64_t)b * p.g.sb + t * p.g.st + (int64_t)h * p.g.sh, p.g.dtype);
-            bv = load_elem(p.beta.p, (int64_t)b * p.beta.sb + t * p.beta.st + (int64_t)h * p.beta.sh, p.beta.dtype);
-        }
-        ms.gc[tid] = gv;
-        ms.beta[tid] = bv;
-    }
     if (warp == 0) {
         tmem_alloc(&ms.tmem, kPrepTmemCols);
         tmem_relinquish();
@@ -212,12 +197,68 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         mbar_init(&ms.bar, 1);
         fence_mbar_init();
     }
-    fence_proxy_async_smem();
+    float g_next = 0.f, b_next = 0.f;  // g / beta of the chunk whose rows are in flight (threads 0-63)
+    if ((int64_t)blockIdx.x < nchunks) prep_prefetch(p, blockIdx.x, raw, tid, g_next, b_next);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = ms.tmem;
     const uint32_t sbase = smem_u32(sm);
+    bool ok = true;
+    int it = 0;
+
+    // Persistent: one CTA per SM walks the chunks, the next chunk's rows landing while this one computes.
+    for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x, ++it) {
+    const int c = (int)(chunk % p.NC);
+    const int bh = (int)(chunk / p.NC);
+    const int b = bh / p.H, h = bh % p.H;
+    const int64_t t0 = (int64_t)c * kChunk;
+    unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
+    const uint32_t ph = (uint32_t)it & 1u;  // parity of this chunk's first of three barrier phases
+
+    // ---- 1. normalised rows -> swizzled bf16 tiles (qwen3_5_transformers.py:122-137).
+    //      The rows were prefetched; the previous chunk's Q'/o0/M copies must have left L and KQ.
+    cp_async_wait_all();
+    if (tid == 32) bulk_wait_read_keep1();
+    __syncthreads();
+    {
+        constexpr int kRows = kChunk / (kPrepThreads / 32);
+#pragma unroll
+        for (int rr = 0; rr < kRows; ++rr) {
+            const int r = warp + 16 * rr;
+            float q[4], k[4], v[4];
+            const uint2 qu = *reinterpret_cast<const uint2*>(raw + 0 * 16384 + r * 256 + 8 * lane);
+            const uint2 ku = *reinterpret_cast<const uint2*>(raw + 1 * 16384 + r * 256 + 8 * lane);
+            const uint2 vu = *reinterpret_cast<const uint2*>(raw + 2 * 16384 + r * 256 + 8 * lane);
+            const __nv_bfloat162* qb = reinterpret_cast<const __nv_bfloat162*>(&qu);
+            const __nv_bfloat162* kb = reinterpret_cast<const __nv_bfloat162*>(&ku);
+            const __nv_bfloat162* vb = reinterpret_cast<const __nv_bfloat162*>(&vu);
+            q[0] = __low2float(qb[0]); q[1] = __high2float(qb[0]); q[2] = __low2float(qb[1]); q[3] = __high2float(qb[1]);
+            k[0] = __low2float(kb[0]); k[1] = __high2float(kb[0]); k[2] = __low2float(kb[1]); k[3] = __high2float(kb[1]);
+            v[0] = __low2float(vb[0]); v[1] = __high2float(vb[0]); v[2] = __low2float(vb[1]); v[3] = __high2float(vb[1]);
+            if (p.l2norm && t0 + r < p.T) {
+                const float iq = l2norm_inv(q, GDN_BF16), ik = l2norm_inv(k, GDN_BF16);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    q[e] = round_to(q[e] * iq, GDN_BF16);
+                    k[e] = round_to(k[e] * ik, GDN_BF16);
+                }
+            }
+            store_bf16x4(sm + P_KQ, sw128_offset(r, 4 * lane, 128), k);
+            store_bf16x4(sm + P_KQ, sw128_offset(64 + r, 4 * lane, 128), q);
+            store_bf16x4(sm + P_V, sw128_offset(r, 4 * lane, 64), v);
+        }
+    }
+    if (tid < kChunk) {
+        ms.gc[tid] = g_next;
+        ms.beta[tid] = b_next;
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // the raw staging is consumed: pull in the chunk after this one
+    if (chunk + gridDim.x < nchunks) prep_prefetch(p, chunk + gridDim.x, raw, tid, g_next, b_next);
 
     // ---- 2. [k^; q^] k^T -> TMEM cols [0,64): lanes 0-63 G_k = k^ k^T, lanes 64-127 G_q = q^ k^T
     if (tid == 0) {
@@ -245,7 +286,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         ms.egc[tid] = __expf(ms.gc[tid]);
         ms.ekd[tid] = __expf(ms.gc[kChunk - 1] - ms.gc[tid]);
     }
-    bool ok = mbar_wait(&ms.bar, 0, kWaitNs);
+    ok = mbar_wait(&ms.bar, ph, kWaitNs);
     tc_fence_after();
 
     // ---- 3. L = -(beta_i G_k e^(gc_i-gc_j)) strictly lower (:152-153), Aqk = Dk^-1/2 G_q e^(gc_i-gc_j) causal (:172)
@@ -377,6 +418,9 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     }
     __syncthreads();
 
+    if (tid == 32) bulk_wait_read_all();  // the previous chunk's b copy has left P_SPLIT
+    __syncthreads();
+
     // ---- 5. the four 64x64 coefficient matrices, hi/lo bf16 A tiles [X;Z] and [Y;W]
     //      X = E_d T B_e, Y = E_d T B, W = (Aqk T) B, Z = (Aqk T) B_e
     if (ok) {
@@ -441,7 +485,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         }
         mma_commit(&ms.bar);
     }
-    if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);
+    if (ok) ok = mbar_wait(&ms.bar, ph ^ 1u, kWaitNs);
     tc_fence_after();
 
     // ---- 7. rows 0-63: P_X, P_Y -> hi/lo B tiles; rows 64-127: Q' and o0 -> workspace
@@ -512,7 +556,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         }
         mma_commit(&ms.bar);
     }
-    if (ok) ok = mbar_wait(&ms.bar, 0, kWaitNs);
+    if (ok) ok = mbar_wait(&ms.bar, ph, kWaitNs);
     tc_fence_after();
 
     // ---- 9. M = e^gc_last I - M' (bf16 image), b (fp32 column tiles)
@@ -543,17 +587,21 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
-    if (tid == 32) {
-        if (ok) {
-            bulk_s2g(wrec + kTcM, sm + P_STG_M, 32768);
-            bulk_s2g(wrec + kTcB, sm + P_STG_B, 65536);
-            bulk_commit();
-        }
-        bulk_wait_read_all();  // shared memory must outlive every copy that reads it
+    tc_fence_after();
+    if (tid == 32 && ok) {  // two groups: M (KQ region) then b (P_SPLIT region)
+        bulk_s2g(wrec + kTcM, sm + P_STG_M, 32768);
+        bulk_commit();
+        bulk_s2g(wrec + kTcB, sm + P_STG_B, 65536);
+        bulk_commit();
     }
+    if (!ok) break;
+    }  // chunk loop
+    if (tid == 32) bulk_wait_read_all();  // shared memory must outlive every copy that reads it
+    cp_async_wait_all();                 // and every prefetch that writes it
     if (!ok && tid == 0) report(p.err, kErrTimeoutPrep);
-    if (warp == 0) tmem_dealloc(tm, kPrepTmemCols);
+    tc_fence_before();
     __syncthreads();
+    if (warp == 0) tmem_dealloc(tm, kPrepTmemCols);
 }
 
 // ============================================================================ scan
@@ -820,8 +868,12 @@ cudaError_t launch_chunk_tc(const ChunkParams& p, cudaStream_t stream) {
     e = cudaFuncSetAttribute(gdn_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
     if (e != cudaSuccess) return e;
     const int64_t nchunks = (int64_t)p.B * p.H * p.NC;
+    int dev = 0, sms = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    const unsigned prep_grid = (unsigned)(nchunks < (int64_t)sms ? nchunks : (int64_t)sms);
     if ((e = phase_event(0, stream)) != cudaSuccess) return e;
-    gdn_prep_tc<<<(unsigned)nchunks, kPrepThreads, P_SMEM, stream>>>(p);
+    gdn_prep_tc<<<prep_grid, kPrepThreads, P_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     if ((e = phase_event(1, stream)) != cudaSuccess) return e;

@@ -136,6 +136,20 @@ __device__ __forceinline__ void bulk_wait_read_all() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
+// Wait until at most one committed bulk group of this thread is still reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_keep1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
+// 16-byte asynchronous global -> shared copy (cp.async); src_bytes = 0 zero-fills the destination.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+                 "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Hint: bring [gsrc, gsrc + bytes) into L2 (no shared-memory destination, no completion).
 __device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
