@@ -101,18 +101,6 @@ struct PrepMisc {
     uint32_t tmem;
 };
 
-__device__ __forceinline__ void load_bf16x4(const View4& v, int b, int64_t t, int h, int lane, float (&x)[4]) {
-    const __nv_bfloat16* p =
-        reinterpret_cast<const __nv_bfloat16*>(v.p) + (int64_t)b * v.sb + t * v.st + (int64_t)h * v.sh + 4 * lane;
-    const uint2 u = *reinterpret_cast<const uint2*>(p);
-    const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
-    const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
-    x[0] = __low2float(lo);
-    x[1] = __high2float(lo);
-    x[2] = __low2float(hi);
-    x[3] = __high2float(hi);
-}
-
 __device__ __forceinline__ void store_bf16x4(unsigned char* tile, uint32_t off, const float (&x)[4]) {
     uint2 u;
     u.x = pack_bf16x2(x[0], x[1]);
@@ -210,8 +198,6 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     // Persistent: one CTA per SM walks the chunks, the next chunk's rows landing while this one computes.
     for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x, ++it) {
     const int c = (int)(chunk % p.NC);
-    const int bh = (int)(chunk / p.NC);
-    const int b = bh / p.H, h = bh % p.H;
     const int64_t t0 = (int64_t)c * kChunk;
     unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
     const uint32_t ph = (uint32_t)it & 1u;  // parity of this chunk's first of three barrier phases
@@ -222,31 +208,59 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     if (tid == 32) bulk_wait_read_keep1();
     __syncthreads();
     {
+        // 8 sums of squares (q and k of 4 rows) reduced together: independent shuffle chains.
+        // The inverse norm uses rsqrtf: it is rounded to bf16 right away, so it differs from a
+        // correctly rounded 1/sqrt only when it lies within ~2 fp32 ulp of a bf16 rounding boundary
+        // (the reference's own CPU bf16 rsqrt is an estimate as well).
         constexpr int kRows = kChunk / (kPrepThreads / 32);
+        float q[kRows][4], k[kRows][4], v[kRows][4], ss[2 * kRows];
 #pragma unroll
         for (int rr = 0; rr < kRows; ++rr) {
             const int r = warp + 16 * rr;
-            float q[4], k[4], v[4];
             const uint2 qu = *reinterpret_cast<const uint2*>(raw + 0 * 16384 + r * 256 + 8 * lane);
             const uint2 ku = *reinterpret_cast<const uint2*>(raw + 1 * 16384 + r * 256 + 8 * lane);
             const uint2 vu = *reinterpret_cast<const uint2*>(raw + 2 * 16384 + r * 256 + 8 * lane);
             const __nv_bfloat162* qb = reinterpret_cast<const __nv_bfloat162*>(&qu);
             const __nv_bfloat162* kb = reinterpret_cast<const __nv_bfloat162*>(&ku);
             const __nv_bfloat162* vb = reinterpret_cast<const __nv_bfloat162*>(&vu);
-            q[0] = __low2float(qb[0]); q[1] = __high2float(qb[0]); q[2] = __low2float(qb[1]); q[3] = __high2float(qb[1]);
-            k[0] = __low2float(kb[0]); k[1] = __high2float(kb[0]); k[2] = __low2float(kb[1]); k[3] = __high2float(kb[1]);
-            v[0] = __low2float(vb[0]); v[1] = __high2float(vb[0]); v[2] = __low2float(vb[1]); v[3] = __high2float(vb[1]);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                q[rr][2 * e] = __low2float(qb[e]);
+                q[rr][2 * e + 1] = __high2float(qb[e]);
+                k[rr][2 * e] = __low2float(kb[e]);
+                k[rr][2 * e + 1] = __high2float(kb[e]);
+                v[rr][2 * e] = __low2float(vb[e]);
+                v[rr][2 * e + 1] = __high2float(vb[e]);
+            }
+            float sq = 0.f, sk = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {  // x*x rounded in bf16, summed in fp32 (qwen3_5_transformers.py:106)
+                sq += round_to(q[rr][e] * q[rr][e], GDN_BF16);
+                sk += round_to(k[rr][e] * k[rr][e], GDN_BF16);
+            }
+            ss[2 * rr] = sq;
+            ss[2 * rr + 1] = sk;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int i = 0; i < 2 * kRows; ++i) ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], o);
+        }
+#pragma unroll
+        for (int rr = 0; rr < kRows; ++rr) {
+            const int r = warp + 16 * rr;
             if (p.l2norm && t0 + r < p.T) {
-                const float iq = l2norm_inv(q, GDN_BF16), ik = l2norm_inv(k, GDN_BF16);
+                const float iq = round_to(rsqrtf(round_to(round_to(ss[2 * rr], GDN_BF16) + 1e-6f, GDN_BF16)), GDN_BF16);
+                const float ik = round_to(rsqrtf(round_to(round_to(ss[2 * rr + 1], GDN_BF16) + 1e-6f, GDN_BF16)), GDN_BF16);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    q[e] = round_to(q[e] * iq, GDN_BF16);
-                    k[e] = round_to(k[e] * ik, GDN_BF16);
+                    q[rr][e] = round_to(q[rr][e] * iq, GDN_BF16);
+                    k[rr][e] = round_to(k[rr][e] * ik, GDN_BF16);
                 }
             }
-            store_bf16x4(sm + P_KQ, sw128_offset(r, 4 * lane, 128), k);
-            store_bf16x4(sm + P_KQ, sw128_offset(64 + r, 4 * lane, 128), q);
-            store_bf16x4(sm + P_V, sw128_offset(r, 4 * lane, 64), v);
+            store_bf16x4(sm + P_KQ, sw128_offset(r, 4 * lane, 128), k[rr]);
+            store_bf16x4(sm + P_KQ, sw128_offset(64 + r, 4 * lane, 128), q[rr]);
+            store_bf16x4(sm + P_V, sw128_offset(r, 4 * lane, 64), v[rr]);
         }
     }
     if (tid < kChunk) {
