@@ -58,14 +58,14 @@ __device__ __forceinline__ void report(unsigned int* err, unsigned int bit) {
     if (err) atomicOr(err, bit);
 }
 
-// Two fp32 values -> packed bf16x2 (a in the low half), round to nearest even.
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-    return __byte_perm(bf16_round_bits(a), bf16_round_bits(b), 0x7632);
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 // bf16 hi/lo split: x ~= hi + lo with |x - hi - lo| <= 2^-16 |x|.
 __device__ __forceinline__ void split_bf16(float x, float& hi, float& lo) {
-    hi = __uint_as_float(bf16_round_bits(x));
+    hi = __bfloat162float(__float2bfloat16_rn(x));
     lo = x - hi;
 }
 

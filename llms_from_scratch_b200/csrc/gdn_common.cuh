@@ -38,18 +38,10 @@ __device__ __forceinline__ void store_elem(void* base, int64_t idx, int dtype, f
     else reinterpret_cast<float*>(base)[idx] = x;
 }
 
-// fp32 -> bf16 round-to-nearest-even with integer ops (full-rate ALU instead of the
-// conversion pipe); the upper 16 bits of the result are the bf16 bit pattern.
-// Same result as cvt.rn.bf16.f32 for every finite input and for +-inf.
-__device__ __forceinline__ uint32_t bf16_round_bits(float x) {
-    const uint32_t u = __float_as_uint(x);
-    return (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
-}
-
 // Round an fp32 value to `dtype` and back (identity for fp32): reproduces the
 // roundings a torch op in that dtype would do.
 __device__ __forceinline__ float round_to(float x, int dtype) {
-    if (dtype == GDN_BF16) return __uint_as_float(bf16_round_bits(x));
+    if (dtype == GDN_BF16) return __bfloat162float(__float2bfloat16_rn(x));
     if (dtype == GDN_F16) return __half2float(__float2half_rn(x));
     return x;
 }
