@@ -104,6 +104,29 @@ GDN_API int gdn_chunk_gated_delta_rule_noalloc(const gdn_tensor* query, const gd
                                                int use_qk_l2norm_in_kernel, gdn_tensor* out,
                                                float* final_state, void* stream);
 
+/* Sequence parallelism: one long sequence split into contiguous time shards,
+ * one shard per GPU.  No counterpart in the reference, which runs the chunk
+ * loop on one device (qwen3_5_cutedsl_kernels.py:427-453); these two calls are
+ * the per-shard halves of gdn_chunk_gated_delta_rule.
+ *
+ * The state at the end of a shard is an affine map of the state at its start,
+ * S_end = transition @ S_start + local_state (transition [B,H,Dk,Dk], local_state
+ * [B,H,Dk,Dv], fp32).  gdn_chunk_sp_summary computes both for this shard and
+ * leaves its chunk records in `workspace`; after the shards' summaries are
+ * exchanged and composed into this shard's start state, gdn_chunk_sp_finish
+ * (same inputs, same untouched workspace) writes the shard's outputs and its
+ * end state.  bf16 q/k/v/out with 16-byte aligned rows only (GDN_ERR_UNSUPPORTED
+ * otherwise); T > 0. */
+GDN_API int gdn_chunk_sp_summary(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
+                                 const gdn_tensor* g, const gdn_tensor* beta, int chunk_size,
+                                 int use_qk_l2norm_in_kernel, float* transition, float* local_state,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+GDN_API int gdn_chunk_sp_finish(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
+                                const gdn_tensor* g, const gdn_tensor* beta, int chunk_size,
+                                const float* initial_state, int output_final_state, int use_qk_l2norm_in_kernel,
+                                gdn_tensor* out, float* final_state, const void* workspace, size_t workspace_bytes,
+                                void* stream);
+
 /* Token-by-token recurrent rule (decode step when T == 1).
  *
  * Replaces torch_recurrent_gated_delta_rule(query, key, value, g, beta,

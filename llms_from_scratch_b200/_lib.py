@@ -47,6 +47,10 @@ SIGNATURES = {
     "gdn_chunk_gated_delta_rule_noalloc": (c_int, [_P, _P, _P, _P, _P, c_int, c_void_p, c_int, c_int, _P,
                                                    c_void_p, c_void_p]),
     "gdn_recurrent_gated_delta_rule": (c_int, [_P, _P, _P, _P, _P, c_void_p, c_int, c_int, _P, c_void_p, c_void_p]),
+    "gdn_chunk_sp_summary": (c_int, [_P, _P, _P, _P, _P, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t,
+                                     c_void_p]),
+    "gdn_chunk_sp_finish": (c_int, [_P, _P, _P, _P, _P, c_int, c_void_p, c_int, c_int, _P, c_void_p, c_void_p,
+                                    c_size_t, c_void_p]),
     "gdn_launch_count": (ctypes.c_uint64, []),
     "gdn_set_phase_events": (None, [ctypes.POINTER(c_void_p), c_int]),
     "gdn_device_error": (ctypes.c_uint, [c_int]),

@@ -290,6 +290,99 @@ int gdn_recurrent_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* ke
     return e == cudaSuccess ? GDN_OK : cuda_fail(e, "recurrent kernel launch");
 }
 
+// ---------------------------------------------------------------- sequence parallelism
+
+namespace {
+
+// Validates a time shard for the sequence-parallel calls and fills the shared kernel parameters.
+int sp_params(const gdn_tensor* q, const gdn_tensor* k, const gdn_tensor* v, const gdn_tensor* g,
+              const gdn_tensor* beta, int chunk_size, int use_qk_l2norm, const gdn_tensor* out, const void* ws,
+              size_t ws_bytes, gdn::ChunkParams* p) {
+    if (chunk_size != gdn::kChunk)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "chunk_size must be %d, got %d", gdn::kChunk, chunk_size);
+    if (!q || q->ndim != 4) return fail(GDN_ERR_INVALID_ARGUMENT, "query must be 4-D [B,T,H,Dk]");
+    const int64_t B = q->shape[0], T = q->shape[1], H = q->shape[2];
+    if (B <= 0 || T <= 0 || H <= 0) return fail(GDN_ERR_INVALID_ARGUMENT, "a time shard needs B, T, H > 0");
+    int rc;
+    if ((rc = check4("query", q, B, T, H, gdn::kDk))) return rc;
+    if ((rc = check4("key", k, B, T, H, gdn::kDk))) return rc;
+    if ((rc = check4("value", v, B, T, H, gdn::kDv))) return rc;
+    if ((rc = check3("g", g, B, T, H))) return rc;
+    if ((rc = check3("beta", beta, B, T, H))) return rc;
+    if (out && (rc = check4("out", out, B, T, H, gdn::kDv))) return rc;
+    if (!tc_eligible(q, k, v, out ? out : v))
+        return fail(GDN_ERR_UNSUPPORTED, "sequence-parallel shards need bf16 q/k/v%s with 16-byte aligned rows",
+                    out ? "/out" : "");
+    if ((rc = check_device())) return rc;
+    const size_t need = gdn_chunk_workspace_bytes(B, T, H, gdn::kDk, gdn::kDv, q->dtype);
+    if (!ws || ws_bytes < need)
+        return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, ws ? ws_bytes : 0);
+    if (reinterpret_cast<uintptr_t>(ws) & 255) return fail(GDN_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    *p = gdn::ChunkParams{};
+    p->q = view4(q);
+    p->k = view4(k);
+    p->v = view4(v);
+    p->g = view3(g);
+    p->beta = view3(beta);
+    p->ws = reinterpret_cast<float*>(const_cast<void*>(ws));
+    p->B = (int)B;
+    p->H = (int)H;
+    p->T = T;
+    p->NC = (int)((T + gdn::kChunk - 1) / gdn::kChunk);
+    p->l2norm = use_qk_l2norm ? 1 : 0;
+    p->err = device_error_word(dev);
+    return GDN_OK;
+}
+
+}  // namespace
+
+int gdn_chunk_sp_summary(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value, const gdn_tensor* g,
+                         const gdn_tensor* beta, int chunk_size, int use_qk_l2norm_in_kernel, float* transition,
+                         float* local_state, void* workspace, size_t workspace_bytes, void* stream) {
+    g_last_error.clear();
+    gdn::ChunkParams p;
+    int rc = sp_params(query, key, value, g, beta, chunk_size, use_qk_l2norm_in_kernel, nullptr, workspace,
+                       workspace_bytes, &p);
+    if (rc) return rc;
+    if (!transition || !local_state || (reinterpret_cast<uintptr_t>(transition) & 15) ||
+        (reinterpret_cast<uintptr_t>(local_state) & 15))
+        return fail(GDN_ERR_INVALID_ARGUMENT, "transition and local_state must be 16-byte aligned fp32 buffers");
+    p.scan_mode = 1;
+    p.hT = transition;
+    p.hT2 = local_state;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = gdn::launch_chunk_tc_prep(p, st);
+    if (e == cudaSuccess) e = gdn::launch_chunk_tc_scan(p, st);
+    return e == cudaSuccess ? GDN_OK : cuda_fail(e, "shard summary launch");
+}
+
+int gdn_chunk_sp_finish(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value, const gdn_tensor* g,
+                        const gdn_tensor* beta, int chunk_size, const float* initial_state, int output_final_state,
+                        int use_qk_l2norm_in_kernel, gdn_tensor* out, float* final_state, const void* workspace,
+                        size_t workspace_bytes, void* stream) {
+    g_last_error.clear();
+    if (!out) return fail(GDN_ERR_INVALID_ARGUMENT, "out is NULL");
+    gdn::ChunkParams p;
+    int rc = sp_params(query, key, value, g, beta, chunk_size, use_qk_l2norm_in_kernel, out, workspace,
+                       workspace_bytes, &p);
+    if (rc) return rc;
+    if (initial_state && (reinterpret_cast<uintptr_t>(initial_state) & 15))
+        return fail(GDN_ERR_INVALID_ARGUMENT, "initial_state must be 16-byte aligned");
+    if (output_final_state && (!final_state || (reinterpret_cast<uintptr_t>(final_state) & 15)))
+        return fail(GDN_ERR_INVALID_ARGUMENT, "final_state must be a 16-byte aligned fp32 buffer");
+    p.out = out->data;
+    p.out_sb = out->stride[0];
+    p.out_st = out->stride[1];
+    p.out_sh = out->stride[2];
+    p.out_dtype = out->dtype;
+    p.h0 = initial_state;
+    p.hT = output_final_state ? final_state : nullptr;
+    cudaError_t e = gdn::launch_chunk_tc_scan(p, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? GDN_OK : cuda_fail(e, "shard finish launch");
+}
+
 unsigned int gdn_device_error(int clear) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;

@@ -687,7 +687,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bh = blockIdx.x;
     const int b = bh / p.H, h = bh % p.H;
-    const int dvt = blockIdx.y;
+    const int dvt = blockIdx.y & 3;  // 32-column slice of the state (and of b / o0)
+    const bool summary = p.scan_mode == 1;
+    const bool transition = summary && blockIdx.y < 4;  // state starts from I, b ignored
     const int dv0 = dvt * kTcDvTile;
     const unsigned char* wbase = reinterpret_cast<const unsigned char*>(p.ws) + (int64_t)bh * p.NC * kTcChunkBytes;
 
@@ -759,7 +761,14 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
         const int64_t srow = ((int64_t)bh * kDk + dk) * kDv + dv0;
 #pragma unroll
         for (int q4 = 0; q4 < kTcDvTile / 4; ++q4) {
-            const float4 v = p.h0 ? *reinterpret_cast<const float4*>(p.h0 + srow + 4 * q4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 v = (p.h0 && !summary) ? *reinterpret_cast<const float4*>(p.h0 + srow + 4 * q4)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (transition) {  // identity columns dv0 .. dv0+31
+                v.x = (dk == dv0 + 4 * q4) ? 1.f : 0.f;
+                v.y = (dk == dv0 + 4 * q4 + 1) ? 1.f : 0.f;
+                v.z = (dk == dv0 + 4 * q4 + 2) ? 1.f : 0.f;
+                v.w = (dk == dv0 + 4 * q4 + 3) ? 1.f : 0.f;
+            }
             S[4 * q4] = v.x;
             S[4 * q4 + 1] = v.y;
             S[4 * q4 + 2] = v.z;
@@ -815,7 +824,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                 float o[32];
                 tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + sp)), o);
                 tmem_ld_wait();
-                scan_store_output(p, sm + sp * S_STAGE, o, c - 1, warp, lane, b, h, dv0);
+                if (!summary) scan_store_output(p, sm + sp * S_STAGE, o, c - 1, warp, lane, b, h, dv0);
                 mbar_arrive(&ms.empty_bo[sp]);
             }
             if (!mbar_wait(&ms.mma_s, c & 1, kWaitNs) || !mbar_wait(&ms.full_bo[s], (c >> 1) & 1, kWaitNs)) {
@@ -830,7 +839,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             // S_{c+1} = M_c S_c + b_c
 #pragma unroll
             for (int q4 = 0; q4 < 8; ++q4) {
-                const float4 bb = *reinterpret_cast<const float4*>(st + S_OFF_B + f32blk_offset(dk, q4));
+                float4 bb = *reinterpret_cast<const float4*>(st + S_OFF_B + f32blk_offset(dk, q4));
+                if (transition) bb = make_float4(0.f, 0.f, 0.f, 0.f);
                 S[4 * q4] = d[4 * q4] + bb.x;
                 S[4 * q4 + 1] = d[4 * q4 + 1] + bb.y;
                 S[4 * q4 + 2] = d[4 * q4 + 2] + bb.z;
@@ -851,15 +861,16 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                 float o[32];
                 tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + sp)), o);
                 tmem_ld_wait();
-                scan_store_output(p, sm + sp * S_STAGE, o, p.NC - 1, warp, lane, b, h, dv0);
+                if (!summary) scan_store_output(p, sm + sp * S_STAGE, o, p.NC - 1, warp, lane, b, h, dv0);
                 mbar_arrive(&ms.empty_bo[sp]);
             } else {
                 ok = false;
             }
-            if (ok && p.hT) {
+            float* dst = summary ? (transition ? p.hT : p.hT2) : p.hT;
+            if (ok && dst) {
 #pragma unroll
                 for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
-                    *reinterpret_cast<float4*>(p.hT + srow + 4 * q4) =
+                    *reinterpret_cast<float4*>(dst + srow + 4 * q4) =
                         make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
             }
         }
@@ -875,26 +886,37 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
 
 }  // namespace
 
-cudaError_t launch_chunk_tc(const ChunkParams& p, cudaStream_t stream) {
+cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream) {
     static_assert(P_SMEM <= 227 * 1024 && S_SMEM <= 227 * 1024, "shared memory budget");
     cudaError_t e = cudaFuncSetAttribute(gdn_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(gdn_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
     if (e != cudaSuccess) return e;
     const int64_t nchunks = (int64_t)p.B * p.H * p.NC;
     int dev = 0, sms = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
     const unsigned prep_grid = (unsigned)(nchunks < (int64_t)sms ? nchunks : (int64_t)sms);
-    if ((e = phase_event(0, stream)) != cudaSuccess) return e;
     gdn_prep_tc<<<prep_grid, kPrepThreads, P_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
-    if ((e = phase_event(1, stream)) != cudaSuccess) return e;
-    dim3 grid((unsigned)(p.B * p.H), kDv / kTcDvTile);
+    return cudaSuccess;
+}
+
+cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
+    cudaError_t e = cudaFuncSetAttribute(gdn_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)(p.B * p.H), (p.scan_mode == 1 ? 2 : 1) * (kDv / kTcDvTile));
     gdn_scan_tc<<<grid, kScanThreads, S_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
+    return cudaSuccess;
+}
+
+cudaError_t launch_chunk_tc(const ChunkParams& p, cudaStream_t stream) {
+    cudaError_t e;
+    if ((e = phase_event(0, stream)) != cudaSuccess) return e;
+    if ((e = launch_chunk_tc_prep(p, stream)) != cudaSuccess) return e;
+    if ((e = phase_event(1, stream)) != cudaSuccess) return e;
+    if ((e = launch_chunk_tc_scan(p, stream)) != cudaSuccess) return e;
     return phase_event(2, stream);
 }
 

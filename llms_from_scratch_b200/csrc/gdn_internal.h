@@ -40,6 +40,11 @@ struct ChunkParams {
     int64_t T;
     int l2norm;
     unsigned int* err;  // device error word (bounded waits that gave up set bits here)
+    // Tensor-core scan mode: 0 = outputs + final state; 1 = shard summary (no outputs):
+    // column slices 0-3 of grid.y write the transition prod_c M_c to hT (state started
+    // from I, b ignored), slices 4-7 the local final state (state started from 0) to hT2.
+    int scan_mode;
+    float* hT2;
 };
 
 struct RecurrentParams {
@@ -68,6 +73,10 @@ enum : unsigned int { kErrTimeoutPrep = 1u, kErrTimeoutScan = 2u };
 
 cudaError_t launch_chunk_simt(const ChunkParams& p, cudaStream_t stream);
 cudaError_t launch_chunk_tc(const ChunkParams& p, cudaStream_t stream);
+// The two halves of the tensor-core path: prep fills the workspace records; scan reads them
+// (in p.scan_mode) -- the sequence-parallel entry points run them separately.
+cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream);
+cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream);
 cudaError_t launch_recurrent(const RecurrentParams& p, cudaStream_t stream);
 
 }  // namespace gdn
