@@ -53,6 +53,9 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--soak-seconds", type=float, default=1.0, help="untimed load before timing (clock sampling)")
+    ap.add_argument("--sp", action="store_true",
+                    help="config 5: one sequence of --sp-T tokens (B=1) split in time across the ranks")
+    ap.add_argument("--sp-T", type=int, default=131072)
     return ap.parse_args()
 
 
@@ -220,11 +223,81 @@ def run_reference(args, rank, world):
 
 # --------------------------------------------------------------------------- GPU arm
 
+def run_sequence_parallel(args, rank, world, local):
+    """Config 5: B=1, one sequence of args.sp_T tokens, contiguous time shards, one per rank
+    (strong scaling).  A step = shard summary + all_gather of (transition, local state) +
+    start-state composition + shard finish; device time, max over ranks."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from llms_from_scratch_b200.parallel import chunk_shard_finish, chunk_shard_summary, compose_start_states
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    T, H = args.sp_T, args.H
+    lo, hi = T * rank // world, T * (rank + 1) // world
+    q, k, v, g, beta, s0 = make_inputs(torch, 1, hi - lo, H, seed=77 + rank, device=device)
+    from llms_from_scratch_b200 import _lib
+    ws = torch.empty(_lib.load().gdn_chunk_workspace_bytes(1, hi - lo, H, D, D, _lib.GDN_BF16), dtype=torch.uint8,
+                     device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def step():
+        M, b, _ = chunk_shard_summary(q, k, v, g, beta, True, ws)
+        packed = torch.stack([M, b])
+        if world > 1:
+            gathered = [torch.empty_like(packed) for _ in range(world)]
+            dist.all_gather(gathered, packed)
+        else:
+            gathered = [packed]
+        start = s0 if rank == 0 else compose_start_states([x[0] for x in gathered[:rank]],
+                                                           [x[1] for x in gathered[:rank]], s0)[rank]
+        return chunk_shard_finish(q, k, v, g, beta, start, True, True, ws)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        evs[i][0].record()
+        step()
+        evs[i][1].record()
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b_) for a, b_ in evs)
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank == 0:
+        print(json.dumps({
+            "metric": "GDN chunk-fwd tok/s, sequence parallel @B=1,T=%d" % T, "value": T / (ms / 1e3),
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"gdn_chunk_fwd B=1 T={T} H={H} time-sharded x{world} (summary + all_gather + "
+                                   "compose + finish)", "global_batch": 1, "seq_len": T,
+                       "parallelism": f"sequence-parallel x{world}", "l2": "256 MiB buffer written between steps"},
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.sp:
+        run_sequence_parallel(args, rank, world, local)
         return
 
     import torch
