@@ -18,11 +18,11 @@
 // hi + lo pair of bf16 (two MMAs), so the prep is fp32-accurate.  The scan
 // feeds M_c, Q'_c and S_c to the MMA in bf16 and keeps S, b and o0 in fp32.
 //
-// gdn_prep_tc: persistent, one CTA (16 warps) per SM walking the (batch, head,
-// 64-token chunk) records; the next chunk's rows are prefetched with cp.async
-// and each output image leaves with an asynchronous bulk copy.  Operands
-// that share a B matrix are stacked into M=128 MMAs so every accumulator fills
-// all 128 TMEM lanes.
+// gdn_prep_tc: one CTA (8 warps) per (batch, head, 64-token chunk), two CTAs per
+// SM (105 KB of shared memory each, one work region reused phase by phase), so
+// one CTA's memory and barrier waits overlap the other's work; the output images
+// leave with asynchronous bulk copies.  Operands that share a B matrix are
+// stacked into M=128 MMAs so every accumulator fills all 128 TMEM lanes.
 //   1. rows of q, k, v -> l2norm (16-bit rounding as the reference) -> bf16
 //      128B-swizzled tiles [k^; q^] and v in shared memory
 //   2. [k^; q^] k^T on the tensor cores -> G_k (lanes 0-63) and G_q (64-127)
@@ -30,7 +30,7 @@
 //   4. T = (I - L)^-1 in 16x16 blocks (diagonal blocks by substitution, then
 //      the off-diagonal blocks by distance)
 //   5. X = E_d T B_e, Y = E_d T B, W = Aqk T B, Z = Aqk T B_e  (64x64, fp32)
-//   6. [X; Z] k^ -> P_X | Zk and [Y; W] v -> P_Y | o0  (M=128, N=128, K=64, hi+lo)
+//   6. [X; Z] k^ -> P_X | Zk, then [Y; W] v -> P_Y | o0  (M=128, N=128, K=64, hi+lo)
 //   7. Q' = q^ e^gc Dk^-1/2 - Zk, o0 -> workspace; P_X, P_Y -> hi+lo B tiles
 //   8. M' = k^T P_X, b = k^T P_Y (M=128, N=128, K=64, hi+lo)
 //   9. M = e^gc_last I - M', b -> workspace
@@ -71,26 +71,25 @@ __device__ __forceinline__ void split_bf16(float x, float& hi, float& lo) {
 
 // ============================================================================ prep
 
-constexpr int kPrepThreads = 512;
-constexpr uint32_t P_KQ = 0;           // bf16 [128 rows][128] swizzled: rows 0-63 k^, 64-127 q^ (atom columns 16 KiB apart)
-constexpr uint32_t P_V = 32768;        // bf16 [64 rows][128] swizzled v (atom columns 8 KiB apart)
-constexpr int kLd = 68;                // fp32 row stride of L and T (16-byte rows)
-constexpr int kAqkLd = 65;             // Aqk is only accessed as scalars: odd stride
-constexpr uint32_t P_L = 49152;        // fp32 [64][68]
-constexpr uint32_t P_AQK = 66560;      // fp32 [64][65]
-constexpr uint32_t P_T = 83200;        // fp32 [64][68]
-constexpr uint32_t P_Y3 = 100608;      // fp32 [3][16][16], scratch of the blocked inverse
-constexpr uint32_t P_SPLIT = 104448;   // [X;Z] and [Y;W] hi/lo A tiles (4 x 16 KiB), later PX/PY hi/lo B tiles
-constexpr uint32_t P_MISC = 169984;
-constexpr uint32_t P_RAW = 172032;     // raw bf16 rows [3][64][128] of the next chunk (cp.async prefetch, 48 KiB)
-// Output staging in regions that are dead by then; each image leaves with one bulk copy.
-constexpr uint32_t P_STG_Q = P_L;           // Q' image (16 KiB), written in step 7 (L/Aqk/T are dead)
-constexpr uint32_t P_STG_O0 = P_L + 16384;  // o0 column tiles (32 KiB), step 7
-constexpr uint32_t P_STG_M = P_KQ;          // M image (32 KiB), step 9 (k^/q^ are dead after step 8)
-constexpr uint32_t P_STG_B = P_SPLIT;       // b column tiles (64 KiB), step 9 (P tiles are dead after step 8)
-static_assert(P_STG_O0 + 32768 <= P_SPLIT, "step-7 staging must not overlap the P tiles");
-constexpr uint32_t P_SMEM = P_RAW + 49152 + 1024;
+constexpr int kPrepThreads = 256;          // 8 warps; two CTAs share an SM
+constexpr uint32_t P_KQ = 0;               // bf16 [128 rows][128] swizzled: rows 0-63 k^, 64-127 q^ (atom columns 16 KiB apart)
+constexpr uint32_t P_V = 32768;            // bf16 [64 rows][128] swizzled v (atom columns 8 KiB apart)
+constexpr uint32_t P_W = 49152;            // work region, reused phase by phase:
+constexpr int kLd = 68;                    //   fp32 row stride of T (16-byte rows for float4 reads)
+constexpr int kSLd = 65;                   //   odd stride of L and Aqk (scalar access only)
+constexpr uint32_t P_L = P_W;              //   steps 3-4: L   fp32 [64][65]
+constexpr uint32_t P_AQK = P_W + 16640;    //   steps 3-5: Aqk fp32 [64][65]
+constexpr uint32_t P_T = P_W + 33280;      //   steps 4-5: T   fp32 [64][68]
+constexpr uint32_t P_Y3 = P_W + 50688;     //   step 4: fp32 [3][16][16] scratch of the blocked inverse
+constexpr uint32_t P_ATILE = P_W;          //   step 6: [X;Z] then [Y;W] hi/lo A tiles (2 x 16 KiB)
+constexpr uint32_t P_PX = P_W;             //   steps 7-8: P_X hi/lo B tiles (2 x 16 KiB)
+constexpr uint32_t P_PYH = P_V;            //   steps 7-8: P_Y hi (v is dead after step 6)
+constexpr uint32_t P_PYL = P_W + 32768;    //   steps 7-8: P_Y lo
+constexpr uint32_t P_MISC = P_W + 53760;
+constexpr uint32_t P_SMEM = P_MISC + 1088 + 1024;  // + alignment slack
 constexpr uint32_t kPrepTmemCols = 256;
+static_assert(P_Y3 + 3072 <= P_MISC, "work region");
+static_assert(P_PYL + 16384 <= P_MISC, "work region");
 
 struct PrepMisc {
     float gc[64];
@@ -133,49 +132,48 @@ __device__ __forceinline__ uint32_t f32blk_offset(int row, int chunk4) {
     return (uint32_t)row * 128u + (uint32_t)((chunk4 ^ (row & 7)) * 16);
 }
 
-// Issue the row loads of `chunk` into the raw staging (q, k, v: [64 rows][128] bf16 each, rows
-// past T zero-filled) and load its g / beta into registers of threads 0-63.
-__device__ __forceinline__ void prep_prefetch(const ChunkParams& p, int64_t chunk, unsigned char* raw, int tid,
-                                              float& g_next, float& b_next) {
-    const int c = (int)(chunk % p.NC);
-    const int bh = (int)(chunk / p.NC);
-    const int b = bh / p.H, h = bh % p.H;
-    const int64_t t0 = (int64_t)c * kChunk;
-    for (int idx = tid; idx < 3 * kChunk * 16; idx += kPrepThreads) {
-        const int tsr = idx >> 10, r = (idx >> 4) & 63, j = idx & 15;
-        const View4& vw = tsr == 0 ? p.q : (tsr == 1 ? p.k : p.v);
-        const int64_t t = t0 + r;
-        const bool valid = t < p.T;
-        const __nv_bfloat16* base = reinterpret_cast<const __nv_bfloat16*>(vw.p);
-        const void* src = valid ? static_cast<const void*>(base + (int64_t)b * vw.sb + t * vw.st + (int64_t)h * vw.sh + 8 * j)
-                                : static_cast<const void*>(base);
-        cp_async16(raw + tsr * 16384 + r * 256 + j * 16, src, valid ? 16u : 0u);
-    }
-    cp_async_commit();
-    if (tid < kChunk) {
-        const int64_t t = t0 + tid;
-        g_next = b_next = 0.f;
-        if (t < p.T) {
-            g_next = load_elem(p.g.p, (int64_t)b * p.g.sb + t * p.g.st + (int64_t)h * p.g.sh, p.g.dtype);
-            b_next = load_elem(p.beta.p, (int64_t)b * p.beta.sb + t * p.beta.st + (int64_t)h * p.beta.sh, p.beta.dtype);
-        }
-    }
+__device__ __forceinline__ void load_bf16x4(const View4& v, int b, int64_t t, int h, int lane, float (&x)[4]) {
+    const __nv_bfloat16* p =
+        reinterpret_cast<const __nv_bfloat16*>(v.p) + (int64_t)b * v.sb + t * v.st + (int64_t)h * v.sh + 4 * lane;
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+    const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+    x[0] = __low2float(lo);
+    x[1] = __high2float(lo);
+    x[2] = __low2float(hi);
+    x[3] = __high2float(hi);
 }
 
-__global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
+// One M=128, N=128, K=64 product accumulated from the hi and lo halves of a K-major A tile
+// (single atom column, 128 rows) against an MN-major B tile (rows = the 64 tokens).
+__device__ __forceinline__ void mma_split_a(uint32_t d_tmem, uint32_t a_hi, uint32_t a_lo, uint32_t b_tile,
+                                            uint32_t b_lbo, uint32_t idesc) {
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+            mma_f16(d_tmem, make_sdesc((s2 ? a_lo : a_hi) + ks * 32, 16, 1024, kSwizzle128B),
+                    make_sdesc(b_tile + ks * 2048, b_lbo, 1024, kSwizzle128B), idesc, (s2 | ks) != 0);
+}
+
+__global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     PrepMisc& ms = *reinterpret_cast<PrepMisc*>(sm + P_MISC);
-    float(*sL)[kLd] = reinterpret_cast<float(*)[kLd]>(sm + P_L);
-    float(*sA)[kAqkLd] = reinterpret_cast<float(*)[kAqkLd]>(sm + P_AQK);
+    float(*sL)[kSLd] = reinterpret_cast<float(*)[kSLd]>(sm + P_L);
+    float(*sA)[kSLd] = reinterpret_cast<float(*)[kSLd]>(sm + P_AQK);
     float(*sT)[kLd] = reinterpret_cast<float(*)[kLd]>(sm + P_T);
     float(*sY)[16][16] = reinterpret_cast<float(*)[16][16]>(sm + P_Y3);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int quad = warp & 3, cq = warp >> 2;  // TMEM lane quadrant, column quarter
+    const int quad = warp & 3, half = warp >> 2;  // TMEM lane quadrant, column half
+    const int64_t chunk = blockIdx.x;
+    const int c = (int)(chunk % p.NC);
+    const int bh = (int)(chunk / p.NC);
+    const int b = bh / p.H, h = bh % p.H;
+    const int64_t t0 = (int64_t)c * kChunk;
     const float scale = rsqrtf((float)kDk);
-    const int64_t nchunks = (int64_t)p.B * p.H * p.NC;
-    unsigned char* raw = sm + P_RAW;
+    unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
 
     if (warp == 0) {
         tmem_alloc(&ms.tmem, kPrepTmemCols);
@@ -185,53 +183,40 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         mbar_init(&ms.bar, 1);
         fence_mbar_init();
     }
-    float g_next = 0.f, b_next = 0.f;  // g / beta of the chunk whose rows are in flight (threads 0-63)
-    if ((int64_t)blockIdx.x < nchunks) prep_prefetch(p, blockIdx.x, raw, tid, g_next, b_next);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tm = ms.tmem;
-    const uint32_t sbase = smem_u32(sm);
-    bool ok = true;
-    int it = 0;
-
-    // Persistent: one CTA per SM walks the chunks, the next chunk's rows landing while this one computes.
-    for (int64_t chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x, ++it) {
-    const int c = (int)(chunk % p.NC);
-    const int64_t t0 = (int64_t)c * kChunk;
-    unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
-    const uint32_t ph = (uint32_t)it & 1u;  // parity of this chunk's first of three barrier phases
+    if (tid < kChunk) {  // g, beta of the chunk (rows past T are the zero padding)
+        const int64_t t = t0 + tid;
+        float gv = 0.f, bv = 0.f;
+        if (t < p.T) {
+            gv = load_elem(p.g.p, (int64_t)b * p.g.sb + t * p.g.st + (int64_t)h * p.g.sh, p.g.dtype);
+            bv = load_elem(p.beta.p, (int64_t)b * p.beta.sb + t * p.beta.st + (int64_t)h * p.beta.sh, p.beta.dtype);
+        }
+        ms.gc[tid] = gv;
+        ms.beta[tid] = bv;
+    }
 
     // ---- 1. normalised rows -> swizzled bf16 tiles (qwen3_5_transformers.py:122-137).
-    //      The rows were prefetched; the previous chunk's Q'/o0/M copies must have left L and KQ.
-    cp_async_wait_all();
-    if (tid == 32) bulk_wait_read_keep1();
-    __syncthreads();
-    {
-        // 8 sums of squares (q and k of 4 rows) reduced together: independent shuffle chains.
-        // The inverse norm uses rsqrtf: it is rounded to bf16 right away, so it differs from a
-        // correctly rounded 1/sqrt only when it lies within ~2 fp32 ulp of a bf16 rounding boundary
-        // (the reference's own CPU bf16 rsqrt is an estimate as well).
-        constexpr int kRows = kChunk / (kPrepThreads / 32);
+    //      Each warp owns 8 rows, in two batches of 4 whose 12 row loads are issued together; the 8
+    //      sums of squares of a batch are reduced together.  The inverse norm uses rsqrtf before its
+    //      bf16 rounding: it differs from a correctly rounded 1/sqrt only within ~2 fp32 ulp of a bf16
+    //      rounding boundary (the reference's own CPU bf16 rsqrt is an estimate as well).
+#pragma unroll
+    for (int batch = 0; batch < 2; ++batch) {
+        constexpr int kRows = 4;
         float q[kRows][4], k[kRows][4], v[kRows][4], ss[2 * kRows];
 #pragma unroll
         for (int rr = 0; rr < kRows; ++rr) {
-            const int r = warp + 16 * rr;
-            const uint2 qu = *reinterpret_cast<const uint2*>(raw + 0 * 16384 + r * 256 + 8 * lane);
-            const uint2 ku = *reinterpret_cast<const uint2*>(raw + 1 * 16384 + r * 256 + 8 * lane);
-            const uint2 vu = *reinterpret_cast<const uint2*>(raw + 2 * 16384 + r * 256 + 8 * lane);
-            const __nv_bfloat162* qb = reinterpret_cast<const __nv_bfloat162*>(&qu);
-            const __nv_bfloat162* kb = reinterpret_cast<const __nv_bfloat162*>(&ku);
-            const __nv_bfloat162* vb = reinterpret_cast<const __nv_bfloat162*>(&vu);
+            const int64_t t = t0 + warp + 8 * (4 * batch + rr);
+            if (t < p.T) {
+                load_bf16x4(p.q, b, t, h, lane, q[rr]);
+                load_bf16x4(p.k, b, t, h, lane, k[rr]);
+                load_bf16x4(p.v, b, t, h, lane, v[rr]);
+            } else {
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                q[rr][2 * e] = __low2float(qb[e]);
-                q[rr][2 * e + 1] = __high2float(qb[e]);
-                k[rr][2 * e] = __low2float(kb[e]);
-                k[rr][2 * e + 1] = __high2float(kb[e]);
-                v[rr][2 * e] = __low2float(vb[e]);
-                v[rr][2 * e + 1] = __high2float(vb[e]);
+                for (int e = 0; e < 4; ++e) q[rr][e] = k[rr][e] = v[rr][e] = 0.f;
             }
+        }
+#pragma unroll
+        for (int rr = 0; rr < kRows; ++rr) {
             float sq = 0.f, sk = 0.f;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {  // x*x rounded in bf16, summed in fp32 (qwen3_5_transformers.py:106)
@@ -248,7 +233,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         }
 #pragma unroll
         for (int rr = 0; rr < kRows; ++rr) {
-            const int r = warp + 16 * rr;
+            const int r = warp + 8 * (4 * batch + rr);
             if (p.l2norm && t0 + r < p.T) {
                 const float iq = round_to(rsqrtf(round_to(round_to(ss[2 * rr], GDN_BF16) + 1e-6f, GDN_BF16)), GDN_BF16);
                 const float ik = round_to(rsqrtf(round_to(round_to(ss[2 * rr + 1], GDN_BF16) + 1e-6f, GDN_BF16)), GDN_BF16);
@@ -263,16 +248,12 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
             store_bf16x4(sm + P_V, sw128_offset(r, 4 * lane, 64), v[rr]);
         }
     }
-    if (tid < kChunk) {
-        ms.gc[tid] = g_next;
-        ms.beta[tid] = b_next;
-    }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // the raw staging is consumed: pull in the chunk after this one
-    if (chunk + gridDim.x < nchunks) prep_prefetch(p, chunk + gridDim.x, raw, tid, g_next, b_next);
+    const uint32_t tm = ms.tmem;
+    const uint32_t sbase = smem_u32(sm);
 
     // ---- 2. [k^; q^] k^T -> TMEM cols [0,64): lanes 0-63 G_k = k^ k^T, lanes 64-127 G_q = q^ k^T
     if (tid == 0) {
@@ -300,27 +281,27 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         ms.egc[tid] = __expf(ms.gc[tid]);
         ms.ekd[tid] = __expf(ms.gc[kChunk - 1] - ms.gc[tid]);
     }
-    ok = mbar_wait(&ms.bar, ph, kWaitNs);
+    bool ok = mbar_wait(&ms.bar, 0, kWaitNs);
     tc_fence_after();
 
     // ---- 3. L = -(beta_i G_k e^(gc_i-gc_j)) strictly lower (:152-153), Aqk = Dk^-1/2 G_q e^(gc_i-gc_j) causal (:172)
     if (!__syncthreads_or(!ok)) {
-        float gv[16];
-        tmem_ld16(tmem_addr(tm, 32 * quad, 16 * cq), gv);
+        float gv[32];
+        tmem_ld32(tmem_addr(tm, 32 * quad, 32 * half), gv);
         tmem_ld_wait();
         const int r = 32 * quad + lane, i = r & 63;
         const float gci = ms.gc[i];
         if (r < 64) {
             const float bi = ms.beta[i];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const int j = 16 * cq + e;
+            for (int e = 0; e < 32; ++e) {
+                const int j = 32 * half + e;
                 sL[i][j] = (j < i) ? -(bi * gv[e]) * __expf(gci - ms.gc[j]) : 0.f;
             }
         } else {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const int j = 16 * cq + e;
+            for (int e = 0; e < 32; ++e) {
+                const int j = 32 * half + e;
                 sA[i][j] = (j <= i) ? (scale * gv[e]) * __expf(gci - ms.gc[j]) : 0.f;
             }
         }
@@ -387,28 +368,32 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     }
     __syncthreads();
     if (ok) {  // distance 2: Y_c = L_{c+2,c} T_cc + L_{c+2,c+1} T_{c+1,c}
-        const int cb = tid >> 8, i = (tid >> 4) & 15, j = tid & 15, rb = 16 * (cb + 2);
-        float s0 = 0.f, s1 = 0.f;
+        for (int o = tid; o < 512; o += kPrepThreads) {
+            const int cb = o >> 8, i = (o >> 4) & 15, j = o & 15, rb = 16 * (cb + 2);
+            float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-        for (int m = 0; m < 16; ++m) {
-            s0 += sL[rb + i][16 * cb + m] * sT[16 * cb + m][16 * cb + j];
-            s1 += sL[rb + i][16 * (cb + 1) + m] * sT[16 * (cb + 1) + m][16 * cb + j];
+            for (int m = 0; m < 16; ++m) {
+                s0 += sL[rb + i][16 * cb + m] * sT[16 * cb + m][16 * cb + j];
+                s1 += sL[rb + i][16 * (cb + 1) + m] * sT[16 * (cb + 1) + m][16 * cb + j];
+            }
+            sY[cb][i][j] = s0 + s1;
         }
-        sY[cb][i][j] = s0 + s1;
     }
     __syncthreads();
     if (ok) {  // T_{c+2,c} = T_{c+2,c+2} Y_c
-        const int cb = tid >> 8, i = (tid >> 4) & 15, j = tid & 15, rb = 16 * (cb + 2);
-        float s0 = 0.f, s1 = 0.f;
+        for (int o = tid; o < 512; o += kPrepThreads) {
+            const int cb = o >> 8, i = (o >> 4) & 15, j = o & 15, rb = 16 * (cb + 2);
+            float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-        for (int m = 0; m < 16; m += 2) {
-            s0 += sT[rb + i][rb + m] * sY[cb][m][j];
-            s1 += sT[rb + i][rb + m + 1] * sY[cb][m + 1][j];
+            for (int m = 0; m < 16; m += 2) {
+                s0 += sT[rb + i][rb + m] * sY[cb][m][j];
+                s1 += sT[rb + i][rb + m + 1] * sY[cb][m + 1][j];
+            }
+            sT[rb + i][16 * cb + j] = s0 + s1;
         }
-        sT[rb + i][16 * cb + j] = s0 + s1;
     }
     __syncthreads();
-    if (ok && tid < 256) {  // distance 3: Y = sum_{k<3} L_{3,k} T_{k,0}
+    if (ok) {  // distance 3: Y = sum_{k<3} L_{3,k} T_{k,0}
         const int i = tid >> 4, j = tid & 15;
         float s0 = 0.f, s1 = 0.f, s2 = 0.f;
 #pragma unroll
@@ -420,7 +405,7 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
         sY[0][i][j] = s0 + s1 + s2;
     }
     __syncthreads();
-    if (ok && tid < 256) {  // T_{3,0} = T_33 Y
+    if (ok) {  // T_{3,0} = T_33 Y
         const int i = tid >> 4, j = tid & 15;
         float s0 = 0.f, s1 = 0.f;
 #pragma unroll
@@ -432,111 +417,179 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     }
     __syncthreads();
 
-    if (tid == 32) bulk_wait_read_all();  // the previous chunk's b copy has left P_SPLIT
-    __syncthreads();
-
-    // ---- 5. the four 64x64 coefficient matrices, hi/lo bf16 A tiles [X;Z] and [Y;W]
-    //      X = E_d T B_e, Y = E_d T B, W = (Aqk T) B, Z = (Aqk T) B_e
+    // ---- 5. the four 64x64 coefficient matrices X = E_d T B_e, Y = E_d T B, W = (Aqk T) B, Z = (Aqk T) B_e.
+    //      Thread (row i, 16 columns) keeps T's row and (Aqk T)'s row in registers: once every thread has
+    //      read them, the work region is free for the A tiles.
+    float ti[16], at[16];
+    const int ri = tid & 63, j0 = (tid >> 6) * 16;
     if (ok) {
-        const int i = tid & 63, j0 = (tid >> 6) * 8;
-        float at[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) at[e] = 0.f;
-        for (int m = j0; m <= i; ++m) {  // (Aqk T)[i][j] = sum_{m=j..i} Aqk[i][m] T[m][j]
-            const float a = sA[i][m];
-            const float4 t0v = *reinterpret_cast<const float4*>(&sT[m][j0]);
-            const float4 t1v = *reinterpret_cast<const float4*>(&sT[m][j0 + 4]);
-            at[0] += a * t0v.x;
-            at[1] += a * t0v.y;
-            at[2] += a * t0v.z;
-            at[3] += a * t0v.w;
-            at[4] += a * t1v.x;
-            at[5] += a * t1v.y;
-            at[6] += a * t1v.z;
-            at[7] += a * t1v.w;
+        for (int e = 0; e < 16; ++e) at[e] = 0.f;
+        for (int m = j0; m <= ri; ++m) {  // (Aqk T)[i][j] = sum_{m=j..i} Aqk[i][m] T[m][j]
+            const float a = sA[ri][m];
+#pragma unroll
+            for (int e4 = 0; e4 < 4; ++e4) {
+                const float4 tv = *reinterpret_cast<const float4*>(&sT[m][j0 + 4 * e4]);
+                at[4 * e4] += a * tv.x;
+                at[4 * e4 + 1] += a * tv.y;
+                at[4 * e4 + 2] += a * tv.z;
+                at[4 * e4 + 3] += a * tv.w;
+            }
         }
-        const float4 ta = *reinterpret_cast<const float4*>(&sT[i][j0]);
-        const float4 tb = *reinterpret_cast<const float4*>(&sT[i][j0 + 4]);
-        const float ti[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
-        const float ekdi = ms.ekd[i];
-        float X[8], Y[8], W[8], Z[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
+        for (int e4 = 0; e4 < 4; ++e4) {
+            const float4 tv = *reinterpret_cast<const float4*>(&sT[ri][j0 + 4 * e4]);
+            ti[4 * e4] = tv.x;
+            ti[4 * e4 + 1] = tv.y;
+            ti[4 * e4 + 2] = tv.z;
+            ti[4 * e4 + 3] = tv.w;
+        }
+    }
+    __syncthreads();
+    const float ekdi = ms.ekd[ri];
+    // ---- 6. two M=128, N=128, K=64 rounds (hi+lo): [X;Z] k^ -> cols [0,128) (P_X | Zk), then
+    //      [Y;W] v -> cols [128,256) (P_Y | o0), the A tiles of the second round written over the first's.
+    const uint32_t id6 = make_idesc_f16(128, 128, false, true, true);
+    uint32_t ph = 0;
+    for (int round = 0; round < 2 && ok; ++round) {
+        float top[16], bot[16];  // rows i (X or Y) and 64+i (Z or W)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
             const int j = j0 + e;
-            const float bj = ms.beta[j], bej = ms.beta[j] * ms.egc[j];
-            X[e] = ekdi * ti[e] * bej;
-            Y[e] = ekdi * ti[e] * bj;
-            W[e] = at[e] * bj;
-            Z[e] = at[e] * bej;
+            const float bj = ms.beta[j], bej = bj * ms.egc[j];
+            const float bb = round == 0 ? bej : bj;
+            top[e] = ekdi * ti[e] * bb;
+            bot[e] = at[e] * bb;
         }
-        unsigned char* sp = sm + P_SPLIT;
-        store_split8(sp + 0 * 16384, sp + 1 * 16384, sw128_offset(i, j0, 128), X);
-        store_split8(sp + 0 * 16384, sp + 1 * 16384, sw128_offset(64 + i, j0, 128), Z);
-        store_split8(sp + 2 * 16384, sp + 3 * 16384, sw128_offset(i, j0, 128), Y);
-        store_split8(sp + 2 * 16384, sp + 3 * 16384, sw128_offset(64 + i, j0, 128), W);
+        unsigned char* at_hi = sm + P_ATILE;
+        unsigned char* at_lo = sm + P_ATILE + 16384;
+#pragma unroll
+        for (int h8 = 0; h8 < 2; ++h8) {
+            store_split8(at_hi, at_lo, sw128_offset(ri, j0 + 8 * h8, 128), top + 8 * h8);
+            store_split8(at_hi, at_lo, sw128_offset(64 + ri, j0 + 8 * h8, 128), bot + 8 * h8);
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            mma_split_a(tm + 128 * round, sbase + P_ATILE, sbase + P_ATILE + 16384,
+                        round == 0 ? sbase + P_KQ : sbase + P_V, round == 0 ? 16384 : 8192, id6);
+            mma_commit(&ms.bar);
+        }
+        ++ph;
+        ok = mbar_wait(&ms.bar, ph & 1, kWaitNs);  // the A tiles may be rewritten only after the MMAs read them
+        ok = !__syncthreads_or(!ok);
+    }
+    tc_fence_after();
+
+    // ---- 7. rows 0-63: P_X, P_Y -> hi/lo B tiles; rows 64-127: Q' (in place of q^) and o0 -> workspace
+    if (ok) {
+        const int r = 32 * quad + lane, i = r & 63;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+            float v[32];
+            const int d0 = 64 * half + 32 * cc;
+            tmem_ld32(tmem_addr(tm, 32 * quad, d0), v);
+            tmem_ld_wait();
+            if (r < 64) {  // P_X (MN-major B tile: rows = tokens)
+#pragma unroll
+                for (int q8 = 0; q8 < 4; ++q8)
+                    store_split8(sm + P_PX, sm + P_PX + 16384, sw128_offset(i, d0 + 8 * q8, 64), v + 8 * q8);
+            } else {  // Q' = q^ Dk^-1/2 e^gc - Zk (the q e^gc S of :175 and -Aqk w S of :176 combined)
+                const float qs = scale * ms.egc[i];
+#pragma unroll
+                for (int q8 = 0; q8 < 4; ++q8) {
+                    const uint32_t off = sw128_offset(64 + i, d0 + 8 * q8, 128);
+                    const uint4 qu = *reinterpret_cast<const uint4*>(sm + P_KQ + off);
+                    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(&qu);
+                    float o[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o[e] = qs * __bfloat162float(qb[e]) - v[8 * q8 + e];
+                    store_bf16x8(sm + P_KQ, off, o);  // rows 64-127 of KQ: the layout of the Q' image
+                }
+            }
+        }
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+            float v[32];
+            const int d0 = 64 * half + 32 * cc;
+            tmem_ld32(tmem_addr(tm, 32 * quad, 128 + d0), v);
+            tmem_ld_wait();
+            if (r < 64) {  // P_Y
+#pragma unroll
+                for (int q8 = 0; q8 < 4; ++q8)
+                    store_split8(sm + P_PYH, sm + P_PYL, sw128_offset(i, d0 + 8 * q8, 64), v + 8 * q8);
+            } else {  // o0 = Aqk u, fp32 column tile d0/32, straight to the workspace
+                unsigned char* blk = wrec + kTcO0 + (d0 >> 5) * (64 * 128);
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4)
+                    *reinterpret_cast<float4*>(blk + f32blk_offset(i, q4)) =
+                        make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+            }
+        }
     }
     fence_proxy_async_smem();
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    if (ok && tid == 32) {  // the Q' image leaves while the tensor core works on step 8
+        bulk_s2g(wrec + kTcQ, sm + P_KQ + 8192, 8192);
+        bulk_s2g(wrec + kTcQ + 8192, sm + P_KQ + 16384 + 8192, 8192);
+        bulk_commit();
+    }
 
-    // ---- 6. [X;Z] k^ -> cols [0,128) (P_X | Zk), [Y;W] v -> cols [128,256) (P_Y | o0); M=128, N=128, K=64, hi+lo
+    // ---- 8. M' = k^T P_X -> [0,128), b = k^T P_Y -> [128,256)  (M=128 over Dk, K = tokens)
     if (ok && tid == 0) {
-        tc_fence_after();
-        const uint32_t id = make_idesc_f16(128, 128, false, true, true);
-        const uint32_t sp = sbase + P_SPLIT;
+        const uint32_t id = make_idesc_f16(128, 128, true, true, true);
+        const uint32_t btiles[4] = {sbase + P_PX, sbase + P_PX + 16384, sbase + P_PYH, sbase + P_PYL};
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-            const uint32_t bt = r == 0 ? sbase + P_KQ : sbase + P_V;
-            const uint32_t blbo = r == 0 ? 16384 : 8192;
 #pragma unroll
-            for (int s2 = 0; s2 < 2; ++s2) {  // hi, lo
+            for (int s2 = 0; s2 < 2; ++s2) {
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks) {
-                    const uint64_t ad = make_sdesc(sp + (2 * r + s2) * 16384 + ks * 32, 16, 1024, kSwizzle128B);
-                    const uint64_t bd = make_sdesc(bt + ks * 2048, blbo, 1024, kSwizzle128B);
+                    const uint64_t ad = make_sdesc(sbase + P_KQ + ks * 2048, 16384, 1024, kSwizzle128B);
+                    const uint64_t bd = make_sdesc(btiles[2 * r + s2] + ks * 2048, 8192, 1024, kSwizzle128B);
                     mma_f16(tm + 128 * r, ad, bd, id, (s2 | ks) != 0);
                 }
             }
         }
         mma_commit(&ms.bar);
     }
-    if (ok) ok = mbar_wait(&ms.bar, ph ^ 1u, kWaitNs);
+    if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);  // fourth completion of the barrier
+    if (tid == 32) bulk_wait_read_all();       // KQ is rewritten below: the Q' copy must have read it
     tc_fence_after();
 
-    // ---- 7. rows 0-63: P_X, P_Y -> hi/lo B tiles; rows 64-127: Q' and o0 -> workspace
+    // ---- 9. M = e^gc_last I - M' (bf16 image into KQ), b (fp32 column tiles into V / the P tiles)
     if (!__syncthreads_or(!ok)) {
-        const int r = 32 * quad + lane, i = r & 63;
-        unsigned char* sp = sm + P_SPLIT;
-        float v[32];
-        tmem_ld32(tmem_addr(tm, 32 * quad, 32 * cq), v);
-        tmem_ld_wait();
-        if (r < 64) {  // P_X (MN-major B tile: rows = tokens)
+        const int dk = 32 * quad + lane;
+        const float gamma = ms.egc[kChunk - 1];
 #pragma unroll
-            for (int q8 = 0; q8 < 4; ++q8)
-                store_split8(sp, sp + 16384, sw128_offset(i, 32 * cq + 8 * q8, 64), v + 8 * q8);
-        } else {  // Q' = q^ Dk^-1/2 e^gc - Zk (the q e^gc S of :175 and -Aqk w S of :176 combined)
-            const float qs = scale * ms.egc[i];
+        for (int cc = 0; cc < 2; ++cc) {
+            float v[32];
+            const int c0 = 64 * half + 32 * cc;
+            tmem_ld32(tmem_addr(tm, 32 * quad, c0), v);
+            tmem_ld_wait();
 #pragma unroll
             for (int q8 = 0; q8 < 4; ++q8) {
-                const int d = 32 * cq + 8 * q8;
-                const uint4 qu = *reinterpret_cast<const uint4*>(sm + P_KQ + sw128_offset(64 + i, d, 128));
-                const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(&qu);
-                float o[8];
+                const int col = c0 + 8 * q8;
+                float m[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) o[e] = qs * __bfloat162float(qb[e]) - v[8 * q8 + e];
-                store_bf16x8(sm + P_STG_Q, sw128_offset(i, d, 64), o);
+                for (int e = 0; e < 8; ++e) m[e] = ((col + e) == dk ? gamma : 0.f) - v[8 * q8 + e];
+                store_bf16x8(sm + P_KQ, sw128_offset(dk, col, 128), m);
             }
         }
-        tmem_ld32(tmem_addr(tm, 32 * quad, 128 + 32 * cq), v);
-        tmem_ld_wait();
-        if (r < 64) {  // P_Y
+        const uint32_t btile[4] = {P_V, P_W, P_W + 16384, P_W + 32768};
 #pragma unroll
-            for (int q8 = 0; q8 < 4; ++q8)
-                store_split8(sp + 32768, sp + 49152, sw128_offset(i, 32 * cq + 8 * q8, 64), v + 8 * q8);
-        } else {  // o0 = Aqk u, fp32 column tile cq
-            unsigned char* blk = sm + P_STG_O0 + cq * (64 * 128);
+        for (int cc = 0; cc < 2; ++cc) {
+            float v[32];
+            const int c0 = 64 * half + 32 * cc;
+            tmem_ld32(tmem_addr(tm, 32 * quad, 128 + c0), v);
+            tmem_ld_wait();
+            unsigned char* blk = sm + btile[c0 >> 5];
 #pragma unroll
             for (int q4 = 0; q4 < 8; ++q4)
-                *reinterpret_cast<float4*>(blk + f32blk_offset(i, q4)) =
+                *reinterpret_cast<float4*>(blk + f32blk_offset(dk, q4)) =
                     make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
         }
     } else {
@@ -545,77 +598,23 @@ __global__ void __launch_bounds__(kPrepThreads, 1) gdn_prep_tc(ChunkParams p) {
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
-    tc_fence_after();
-    if (ok && tid == 32) {  // Q' and o0 leave while the tensor core works on step 8
-        bulk_s2g(wrec + kTcQ, sm + P_STG_Q, 16384);
-        bulk_s2g(wrec + kTcO0, sm + P_STG_O0, 32768);
-        bulk_commit();
-    }
-
-    // ---- 8. M' = k^T P_X -> [0,128), b = k^T P_Y -> [128,256)  (M=128 over Dk, K = tokens)
-    if (ok && tid == 0) {
-        const uint32_t id = make_idesc_f16(128, 128, true, true, true);
-        const uint32_t sp = sbase + P_SPLIT;
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-#pragma unroll
-            for (int s2 = 0; s2 < 2; ++s2) {
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) {
-                    const uint64_t ad = make_sdesc(sbase + P_KQ + ks * 2048, 16384, 1024, kSwizzle128B);
-                    const uint64_t bd = make_sdesc(sp + (2 * r + s2) * 16384 + ks * 2048, 8192, 1024, kSwizzle128B);
-                    mma_f16(tm + 128 * r, ad, bd, id, (s2 | ks) != 0);
-                }
-            }
+    if (tid == 32) {
+        if (ok) {
+            bulk_s2g(wrec + kTcM, sm + P_KQ, 32768);
+            bulk_s2g(wrec + kTcB + 0 * 16384, sm + P_V, 16384);
+            bulk_s2g(wrec + kTcB + 1 * 16384, sm + P_W, 16384);
+            bulk_s2g(wrec + kTcB + 2 * 16384, sm + P_W + 16384, 16384);
+            bulk_s2g(wrec + kTcB + 3 * 16384, sm + P_W + 32768, 16384);
+            bulk_commit();
         }
-        mma_commit(&ms.bar);
+        bulk_wait_read_all();  // shared memory must outlive every copy that reads it
     }
-    if (ok) ok = mbar_wait(&ms.bar, ph, kWaitNs);
-    tc_fence_after();
-
-    // ---- 9. M = e^gc_last I - M' (bf16 image), b (fp32 column tiles)
-    if (!__syncthreads_or(!ok)) {
-        const int dk = 32 * quad + lane;
-        const float gamma = ms.egc[kChunk - 1];
-        float v[32];
-        tmem_ld32(tmem_addr(tm, 32 * quad, 32 * cq), v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-            const int col = 32 * cq + 8 * q8;
-            float m[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) m[e] = ((col + e) == dk ? gamma : 0.f) - v[8 * q8 + e];
-            store_bf16x8(sm + P_STG_M, sw128_offset(dk, col, 128), m);
-        }
-        tmem_ld32(tmem_addr(tm, 32 * quad, 128 + 32 * cq), v);
-        tmem_ld_wait();
-        unsigned char* blk = sm + P_STG_B + cq * (128 * 128);
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4)
-            *reinterpret_cast<float4*>(blk + f32blk_offset(dk, q4)) =
-                make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
-    } else {
-        ok = false;
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 32 && ok) {  // two groups: M (KQ region) then b (P_SPLIT region)
-        bulk_s2g(wrec + kTcM, sm + P_STG_M, 32768);
-        bulk_commit();
-        bulk_s2g(wrec + kTcB, sm + P_STG_B, 65536);
-        bulk_commit();
-    }
-    if (!ok) break;
-    }  // chunk loop
-    if (tid == 32) bulk_wait_read_all();  // shared memory must outlive every copy that reads it
-    cp_async_wait_all();                 // and every prefetch that writes it
     if (!ok && tid == 0) report(p.err, kErrTimeoutPrep);
-    tc_fence_before();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tm, kPrepTmemCols);
+    }
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tm, kPrepTmemCols);
 }
 
 // ============================================================================ scan
@@ -891,11 +890,7 @@ cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(gdn_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM);
     if (e != cudaSuccess) return e;
     const int64_t nchunks = (int64_t)p.B * p.H * p.NC;
-    int dev = 0, sms = 0;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    const unsigned prep_grid = (unsigned)(nchunks < (int64_t)sms ? nchunks : (int64_t)sms);
-    gdn_prep_tc<<<prep_grid, kPrepThreads, P_SMEM, stream>>>(p);
+    gdn_prep_tc<<<(unsigned)nchunks, kPrepThreads, P_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     return cudaSuccess;
