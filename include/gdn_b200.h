@@ -50,7 +50,8 @@ typedef enum {
 
 typedef enum { GDN_F32 = 0, GDN_BF16 = 1, GDN_F16 = 2 } gdn_dtype;
 
-/* A strided view of device memory.  Unused trailing dims have size 1. */
+/* A strided view of device memory (host memory for gdn_chunk_gated_delta_rule_host).
+ * Unused trailing dims have size 1. */
 typedef struct {
     void* data;        /* device pointer                                   */
     int32_t dtype;     /* gdn_dtype                                        */
@@ -103,6 +104,42 @@ GDN_API int gdn_chunk_gated_delta_rule_noalloc(const gdn_tensor* query, const gd
                                                const float* initial_state, int output_final_state,
                                                int use_qk_l2norm_in_kernel, gdn_tensor* out,
                                                float* final_state, void* stream);
+
+/* Chunked forward over HOST buffers, the copies overlapped with the compute.
+ *
+ * No counterpart in the reference: its op takes device tensors
+ * (qwen3_5_cutedsl_kernels.py:462-473), so a caller holding host data copies
+ * everything in, runs the op, and copies everything out, one after the other.
+ * This call does the copies itself, cut into time slices of at most
+ * `slice_tokens` (a multiple of chunk_size; 0 = about 12 MiB of q/k/v per
+ * slice, e.g. 1024 tokens at B=1, H=16 bf16): slice s+1's inputs cross PCIe
+ * while slice s computes and slice s-1's outputs come back, on two copy streams
+ * of the library's own ordered against `stream` by events.
+ *   query/key/value/g/beta/out  views of HOST memory, packed [B][T][H][D] and
+ *               [B][T][H] (only the batch stride free; GDN_ERR_UNSUPPORTED
+ *               otherwise); page-locked (cudaHostAlloc / cudaHostRegister) for
+ *               the copies to overlap, pageable memory works but serialises.
+ *   initial_state, final_state  host [B,H,Dk,Dv] fp32 or NULL, as in
+ *               gdn_chunk_gated_delta_rule; may alias.
+ *   workspace   DEVICE memory of gdn_chunk_host_workspace_bytes(...) bytes,
+ *               256-byte aligned (sized for out in the query dtype and 4-byte
+ *               g/beta: wider out or g/beta than that need more and get
+ *               GDN_ERR_WORKSPACE).
+ * Asynchronous like the device call: the results are in host memory once
+ * `stream` has reached the end of this call's work.  The slices start on chunk
+ * boundaries and carry the state in fp32, so the results equal one
+ * gdn_chunk_gated_delta_rule call on the whole sequence. */
+GDN_API int gdn_chunk_gated_delta_rule_host(const gdn_tensor* query, const gdn_tensor* key,
+                                            const gdn_tensor* value, const gdn_tensor* g, const gdn_tensor* beta,
+                                            int chunk_size, const float* initial_state, int output_final_state,
+                                            int use_qk_l2norm_in_kernel, gdn_tensor* out, float* final_state,
+                                            int64_t slice_tokens, void* workspace, size_t workspace_bytes,
+                                            void* stream);
+
+/* Device workspace bytes of gdn_chunk_gated_delta_rule_host (0 for an empty problem
+ * or a slice_tokens that is negative or not a multiple of 64). */
+GDN_API size_t gdn_chunk_host_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int qkv_dtype,
+                                              int64_t slice_tokens);
 
 /* Sequence parallelism: one long sequence split into contiguous time shards,
  * one shard per GPU.  No counterpart in the reference, which runs the chunk

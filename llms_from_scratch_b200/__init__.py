@@ -7,6 +7,7 @@ The CUDA library ``libgdn_b200.so`` is built in-tree by
 """
 
 from .ops import (  # noqa: F401
+    chunk_host_workspace_bytes,
     chunk_workspace_bytes,
     fast_chunk_gated_delta_rule,
     fast_recurrent_gated_delta_rule,
@@ -15,4 +16,4 @@ from .ops import (  # noqa: F401
 )
 
 __all__ = ["fast_chunk_gated_delta_rule", "fast_recurrent_gated_delta_rule", "chunk_workspace_bytes",
-           "get_backend", "l2norm"]
+           "chunk_host_workspace_bytes", "get_backend", "l2norm"]

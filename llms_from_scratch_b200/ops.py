@@ -8,8 +8,13 @@
 
 Both allocate their outputs (the caller owns them), never modify inputs, run
 asynchronously on the current CUDA stream, and raise ``RuntimeError`` (a
-``GDNError``) on bad arguments, as the reference's torch ops do.  CPU tensors
-raise: there is no CPU path.
+``GDNError``) on bad arguments, as the reference's torch ops do.
+
+``fast_chunk_gated_delta_rule`` given CPU tensors computes them on the current
+CUDA device through ``gdn_chunk_gated_delta_rule_host``: the library streams
+time slices in and out over PCIe while earlier slices compute, and the call
+returns page-locked CPU outputs once they have landed.  There is no CPU compute
+path: without a CUDA device, CPU tensors raise.
 """
 
 from __future__ import annotations
@@ -92,6 +97,7 @@ def fast_chunk_gated_delta_rule(
     use_qk_l2norm_in_kernel: bool = False,
     backend: str = "auto",
     workspace: Optional[torch.Tensor] = None,
+    slice_tokens: int = 0,
 ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """Chunked gated delta rule forward on the GPU.
 
@@ -99,8 +105,17 @@ def fast_chunk_gated_delta_rule(
     arguments, layouts (``[B,T,H,D]``) and outputs.  ``workspace`` optionally
     supplies a reusable uint8 CUDA buffer of at least
     ``chunk_workspace_bytes(...)`` bytes (allocated per call otherwise).
+
+    CPU inputs take the host-buffer path (module docstring): outputs come back
+    as page-locked CPU tensors after the call has finished on the device;
+    ``workspace`` is then a CUDA buffer of ``chunk_host_workspace_bytes(...)``
+    bytes and ``slice_tokens`` the time slice the copies are pipelined in
+    (0 = the library's choice).
     """
     _check_backend(backend)
+    if isinstance(query, torch.Tensor) and query.device.type == "cpu":
+        return _chunk_from_host(query, key, value, g, beta, chunk_size, initial_state, output_final_state,
+                                use_qk_l2norm_in_kernel, workspace, slice_tokens)
     q = _as_kernel_tensor(query, "query", 4)
     k = _as_kernel_tensor(key, "key", 4)
     v = _as_kernel_tensor(value, "value", 4)
@@ -137,6 +152,66 @@ def fast_chunk_gated_delta_rule(
 def chunk_workspace_bytes(B: int, T: int, H: int, Dk: int = 128, Dv: int = 128,
                           dtype: torch.dtype = torch.bfloat16) -> int:
     return int(_lib.load().gdn_chunk_workspace_bytes(B, T, H, Dk, Dv, _DTYPES.get(dtype, _lib.GDN_F32)))
+
+
+def chunk_host_workspace_bytes(B: int, T: int, H: int, Dk: int = 128, Dv: int = 128,
+                               dtype: torch.dtype = torch.bfloat16, slice_tokens: int = 0) -> int:
+    """Device bytes the host-buffer path needs (``gdn_chunk_host_workspace_bytes``)."""
+    return int(_lib.load().gdn_chunk_host_workspace_bytes(B, T, H, Dk, Dv, _DTYPES.get(dtype, _lib.GDN_F32),
+                                                          int(slice_tokens)))
+
+
+def _host_tensor(x, name: str, ndim: int) -> torch.Tensor:
+    if not isinstance(x, torch.Tensor):
+        raise RuntimeError(f"{name} must be a torch.Tensor")
+    if x.dim() != ndim:
+        raise RuntimeError(f"{name} must have {ndim} dims, got shape {tuple(x.shape)}")
+    if x.device.type != "cpu":
+        raise RuntimeError(f"{name} is on {x.device}, query on cpu")
+    if x.dtype not in _DTYPES:
+        x = x.float()
+    return x.contiguous()
+
+
+def _chunk_from_host(query, key, value, g, beta, chunk_size, initial_state, output_final_state,
+                     use_qk_l2norm_in_kernel, workspace, slice_tokens):
+    if not torch.cuda.is_available():
+        raise RuntimeError("query is on cpu: the GatedDeltaNet kernels compute host tensors on a CUDA device, "
+                           "and none is available (no CPU path)")
+    q = _host_tensor(query, "query", 4)
+    k = _host_tensor(key, "key", 4)
+    v = _host_tensor(value, "value", 4)
+    gg = _host_tensor(g, "g", 3)
+    bb = _host_tensor(beta, "beta", 3)
+    B, T, H, Dk = q.shape
+    Dv = v.shape[-1]
+    h0 = None
+    if initial_state is not None:
+        if tuple(initial_state.shape) != (B, H, Dk, Dv):
+            raise RuntimeError(f"initial_state must have shape {(B, H, Dk, Dv)}, got {tuple(initial_state.shape)}")
+        if initial_state.device.type != "cpu":
+            raise RuntimeError(f"initial_state is on {initial_state.device}, query on cpu")
+        h0 = initial_state.to(torch.float32).contiguous()
+    out = torch.empty((B, T, H, Dv), dtype=q.dtype, pin_memory=True)
+    final = torch.empty((B, H, Dk, Dv), dtype=torch.float32, pin_memory=True) if output_final_state else None
+    dev = torch.device("cuda", torch.cuda.current_device())
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        need = lib.gdn_chunk_host_workspace_bytes(B, T, H, Dk, Dv, _DTYPES[q.dtype], int(slice_tokens))
+        if workspace is None or workspace.device != dev or workspace.numel() < need:
+            workspace = torch.empty((max(need, 1),), dtype=torch.uint8, device=dev)
+        dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
+        stream = torch.cuda.current_stream(dev)
+        rc = lib.gdn_chunk_gated_delta_rule_host(
+            ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(dg), ctypes.byref(db),
+            int(chunk_size), h0.data_ptr() if h0 is not None else None, int(bool(output_final_state)),
+            int(bool(use_qk_l2norm_in_kernel)), ctypes.byref(do), final.data_ptr() if final is not None else None,
+            int(slice_tokens), workspace.data_ptr(), workspace.numel(), stream.cuda_stream)
+        _lib.check(rc)
+        stream.synchronize()  # the outputs are host memory: hand them over complete
+    if out.dtype != query.dtype:
+        out = out.to(query.dtype)
+    return out, final
 
 
 def fast_recurrent_gated_delta_rule(

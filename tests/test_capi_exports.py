@@ -111,6 +111,57 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call(lib, case, needle):
         _lib.check(rc)
 
 
+def _call_host(lib, q, k, v, g, b, out, slice_tokens=0, ws=0x100000, ws_bytes=1 << 40):
+    return lib.gdn_chunk_gated_delta_rule_host(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v), ctypes.byref(g),
+                                               ctypes.byref(b), 64, None, 0, 1, ctypes.byref(out), None,
+                                               slice_tokens, ws, ws_bytes, None)
+
+
+@pytest.mark.parametrize("case,status,needle", [
+    ("slice", _lib.GDN_ERR_INVALID_ARGUMENT, "slice_tokens"),
+    ("dv", _lib.GDN_ERR_INVALID_ARGUMENT, "head dim must be 128"),
+    ("gshape", _lib.GDN_ERR_INVALID_ARGUMENT, "differs from query"),
+    ("unpacked", _lib.GDN_ERR_UNSUPPORTED, "packed [B][T][H][D]"),
+    ("unpacked_g", _lib.GDN_ERR_UNSUPPORTED, "packed [B][T][H]"),
+    ("workspace", _lib.GDN_ERR_WORKSPACE, "workspace of"),
+])
+def test_host_entry_rejects_bad_arguments_before_any_cuda_call(lib, case, status, needle):
+    B, T, H = 2, 300, 2
+    q, k, v, out = (_t([B, T, H, 128]) for _ in range(4))
+    g, b = _t([B, T, H], _lib.GDN_F32), _t([B, T, H], _lib.GDN_F32)
+    kw = {}
+    if case == "slice":
+        kw["slice_tokens"] = 100
+    elif case == "dv":
+        out = _t([B, T, H, 64])
+    elif case == "gshape":
+        b = _t([B, T, H + 1], _lib.GDN_F32)
+    elif case == "unpacked":
+        v.stride[1] = 2 * H * 128  # every other token of a wider buffer
+    elif case == "unpacked_g":
+        g.stride[2] = 2
+    elif case == "workspace":
+        kw["ws_bytes"] = 1024
+    rc = _call_host(lib, q, k, v, g, b, out, **kw)
+    assert rc == status
+    assert needle in lib.gdn_last_error().decode()
+
+
+def test_host_workspace_size(lib):
+    f = lib.gdn_chunk_host_workspace_bytes
+    assert f(1, 4096, 16, 128, 128, _lib.GDN_BF16, 100) == 0  # slice not a multiple of 64
+    assert f(0, 4096, 16, 128, 128, _lib.GDN_BF16, 0) == 0
+    a = f(1, 4096, 16, 128, 128, _lib.GDN_BF16, 0)
+    b = f(1, 4096, 16, 128, 128, _lib.GDN_BF16, 1024)
+    assert a == b > 0 and a % 256 == 0  # the default largest slice at B=1, H=16 is 1024 tokens (12 MiB of q/k/v)
+    # one slice's chunk workspace + the state + g/beta of the whole sequence + two q/k/v and two out slices
+    ws = lib.gdn_chunk_workspace_bytes(1, 1024, 16, 128, 128, _lib.GDN_BF16)
+    rows = 1024 * 16
+    assert a == ws + 16 * 128 * 128 * 4 + 2 * 4096 * 16 * 4 + 2 * 3 * rows * 256 + 2 * rows * 256
+    # short sequences stage one slice rounded up to the chunk
+    assert f(1, 100, 1, 128, 128, _lib.GDN_BF16, 0) == f(1, 128, 1, 128, 128, _lib.GDN_BF16, 0)
+
+
 def test_final_state_pointer_required(lib):
     B, T, H = 1, 8, 1
     q, k, v, out = (_t([B, T, H, 128]) for _ in range(4))
@@ -127,8 +178,9 @@ def test_python_op_refuses_cpu_tensors_and_torch_backend():
     from llms_from_scratch_b200 import fast_chunk_gated_delta_rule, fast_recurrent_gated_delta_rule
     q = torch.zeros(1, 4, 1, 128)
     g = torch.zeros(1, 4, 1)
-    with pytest.raises(RuntimeError, match="CUDA tensors"):
-        fast_chunk_gated_delta_rule(q, q, q, g, g)
+    if not torch.cuda.is_available():  # CPU tensors go to the GPU through the host-buffer path
+        with pytest.raises(RuntimeError, match="no CPU path"):
+            fast_chunk_gated_delta_rule(q, q, q, g, g)
     with pytest.raises(RuntimeError, match="CUDA tensors"):
         fast_recurrent_gated_delta_rule(q, q, q, g, g, None, False)
     with pytest.raises(RuntimeError, match="pure-PyTorch"):
