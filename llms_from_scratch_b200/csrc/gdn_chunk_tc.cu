@@ -37,10 +37,11 @@
 // gdn_scan_tc: one CTA per (batch, head, 32-column slice of Dv); warps 4-5
 //   bulk-copy each chunk's workspace record (double-buffered, the M/Q half freed
 //   as soon as the tensor core has read it, records pulled into L2 four chunks
-//   ahead); warps 0-3 turn the state accumulator into the next state, one lane
-//   issues the next chunk's state MMAs as soon as that state is in shared
-//   memory (then the output MMAs, into alternating TMEM columns), and a chunk's
-//   output rows are written while the next chunk's MMAs run.
+//   ahead); warps 0-3 turn the state accumulator into the next state and signal
+//   warp 6, which issues the next chunk's state MMAs as soon as that state is in
+//   shared memory (then the output MMAs, into alternating TMEM columns) from one
+//   elected lane of a converged warp; a chunk's output rows are written after
+//   the next state has been handed over, while the next chunk's MMAs run.
 #include <cuda_bf16.h>
 
 #include "gdn_common.cuh"
@@ -619,10 +620,12 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
 
 // ============================================================================ scan
 
-constexpr int kScanThreads = 192;          // warps 0-3: state/output epilogue (thread 0 issues the MMAs),
-                                           // 4: M/Q bulk copies + L2 prefetch, 5: b/o0 bulk copies
+constexpr int kScanThreads = 224;          // warps 0-3: state/output epilogue, 4: M/Q bulk copies + L2 prefetch,
+                                           // 5: b/o0 bulk copies, 6: MMA issue
 constexpr int kScanPrefetch = 4;           // chunks ahead that the producer pulls into L2
-constexpr int kScanIssuer = 16;            // warp 0 lane 16: issues the MMAs (lanes 16-31 own no output rows)
+constexpr int kScanMmaWarp = 6;
+constexpr uint32_t kScanBarS = 1;          // named barrier: epilogue (128) arrives with S_c stored, MMA warp waits
+constexpr uint32_t kScanBarCount = 160;
 constexpr uint32_t kScanTmemCols = 128;    // cols [0,32) state accumulator, [32,64) / [64,96) output accumulators
 constexpr uint32_t S_STAGE = 73728;        // M image 32K | Q image 16K | b slice 16K | o0 slice 8K
 constexpr uint32_t S_OFF_Q = 32768, S_OFF_B = 49152, S_OFF_O0 = 65536;
@@ -642,19 +645,8 @@ struct ScanMisc {
     int abort;
 };
 
-// Named barrier over `nthreads` threads that also returns whether any of them passed `flag` != 0,
-// so a failure seen by one thread ends the loop of all of them together.
-__device__ __forceinline__ bool named_barrier_any(uint32_t id, uint32_t nthreads, bool flag) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, %2, %3, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)flag), "r"(id), "r"(nthreads)
-        : "memory");
-    return r != 0;
+__device__ __forceinline__ bool scan_aborted(const ScanMisc& ms) {
+    return *reinterpret_cast<const volatile int*>(&ms.abort) != 0;
 }
 
 // o_c rows 16w..16w+15 of this CTA's 32 columns: o = Q'S (accumulator) + o0 (stage smem).
@@ -679,6 +671,14 @@ __device__ __forceinline__ void scan_store_output(const ChunkParams& p, const un
     for (int q8 = 0; q8 < 4; ++q8) store_bf16x8(dst, 16 * q8, ov + 8 * q8);
 }
 
+// The chunk-to-chunk chain S_{c+1} = M_c S_c + b_c runs through three parties each
+// chunk: the epilogue warps store S_c as a bf16 operand tile and arrive on a named
+// barrier; the MMA warp (converged, one elected lane issuing) waits on it and issues
+// the state product, then the output product; the epilogue waits for the state
+// accumulator, adds b_c, stores S_{c+1} and arrives, and only then turns to chunk c's
+// outputs, which overlap the next chunk's MMAs.  Every party takes every barrier
+// step of every chunk, also after a failed wait (then it skips the work), so the
+// named barrier can never be left short of arrivals.
 __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -716,7 +716,42 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     const uint32_t sbase = smem_u32(sm);
     bool ok = true;
 
-    if (warp >= 4) {
+    if (warp == kScanMmaWarp) {
+        // ---------------- MMA issue: the whole warp runs the loop, one elected lane issues
+        const uint32_t leader = elect_one();
+        const uint32_t idS = make_idesc_f16(128, kTcDvTile, false, true, true);
+        const uint32_t idO = make_idesc_f16(64, kTcDvTile, false, true, true);
+        const uint64_t dM = make_sdesc(sbase, 16, 1024, kSwizzle128B);
+        const uint64_t dQ = make_sdesc(sbase + S_OFF_Q, 16, 1024, kSwizzle128B);
+        const uint64_t dS = make_sdesc(sbase + S_STILE, 16384, 1024, kSwizzle128B);
+        for (int c = 0; c < p.NC; ++c) {
+            const int s = c & 1;
+            named_bar_sync(kScanBarS, kScanBarCount);  // S_c is in operand tile s
+            bool go = ok && !scan_aborted(ms);
+            if (go) go = mbar_wait(&ms.full_mq[s], (c >> 1) & 1, kWaitNs);
+            if (!__all_sync(0xffffffffu, go)) {  // the warp decides together
+                ok = false;  // no MMA from here on: the epilogue's waits give up at the abort flag
+                ms.abort = 1;
+                continue;
+            }
+            tc_fence_after();
+            const uint64_t so = (uint64_t)((s * S_STAGE) >> 4);
+            // state first: it is the only product on the sequential path
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+                mma_f16_if(leader, tm + 0, dM + so + (uint64_t)((((ks >> 2) * 16384) + (ks & 3) * 32) >> 4),
+                           dS + (uint64_t)((s * 16384 + ks * 2048) >> 4), idS, ks > 0);
+            mma_commit_if(leader, &ms.mma_s);
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+                mma_f16_if(leader, tm + kTcDvTile * (1 + s),
+                           dQ + so + (uint64_t)((((ks >> 2) * 8192) + (ks & 3) * 32) >> 4),
+                           dS + (uint64_t)((s * 16384 + ks * 2048) >> 4), idO, ks > 0);
+            mma_commit_if(leader, &ms.mma_o[s]);
+            mma_commit_if(leader, &ms.empty_mq[s]);
+            __syncwarp();
+        }
+    } else if (warp >= 4) {
         // ---------------- producers: warp 4 streams the M/Q images, warp 5 the b/o0 slices
         if (lane == 0) {
             const bool mq = warp == 4;
@@ -732,11 +767,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                     bulk_prefetch_l2(pre + kTcB + dvt * 16384, 16384);
                     bulk_prefetch_l2(pre + kTcO0 + dvt * 8192, 8192);
                 }
+                if (scan_aborted(ms)) break;
                 if (c >= 2 && !mbar_wait(&empty[s], ((c >> 1) - 1) & 1, kWaitNs)) {
                     ok = false;
                     break;
                 }
-                if (ms.abort) break;
                 const unsigned char* rec = wbase + (int64_t)c * kTcChunkBytes;
                 unsigned char* st = sm + s * S_STAGE;
                 mbar_arrive_expect_tx(&full[s], bytes);
@@ -777,101 +812,61 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
 #pragma unroll
         for (int q8 = 0; q8 < kTcDvTile / 8; ++q8) store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
         fence_proxy_async_smem();
-
-        // descriptors of stage 0 / k-step 0; the others differ only in the start address
-        const uint32_t idS = make_idesc_f16(128, kTcDvTile, false, true, true);
-        const uint32_t idO = make_idesc_f16(64, kTcDvTile, false, true, true);
-        const uint64_t dM = make_sdesc(sbase, 16, 1024, kSwizzle128B);
-        const uint64_t dQ = make_sdesc(sbase + S_OFF_Q, 16, 1024, kSwizzle128B);
-        const uint64_t dS = make_sdesc(sbase + S_STILE, 16384, 1024, kSwizzle128B);
+        named_bar_arrive(kScanBarS, kScanBarCount);  // S_0 for chunk 0
 
         for (int c = 0; c < p.NC; ++c) {
             const int s = c & 1;
-            // every row of S_c is in the operand tile; leave together if any thread failed a wait
-            if (named_barrier_any(1, 128, !ok)) {
-                ok = false;
-                break;
-            }
-            if (tid == kScanIssuer) {
-                if (!mbar_wait(&ms.full_mq[s], (c >> 1) & 1, kWaitNs)) {
-                    ms.abort = 1;  // no MMA this chunk: every thread's wait below gives up
-                } else {
-                    tc_fence_after();
-                    const uint64_t so = (uint64_t)((s * S_STAGE) >> 4);
-                    // state first: it is the only product on the sequential path
-#pragma unroll
-                    for (int ks = 0; ks < 8; ++ks)
-                        mma_f16(tm + 0, dM + so + (uint64_t)((((ks >> 2) * 16384) + (ks & 3) * 32) >> 4),
-                                dS + (uint64_t)((s * 16384 + ks * 2048) >> 4), idS, ks > 0);
-                    mma_commit(&ms.mma_s);
-#pragma unroll
-                    for (int ks = 0; ks < 8; ++ks)
-                        mma_f16(tm + kTcDvTile * (1 + s), dQ + so + (uint64_t)((((ks >> 2) * 8192) + (ks & 3) * 32) >> 4),
-                                dS + (uint64_t)((s * 16384 + ks * 2048) >> 4), idO, ks > 0);
-                    mma_commit(&ms.mma_o[s]);
-                    mma_commit(&ms.empty_mq[s]);
-                }
-            }
-            // previous chunk's output rows, overlapping this chunk's MMAs
-            if (c > 0) {
-                const int sp = (c - 1) & 1;
-                if (!mbar_wait(&ms.mma_o[sp], ((c - 1) >> 1) & 1, kWaitNs)) {
-                    ok = false;
-                    continue;
-                }
-                tc_fence_after();
-                float o[32];
-                tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + sp)), o);
-                tmem_ld_wait();
-                if (!summary) scan_store_output(p, sm + sp * S_STAGE, o, c - 1, warp, lane, b, h, dv0);
-                mbar_arrive(&ms.empty_bo[sp]);
-            }
-            if (!mbar_wait(&ms.mma_s, c & 1, kWaitNs) || !mbar_wait(&ms.full_bo[s], (c >> 1) & 1, kWaitNs)) {
-                ok = false;
-                continue;  // the barrier at the top of the loop ends every thread's loop
-            }
-            tc_fence_after();
-            float d[32];
-            tmem_ld32(tmem_addr(tm, 32 * warp, 0), d);
-            tmem_ld_wait();
             const unsigned char* st = sm + s * S_STAGE;
-            // S_{c+1} = M_c S_c + b_c
+            // ---- S_{c+1} = M_c S_c + b_c (the sequential path)
+            if (ok && scan_aborted(ms)) ok = false;
+            if (ok && (!mbar_wait(&ms.mma_s, c & 1, kWaitNs) || !mbar_wait(&ms.full_bo[s], (c >> 1) & 1, kWaitNs)))
+                ok = false;
+            ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: the warp loads or skips together
+            if (ok) {
+                tc_fence_after();
+                float d[32];
+                tmem_ld32(tmem_addr(tm, 32 * warp, 0), d);
+                tmem_ld_wait();
 #pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4) {
-                float4 bb = *reinterpret_cast<const float4*>(st + S_OFF_B + f32blk_offset(dk, q4));
-                if (transition) bb = make_float4(0.f, 0.f, 0.f, 0.f);
-                S[4 * q4] = d[4 * q4] + bb.x;
-                S[4 * q4 + 1] = d[4 * q4 + 1] + bb.y;
-                S[4 * q4 + 2] = d[4 * q4 + 2] + bb.z;
-                S[4 * q4 + 3] = d[4 * q4 + 3] + bb.w;
+                for (int q4 = 0; q4 < 8; ++q4) {
+                    float4 bb = *reinterpret_cast<const float4*>(st + S_OFF_B + f32blk_offset(dk, q4));
+                    if (transition) bb = make_float4(0.f, 0.f, 0.f, 0.f);
+                    S[4 * q4] = d[4 * q4] + bb.x;
+                    S[4 * q4 + 1] = d[4 * q4 + 1] + bb.y;
+                    S[4 * q4 + 2] = d[4 * q4 + 2] + bb.z;
+                    S[4 * q4 + 3] = d[4 * q4 + 3] + bb.w;
+                }
             }
-            if (c + 1 < p.NC) {  // tile (c+1) % 2 was last read by chunk c-1's MMAs, all complete
+            if (c + 1 < p.NC) {
+                if (ok) {  // tile (c+1) % 2 was last read by chunk c-1's MMAs, complete before chunk c's state product
 #pragma unroll
-                for (int q8 = 0; q8 < kTcDvTile / 8; ++q8)
-                    store_bf16x8(stile + (s ^ 1) * 16384, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
-                fence_proxy_async_smem();
+                    for (int q8 = 0; q8 < kTcDvTile / 8; ++q8)
+                        store_bf16x8(stile + (s ^ 1) * 16384, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
+                    fence_proxy_async_smem();
+                }
+                tc_fence_before();
+                named_bar_arrive(kScanBarS, kScanBarCount);
             }
-            tc_fence_before();
-        }
-        if (ok) {
-            const int sp = (p.NC - 1) & 1;
-            if (mbar_wait(&ms.mma_o[sp], ((p.NC - 1) >> 1) & 1, kWaitNs)) {
+            // ---- outputs of chunk c, overlapping chunk c+1's MMAs
+            if (ok && !mbar_wait(&ms.mma_o[s], (c >> 1) & 1, kWaitNs)) ok = false;
+            ok = __all_sync(0xffffffffu, ok);
+            if (ok) {
                 tc_fence_after();
                 float o[32];
-                tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + sp)), o);
+                tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + s)), o);
                 tmem_ld_wait();
-                if (!summary) scan_store_output(p, sm + sp * S_STAGE, o, p.NC - 1, warp, lane, b, h, dv0);
-                mbar_arrive(&ms.empty_bo[sp]);
-            } else {
-                ok = false;
+                if (!summary) scan_store_output(p, st, o, c, warp, lane, b, h, dv0);
+                tc_fence_before();
             }
-            float* dst = summary ? (transition ? p.hT : p.hT2) : p.hT;
-            if (ok && dst) {
+            if (!ok) ms.abort = 1;
+            mbar_arrive(&ms.empty_bo[s]);
+        }
+        float* dst = summary ? (transition ? p.hT : p.hT2) : p.hT;
+        if (ok && dst) {
 #pragma unroll
-                for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
-                    *reinterpret_cast<float4*>(dst + srow + 4 * q4) =
-                        make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
-            }
+            for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
+                *reinterpret_cast<float4*>(dst + srow + 4 * q4) =
+                    make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
         }
     }
     if (!ok) {
