@@ -23,13 +23,15 @@
 // one CTA's memory and barrier waits overlap the other's work; the output images
 // leave with asynchronous bulk copies.  Operands that share a B matrix are
 // stacked into M=128 MMAs so every accumulator fills all 128 TMEM lanes.
-//   1. rows of q, k, v -> l2norm (16-bit rounding as the reference) -> bf16
-//      128B-swizzled tiles [k^; q^] and v in shared memory
+//   1. rows of q, k, v (cp.async-staged at entry, all in flight at once) ->
+//      l2norm (16-bit rounding as the reference) -> bf16 128B-swizzled tiles
+//      [k^; q^] and v in shared memory
 //   2. [k^; q^] k^T on the tensor cores -> G_k (lanes 0-63) and G_q (64-127)
 //   3. L = -(beta G_k e^(gc_i-gc_j)) strictly lower, Aqk = Dk^-1/2 G_q e^(gc_i-gc_j) causal
 //   4. T = (I - L)^-1 in 16x16 blocks (diagonal blocks by substitution, then
 //      the off-diagonal blocks by distance)
-//   5. X = E_d T B_e, Y = E_d T B, W = Aqk T B, Z = Aqk T B_e  (64x64, fp32)
+//   5. Aqk T on the tensor cores (M=64, N=64, K=64, hi/lo operands); then
+//      X = E_d T B_e, Y = E_d T B, W = Aqk T B, Z = Aqk T B_e  (64x64, fp32)
 //   6. [X; Z] k^ -> P_X | Zk, then [Y; W] v -> P_Y | o0  (M=128, N=128, K=64, hi+lo)
 //   7. Q' = q^ e^gc Dk^-1/2 - Zk, o0 -> workspace; P_X, P_Y -> hi+lo B tiles
 //   8. M' = k^T P_X, b = k^T P_Y (M=128, N=128, K=64, hi+lo)
@@ -77,11 +79,13 @@ constexpr uint32_t P_KQ = 0;               // bf16 [128 rows][128] swizzled: row
 constexpr uint32_t P_V = 32768;            // bf16 [64 rows][128] swizzled v (atom columns 8 KiB apart)
 constexpr uint32_t P_W = 49152;            // work region, reused phase by phase:
 constexpr int kLd = 68;                    //   fp32 row stride of T (16-byte rows for float4 reads)
-constexpr int kSLd = 65;                   //   odd stride of L and Aqk (scalar access only)
-constexpr uint32_t P_L = P_W;              //   steps 3-4: L   fp32 [64][65]
-constexpr uint32_t P_AQK = P_W + 16640;    //   steps 3-5: Aqk fp32 [64][65]
-constexpr uint32_t P_T = P_W + 33280;      //   steps 4-5: T   fp32 [64][68]
-constexpr uint32_t P_Y3 = P_W + 50688;     //   step 4: fp32 [3][16][16] scratch of the blocked inverse
+constexpr int kSLd = 65;                   //   odd stride of L (scalar access only)
+constexpr uint32_t P_RAW = P_W;            //   step 1: raw q/k/v rows, [3][64][256 B] (48 KiB)
+constexpr uint32_t P_AQK = P_W;            //   steps 3-5: Aqk as hi/lo bf16 A tiles [64][64] (2 x 8 KiB)
+constexpr uint32_t P_L = P_W + 16384;      //   steps 3-4: L   fp32 [64][65]
+constexpr uint32_t P_TT = P_W + 16384;     //   step 5: T as hi/lo bf16 B tiles [64][64] (2 x 8 KiB; L is dead)
+constexpr uint32_t P_T = P_W + 33024;      //   steps 4-5: T   fp32 [64][68]
+constexpr uint32_t P_Y3 = P_W + 50432;     //   step 4: fp32 [3][16][16] scratch of the blocked inverse
 constexpr uint32_t P_ATILE = P_W;          //   step 6: [X;Z] then [Y;W] hi/lo A tiles (2 x 16 KiB)
 constexpr uint32_t P_PX = P_W;             //   steps 7-8: P_X hi/lo B tiles (2 x 16 KiB)
 constexpr uint32_t P_PYH = P_V;            //   steps 7-8: P_Y hi (v is dead after step 6)
@@ -90,6 +94,7 @@ constexpr uint32_t P_MISC = P_W + 53760;
 constexpr uint32_t P_SMEM = P_MISC + 1088 + 1024;  // + alignment slack
 constexpr uint32_t kPrepTmemCols = 256;
 static_assert(P_Y3 + 3072 <= P_MISC, "work region");
+static_assert(P_L + 64 * kSLd * 4 <= P_T && P_RAW + 3 * 64 * 256 <= P_MISC, "work region");
 static_assert(P_PYL + 16384 <= P_MISC, "work region");
 
 struct PrepMisc {
@@ -133,10 +138,8 @@ __device__ __forceinline__ uint32_t f32blk_offset(int row, int chunk4) {
     return (uint32_t)row * 128u + (uint32_t)((chunk4 ^ (row & 7)) * 16);
 }
 
-__device__ __forceinline__ void load_bf16x4(const View4& v, int b, int64_t t, int h, int lane, float (&x)[4]) {
-    const __nv_bfloat16* p =
-        reinterpret_cast<const __nv_bfloat16*>(v.p) + (int64_t)b * v.sb + t * v.st + (int64_t)h * v.sh + 4 * lane;
-    const uint2 u = *reinterpret_cast<const uint2*>(p);
+__device__ __forceinline__ void load_bf16x4_smem(const unsigned char* src, float (&x)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(src);
     const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
     const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
     x[0] = __low2float(lo);
@@ -162,7 +165,6 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     PrepMisc& ms = *reinterpret_cast<PrepMisc*>(sm + P_MISC);
     float(*sL)[kSLd] = reinterpret_cast<float(*)[kSLd]>(sm + P_L);
-    float(*sA)[kSLd] = reinterpret_cast<float(*)[kSLd]>(sm + P_AQK);
     float(*sT)[kLd] = reinterpret_cast<float(*)[kLd]>(sm + P_T);
     float(*sY)[16][16] = reinterpret_cast<float(*)[16][16]>(sm + P_Y3);
 
@@ -176,6 +178,18 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     const float scale = rsqrtf((float)kDk);
     unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
 
+    // raw q/k/v rows of the chunk into the (still unused) work region, all in flight at once:
+    // 3 x 64 rows x 16 pieces of 16 bytes, 12 per thread; rows past T are zero-filled
+    for (int i = tid; i < 3 * kChunk * 16; i += kPrepThreads) {
+        const int tsr = i >> 10, row = (i >> 4) & 63, piece = i & 15;
+        const View4& V = tsr == 0 ? p.q : (tsr == 1 ? p.k : p.v);
+        const int64_t t = t0 + row;
+        const bool in = t < p.T;
+        const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(V.p) + (int64_t)b * V.sb +
+                                   (in ? t : t0) * V.st + (int64_t)h * V.sh + 8 * piece;
+        cp_async16(sm + P_RAW + (tsr * kChunk + row) * 256 + piece * 16, src, in ? 16u : 0u);
+    }
+    cp_async_commit();
     if (warp == 0) {
         tmem_alloc(&ms.tmem, kPrepTmemCols);
         tmem_relinquish();
@@ -195,9 +209,11 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         ms.beta[tid] = bv;
     }
 
+    cp_async_wait_all();
+    __syncthreads();
     // ---- 1. normalised rows -> swizzled bf16 tiles (qwen3_5_transformers.py:122-137).
-    //      Each warp owns 8 rows, in two batches of 4 whose 12 row loads are issued together; the 8
-    //      sums of squares of a batch are reduced together.  The inverse norm uses rsqrtf before its
+    //      Each warp owns 8 rows of the staged copy, in two batches of 4 whose 8 sums of squares
+    //      are reduced together.  The inverse norm uses rsqrtf before its
     //      bf16 rounding: it differs from a correctly rounded 1/sqrt only within ~2 fp32 ulp of a bf16
     //      rounding boundary (the reference's own CPU bf16 rsqrt is an estimate as well).
 #pragma unroll
@@ -206,15 +222,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         float q[kRows][4], k[kRows][4], v[kRows][4], ss[2 * kRows];
 #pragma unroll
         for (int rr = 0; rr < kRows; ++rr) {
-            const int64_t t = t0 + warp + 8 * (4 * batch + rr);
-            if (t < p.T) {
-                load_bf16x4(p.q, b, t, h, lane, q[rr]);
-                load_bf16x4(p.k, b, t, h, lane, k[rr]);
-                load_bf16x4(p.v, b, t, h, lane, v[rr]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) q[rr][e] = k[rr][e] = v[rr][e] = 0.f;
-            }
+            const int row = warp + 8 * (4 * batch + rr);
+            load_bf16x4_smem(sm + P_RAW + (0 * kChunk + row) * 256 + 8 * lane, q[rr]);
+            load_bf16x4_smem(sm + P_RAW + (1 * kChunk + row) * 256 + 8 * lane, k[rr]);
+            load_bf16x4_smem(sm + P_RAW + (2 * kChunk + row) * 256 + 8 * lane, v[rr]);
         }
 #pragma unroll
         for (int rr = 0; rr < kRows; ++rr) {
@@ -299,12 +310,16 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
                 const int j = 32 * half + e;
                 sL[i][j] = (j < i) ? -(bi * gv[e]) * __expf(gci - ms.gc[j]) : 0.f;
             }
-        } else {
+        } else {  // Aqk rows as the hi/lo bf16 A operand of step 5 (K-major, one atom column)
+            float a[32];
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
                 const int j = 32 * half + e;
-                sA[i][j] = (j <= i) ? (scale * gv[e]) * __expf(gci - ms.gc[j]) : 0.f;
+                a[e] = (j <= i) ? (scale * gv[e]) * __expf(gci - ms.gc[j]) : 0.f;
             }
+#pragma unroll
+            for (int q8 = 0; q8 < 4; ++q8)
+                store_split8(sm + P_AQK, sm + P_AQK + 8192, sw128_offset(i, 32 * half + 8 * q8, 64), a + 8 * q8);
         }
     } else {
         ok = false;
@@ -418,57 +433,83 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     }
     __syncthreads();
 
-    // ---- 5. the four 64x64 coefficient matrices X = E_d T B_e, Y = E_d T B, W = (Aqk T) B, Z = (Aqk T) B_e.
-    //      Thread (row i, 16 columns) keeps T's row and (Aqk T)'s row in registers: once every thread has
-    //      read them, the work region is free for the A tiles.
-    float ti[16], at[16];
-    const int ri = tid & 63, j0 = (tid >> 6) * 16;
+    // ---- 5. (Aqk T) on the tensor core: T -> hi/lo B tiles over L (dead), then three M=64, N=64, K=64
+    //      passes (hi.hi + hi.lo + lo.hi) into TMEM cols [0,64) (G is dead).  Rows of the M=64
+    //      accumulator sit in lanes 0-15 of each 32-lane quadrant.
     if (ok) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) at[e] = 0.f;
-        for (int m = j0; m <= ri; ++m) {  // (Aqk T)[i][j] = sum_{m=j..i} Aqk[i][m] T[m][j]
-            const float a = sA[ri][m];
-#pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-                const float4 tv = *reinterpret_cast<const float4*>(&sT[m][j0 + 4 * e4]);
-                at[4 * e4] += a * tv.x;
-                at[4 * e4 + 1] += a * tv.y;
-                at[4 * e4 + 2] += a * tv.z;
-                at[4 * e4 + 3] += a * tv.w;
-            }
-        }
+        const int m = tid >> 2, c0 = 16 * (tid & 3);
+        float tv[16];
 #pragma unroll
         for (int e4 = 0; e4 < 4; ++e4) {
-            const float4 tv = *reinterpret_cast<const float4*>(&sT[ri][j0 + 4 * e4]);
-            ti[4 * e4] = tv.x;
-            ti[4 * e4 + 1] = tv.y;
-            ti[4 * e4 + 2] = tv.z;
-            ti[4 * e4 + 3] = tv.w;
+            const float4 x = *reinterpret_cast<const float4*>(&sT[m][c0 + 4 * e4]);
+            tv[4 * e4] = x.x;
+            tv[4 * e4 + 1] = x.y;
+            tv[4 * e4 + 2] = x.z;
+            tv[4 * e4 + 3] = x.w;
+        }
+#pragma unroll
+        for (int h8 = 0; h8 < 2; ++h8)
+            store_split8(sm + P_TT, sm + P_TT + 8192, sw128_offset(m, c0 + 8 * h8, 64), tv + 8 * h8);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (ok && tid == 0) {
+        tc_fence_after();
+        const uint32_t id = make_idesc_f16(64, 64, false, true, true);
+        const uint32_t ah = sbase + P_AQK, al = ah + 8192, bh = sbase + P_TT, bl = bh + 8192;
+        const uint32_t as[3] = {ah, ah, al}, bs[3] = {bh, bl, bh};
+#pragma unroll
+        for (int pass = 0; pass < 3; ++pass)
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+                mma_f16(tm, make_sdesc(as[pass] + ks * 32, 16, 1024, kSwizzle128B),
+                        make_sdesc(bs[pass] + ks * 2048, 8192, 1024, kSwizzle128B), id, (pass | ks) != 0);
+        mma_commit(&ms.bar);
+    }
+    if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);  // second completion of the barrier
+    ok = !__syncthreads_or(!ok);
+    tc_fence_after();
+    // Thread (quadrant, lane, half) holds 32 columns jc.. of one coefficient row ri: lanes 16-31 the row
+    // of T (-> X, Y), lanes 0-15 the row of Aqk T (-> Z, W).
+    const bool top = lane >= 16;
+    const int ri = 16 * quad + (lane & 15), jc = 32 * half;
+    float cv[32];
+    if (ok) {
+        tmem_ld32(tmem_addr(tm, 32 * quad, jc), cv);
+        tmem_ld_wait();
+        if (top) {
+#pragma unroll
+            for (int e4 = 0; e4 < 8; ++e4) {
+                const float4 x = *reinterpret_cast<const float4*>(&sT[ri][jc + 4 * e4]);
+                cv[4 * e4] = x.x;
+                cv[4 * e4 + 1] = x.y;
+                cv[4 * e4 + 2] = x.z;
+                cv[4 * e4 + 3] = x.w;
+            }
         }
     }
-    __syncthreads();
-    const float ekdi = ms.ekd[ri];
-    // ---- 6. two M=128, N=128, K=64 rounds (hi+lo): [X;Z] k^ -> cols [0,128) (P_X | Zk), then
+    tc_fence_before();
+    __syncthreads();  // the tiles of step 5 are read: the work region is free for the A tiles
+    // ---- 6. the four 64x64 coefficient matrices X = E_d T B_e, Y = E_d T B, W = (Aqk T) B, Z = (Aqk T) B_e,
+    //      in two M=128, N=128, K=64 rounds (hi+lo): [X;Z] k^ -> cols [0,128) (P_X | Zk), then
     //      [Y;W] v -> cols [128,256) (P_Y | o0), the A tiles of the second round written over the first's.
     const uint32_t id6 = make_idesc_f16(128, 128, false, true, true);
-    uint32_t ph = 0;
+    const float rowc = top ? ms.ekd[ri] : 1.f;
+    uint32_t ph = 1;
     for (int round = 0; round < 2 && ok; ++round) {
-        float top[16], bot[16];  // rows i (X or Y) and 64+i (Z or W)
+        float x[32];  // row ri (X or Y) or 64+ri (Z or W)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            const int j = j0 + e;
-            const float bj = ms.beta[j], bej = bj * ms.egc[j];
-            const float bb = round == 0 ? bej : bj;
-            top[e] = ekdi * ti[e] * bb;
-            bot[e] = at[e] * bb;
+        for (int e = 0; e < 32; ++e) {
+            const int j = jc + e;
+            const float bj = ms.beta[j];
+            const float bb = round == 0 ? bj * ms.egc[j] : bj;
+            x[e] = rowc * cv[e] * bb;
         }
         unsigned char* at_hi = sm + P_ATILE;
         unsigned char* at_lo = sm + P_ATILE + 16384;
 #pragma unroll
-        for (int h8 = 0; h8 < 2; ++h8) {
-            store_split8(at_hi, at_lo, sw128_offset(ri, j0 + 8 * h8, 128), top + 8 * h8);
-            store_split8(at_hi, at_lo, sw128_offset(64 + ri, j0 + 8 * h8, 128), bot + 8 * h8);
-        }
+        for (int q8 = 0; q8 < 4; ++q8)
+            store_split8(at_hi, at_lo, sw128_offset(top ? ri : 64 + ri, jc + 8 * q8, 128), x + 8 * q8);
         fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
@@ -557,7 +598,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         }
         mma_commit(&ms.bar);
     }
-    if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);  // fourth completion of the barrier
+    if (ok) ok = mbar_wait(&ms.bar, 0, kWaitNs);  // fifth completion of the barrier
     if (tid == 32) bulk_wait_read_all();       // KQ is rewritten below: the Q' copy must have read it
     tc_fence_after();
 
