@@ -357,79 +357,73 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         }
     }
     __syncthreads();
-    if (ok) {  // distance 1: Y_c = L_{c+1,c} T_cc
-        for (int o = tid; o < 768; o += kPrepThreads) {
-            const int cb = o >> 8, i = (o >> 4) & 15, j = o & 15;
-            float s0 = 0.f, s1 = 0.f;
+    // Off-diagonal blocks, each output a 1x4 register tile (row i, columns jg..jg+3): one L load and one
+    // float4 T load per four FMAs.  sY holds 16x16 fp32 blocks.
+    auto f4fma = [](float4& acc, float a, const float4 t) {
+        acc.x += a * t.x;
+        acc.y += a * t.y;
+        acc.z += a * t.z;
+        acc.w += a * t.w;
+    };
+    const int mi = (tid >> 2) & 15, mj = 4 * (tid & 3), mg = tid >> 6;  // row, column group, block of a thread
+    if (ok && mg < 3) {  // distance 1: Y_c = L_{c+1,c} T_cc, c = mg
+        const int ro = 16 * (mg + 1), co = 16 * mg;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int m = 0; m < 16; m += 2) {
-                s0 += sL[16 * (cb + 1) + i][16 * cb + m] * sT[16 * cb + m][16 * cb + j];
-                s1 += sL[16 * (cb + 1) + i][16 * cb + m + 1] * sT[16 * cb + m + 1][16 * cb + j];
-            }
-            sY[cb][i][j] = s0 + s1;
-        }
+        for (int m = 0; m < 16; ++m)
+            f4fma(acc, sL[ro + mi][co + m], *reinterpret_cast<const float4*>(&sT[co + m][co + mj]));
+        *reinterpret_cast<float4*>(&sY[mg][mi][mj]) = acc;
     }
     __syncthreads();
-    if (ok) {  // T_{c+1,c} = T_{c+1,c+1} Y_c
-        for (int o = tid; o < 768; o += kPrepThreads) {
-            const int cb = o >> 8, i = (o >> 4) & 15, j = o & 15, rb = 16 * (cb + 1);
-            float s0 = 0.f, s1 = 0.f;
+    if (ok && mg < 3) {  // T_{c+1,c} = T_{c+1,c+1} Y_c
+        const int ro = 16 * (mg + 1), co = 16 * mg;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int m = 0; m < 16; m += 2) {
-                s0 += sT[rb + i][rb + m] * sY[cb][m][j];
-                s1 += sT[rb + i][rb + m + 1] * sY[cb][m + 1][j];
-            }
-            sT[rb + i][16 * cb + j] = s0 + s1;
-        }
+        for (int m = 0; m < 16; ++m)
+            f4fma(acc, sT[ro + mi][ro + m], *reinterpret_cast<const float4*>(&sY[mg][m][mj]));
+        *reinterpret_cast<float4*>(&sT[ro + mi][co + mj]) = acc;
     }
     __syncthreads();
-    if (ok) {  // distance 2: Y_c = L_{c+2,c} T_cc + L_{c+2,c+1} T_{c+1,c}
-        for (int o = tid; o < 512; o += kPrepThreads) {
-            const int cb = o >> 8, i = (o >> 4) & 15, j = o & 15, rb = 16 * (cb + 2);
-            float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-            for (int m = 0; m < 16; ++m) {
-                s0 += sL[rb + i][16 * cb + m] * sT[16 * cb + m][16 * cb + j];
-                s1 += sL[rb + i][16 * (cb + 1) + m] * sT[16 * (cb + 1) + m][16 * cb + j];
-            }
-            sY[cb][i][j] = s0 + s1;
-        }
-    }
-    __syncthreads();
-    if (ok) {  // T_{c+2,c} = T_{c+2,c+2} Y_c
-        for (int o = tid; o < 512; o += kPrepThreads) {
-            const int cb = o >> 8, i = (o >> 4) & 15, j = o & 15, rb = 16 * (cb + 2);
-            float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-            for (int m = 0; m < 16; m += 2) {
-                s0 += sT[rb + i][rb + m] * sY[cb][m][j];
-                s1 += sT[rb + i][rb + m + 1] * sY[cb][m + 1][j];
-            }
-            sT[rb + i][16 * cb + j] = s0 + s1;
-        }
-    }
-    __syncthreads();
-    if (ok) {  // distance 3: Y = sum_{k<3} L_{3,k} T_{k,0}
-        const int i = tid >> 4, j = tid & 15;
-        float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+    if (ok && mg < 2) {  // distance 2: Y_c = L_{c+2,c} T_cc + L_{c+2,c+1} T_{c+1,c}, c = mg
+        const int ro = 16 * (mg + 2), co = 16 * mg;
+        float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
-            s0 += sL[48 + i][m] * sT[m][j];
-            s1 += sL[48 + i][16 + m] * sT[16 + m][j];
-            s2 += sL[48 + i][32 + m] * sT[32 + m][j];
+            f4fma(acc0, sL[ro + mi][co + m], *reinterpret_cast<const float4*>(&sT[co + m][co + mj]));
+            f4fma(acc1, sL[ro + mi][co + 16 + m], *reinterpret_cast<const float4*>(&sT[co + 16 + m][co + mj]));
         }
-        sY[0][i][j] = s0 + s1 + s2;
+        *reinterpret_cast<float4*>(&sY[mg][mi][mj]) =
+            make_float4(acc0.x + acc1.x, acc0.y + acc1.y, acc0.z + acc1.z, acc0.w + acc1.w);
     }
     __syncthreads();
-    if (ok) {  // T_{3,0} = T_33 Y
-        const int i = tid >> 4, j = tid & 15;
-        float s0 = 0.f, s1 = 0.f;
+    if (ok && mg < 2) {  // T_{c+2,c} = T_{c+2,c+2} Y_c
+        const int ro = 16 * (mg + 2), co = 16 * mg;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int m = 0; m < 16; m += 2) {
-            s0 += sT[48 + i][48 + m] * sY[0][m][j];
-            s1 += sT[48 + i][48 + m + 1] * sY[0][m + 1][j];
+        for (int m = 0; m < 16; ++m)
+            f4fma(acc, sT[ro + mi][ro + m], *reinterpret_cast<const float4*>(&sY[mg][m][mj]));
+        *reinterpret_cast<float4*>(&sT[ro + mi][co + mj]) = acc;
+    }
+    __syncthreads();
+    if (ok && mg < 3) {  // distance 3: the three terms L_{3,k} T_{k,0}, k = mg, summed in the next stage
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+            f4fma(acc, sL[48 + mi][16 * mg + m], *reinterpret_cast<const float4*>(&sT[16 * mg + m][mj]));
+        *reinterpret_cast<float4*>(&sY[mg][mi][mj]) = acc;
+    }
+    __syncthreads();
+    if (ok && mg == 0) {  // T_{3,0} = T_33 (Y_0 + Y_1 + Y_2)
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            const float4 y0 = *reinterpret_cast<const float4*>(&sY[0][m][mj]);
+            const float4 y1 = *reinterpret_cast<const float4*>(&sY[1][m][mj]);
+            const float4 y2 = *reinterpret_cast<const float4*>(&sY[2][m][mj]);
+            f4fma(acc, sT[48 + mi][48 + m],
+                  make_float4(y0.x + y1.x + y2.x, y0.y + y1.y + y2.y, y0.z + y1.z + y2.z, y0.w + y1.w + y2.w));
         }
-        sT[48 + i][j] = s0 + s1;
+        *reinterpret_cast<float4*>(&sT[48 + mi][mj]) = acc;
     }
     __syncthreads();
 
