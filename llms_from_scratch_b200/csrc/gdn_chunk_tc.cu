@@ -170,9 +170,13 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int quad = warp & 3, half = warp >> 2;  // TMEM lane quadrant, column half
-    const int64_t chunk = blockIdx.x;
-    const int c = (int)(chunk % p.NC);
-    const int bh = (int)(chunk / p.NC);
+    // Chunks run latest first across all heads (block i -> chunk NC-1 - i/(B*H)), so the records the scan
+    // reads first are the ones written last, still in L2 when the scan starts (a long sequence's records
+    // do not all fit).
+    const int BH = p.B * p.H;
+    const int c = p.NC - 1 - (int)(blockIdx.x / BH);
+    const int bh = (int)(blockIdx.x % BH);
+    const int64_t chunk = (int64_t)bh * p.NC + c;  // record index
     const int b = bh / p.H, h = bh % p.H;
     const int64_t t0 = (int64_t)c * kChunk;
     const float scale = rsqrtf((float)kDk);
