@@ -67,4 +67,13 @@ __device__ __forceinline__ float l2norm_inv(const float (&x)[4], int dtype) {
     return round_to(1.0f / sqrtf(s), dtype);
 }
 
+// 16-byte asynchronous global -> shared copy and its group commit / wait (cp.async; CUDA-core kernels).
+__device__ __forceinline__ void cp_async16_rec(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_rec() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_rec() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 }  // namespace gdn
