@@ -58,6 +58,7 @@ def parse_args():
     ap.add_argument("--sp", action="store_true",
                     help="config 5: one sequence of --sp-T tokens (B=1) split in time across the ranks")
     ap.add_argument("--sp-T", type=int, default=131072)
+    ap.add_argument("--decode-batch", type=int, default=32, help="sequences of the decode-kernel leg")
     return ap.parse_args()
 
 
@@ -434,7 +435,7 @@ def main():
     clocks.stop()
 
     # ---- decode step kernel (config 4 shape, one GatedDeltaNet layer at batch 32)
-    Bd = 32
+    Bd = args.decode_batch
     dq_, dk_, dv_, dg_, db_, dst = make_inputs(torch, Bd, 1, H, seed=99 + rank, device=device)
     dstate = dst.clone()
     for _ in range(5):
