@@ -176,6 +176,42 @@ GDN_API int gdn_recurrent_gated_delta_rule(const gdn_tensor* query, const gdn_te
                                    int output_final_state, int use_qk_l2norm_in_kernel, gdn_tensor* out,
                                    float* final_state, void* stream);
 
+/* GatedDeltaNet layer steps on either side of the rule (Qwen3_5GatedDeltaNet.forward,
+ * qwen3_5_transformers.py:304-419).  Each result is rounded to the layer dtype
+ * as the reference's bf16 torch ops round it.  Views are device memory with a
+ * contiguous last dimension.
+ *
+ * gdn_causal_conv1d_silu replaces the prefill convolution
+ * F.silu(self.conv1d(mixed_qkv)[:, :, :seq_len]) (:356; depthwise Conv1d with
+ * kernel 4, padding 3, no bias, :253-260) and, when conv_state is non-NULL, the
+ * cache's conv state F.pad(mixed_qkv, (4 - seq_len, 0)) (:346-348).
+ *   x [B,T,C]  the in_proj_qkv output, token-major (the reference transposes it
+ *              to [B,C,T], :334); out [B,T,C] must not alias x; both need
+ *              16-byte aligned rows and C a multiple of 8 (bf16/fp16) or 4 (fp32)
+ *   weight [C,4] (conv1d.weight.squeeze(1)); conv_state [B,C,4] or NULL.
+ * q/k/v are then the channel ranges [0,Dk·H), [Dk·H, 2Dk·H), [2Dk·H, C) of out,
+ * views the chunk entry points take as they are. */
+GDN_API int gdn_causal_conv1d_silu(const gdn_tensor* x, const gdn_tensor* weight, gdn_tensor* out,
+                                   gdn_tensor* conv_state, void* stream);
+
+/* Decode convolution: replaces torch_causal_conv1d_update(x, conv_state, weight,
+ * None, "silu") (:85-101).  x [B,T,C] (T new tokens, token-major), conv_state
+ * [B,C,4] read and updated in place, weight [C,4], out [B,T,C]. */
+GDN_API int gdn_causal_conv1d_update(const gdn_tensor* x, gdn_tensor* conv_state, const gdn_tensor* weight,
+                                     gdn_tensor* out, void* stream);
+
+/* Gates: replaces beta = b.sigmoid() and g = -A_log.float().exp() *
+ * F.softplus(a.float() + dt_bias) (:377-379).  a, b, g, beta [B,T,H]; A_log,
+ * dt_bias [H] (one dtype).  g is computed in fp32 and beta rounded to beta's
+ * dtype (the reference keeps it in b's dtype). */
+GDN_API int gdn_gates(const gdn_tensor* a, const gdn_tensor* b, const gdn_tensor* A_log, const gdn_tensor* dt_bias,
+                      gdn_tensor* g, gdn_tensor* beta, void* stream);
+
+/* Gated RMS norm: replaces Qwen3_5RMSNormGated.forward(x, gate) (:62-71) over rows
+ * of 128 (head_v_dim).  x, gate, out [N,128]; weight [128]; one dtype. */
+GDN_API int gdn_rms_norm_gated(const gdn_tensor* x, const gdn_tensor* gate, const gdn_tensor* weight, float eps,
+                               gdn_tensor* out, void* stream);
+
 /* Instrumentation (no counterpart in the reference, which times whole calls
  * with CUDA events, benchmark.py:82-100).
  *

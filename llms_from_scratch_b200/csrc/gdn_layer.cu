@@ -1,0 +1,460 @@
+// GatedDeltaNet layer steps on either side of the gated delta rule
+// (Qwen3_5GatedDeltaNet.forward, qwen3_5_transformers.py:304-419):
+//   * the prefill causal depthwise conv1d (kernel 4) + SiLU over the mixed q/k/v
+//     projection, and the conv state the cache keeps (:346-356);
+//   * the decode convolution against that state, torch_causal_conv1d_update (:85-101);
+//   * the gates beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias) (:377-379);
+//   * the gated RMS norm after the rule, Qwen3_5RMSNormGated (:56-71).
+// All four are HBM-bound elementwise/row passes.  The convolutions read the
+// projection in its token-major [B,T,C] layout (the reference transposes it to
+// [B,C,T] for torch's conv1d, :334, and back, :358) and write the conv output in
+// the same layout, so q/k/v are strided views of it that the chunk kernels take
+// without a copy.  Each thread owns 16 bytes of channels (8 bf16) and walks a run
+// of tokens with the three previous inputs in registers.
+//
+// Numerics follow the reference's bf16 ops, each result rounded to the layer
+// dtype once: the conv sum (four exact bf16 products, accumulated in double in
+// tap order), then SiLU in fp32; the norm's mean of squares in double, IEEE sqrt
+// and division, then the three roundings of Qwen3_5RMSNormGated.
+#include "gdn_common.cuh"
+#include "gdn_internal.h"
+
+namespace gdn {
+namespace {
+
+constexpr int kConvK = 4;          // linear_conv_kernel_dim of Qwen3.5
+constexpr int kConvThreads = 128;  // channel groups per CTA
+constexpr int kConvTokens = 16;    // tokens per thread (prefill)
+
+struct ConvParams {
+    const void* x;       // [B,T,C], channels contiguous
+    int64_t x_sb, x_st;
+    const void* w;       // [C,K], row stride w_sc
+    int64_t w_sc;
+    void* out;           // [B,T,C], channels contiguous
+    int64_t o_sb, o_st;
+    void* state;         // [B,C,K] conv state (prefill: written; update: read and written); may be null
+    int64_t s_sb, s_sc;
+    int B, C;
+    int64_t T;
+    int dtype;           // of x, w, out and state
+};
+
+template <typename E> struct Elem;
+template <> struct Elem<__nv_bfloat16> {
+    static __device__ __forceinline__ float ld(const __nv_bfloat16& v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 st(float x) { return __float2bfloat16_rn(x); }
+    static __device__ __forceinline__ float rnd(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+};
+template <> struct Elem<__half> {
+    static __device__ __forceinline__ float ld(const __half& v) { return __half2float(v); }
+    static __device__ __forceinline__ __half st(float x) { return __float2half_rn(x); }
+    static __device__ __forceinline__ float rnd(float x) { return __half2float(__float2half_rn(x)); }
+};
+template <> struct Elem<float> {
+    static __device__ __forceinline__ float ld(const float& v) { return v; }
+    static __device__ __forceinline__ float st(float x) { return x; }
+    static __device__ __forceinline__ float rnd(float x) { return x; }
+};
+
+// F.silu on a tensor of the layer dtype: computed in fp32, rounded once.
+template <typename E>
+__device__ __forceinline__ float silu_rounded(float y) {
+    return Elem<E>::rnd(y / (1.0f + expf(-y)));
+}
+
+// conv output of one channel: sum_j w_j x_j (exact products, double accumulation in tap order),
+// rounded to the layer dtype, then SiLU rounded again (:356 / :97-98).
+template <typename E>
+__device__ __forceinline__ float conv_silu(const float (&w)[kConvK], float x0, float x1, float x2, float x3) {
+    double acc = 0.0;
+    acc += (double)w[0] * (double)x0;
+    acc += (double)w[1] * (double)x1;
+    acc += (double)w[2] * (double)x2;
+    acc += (double)w[3] * (double)x3;
+    return silu_rounded<E>(Elem<E>::rnd((float)acc));
+}
+
+// Prefill: thread = V consecutive channels x kConvTokens tokens.  16-byte loads and stores of the
+// channel vector per token; the three inputs before the run come from the previous tokens (zero
+// before t = 0, the conv's left padding).
+template <typename E>
+__global__ void __launch_bounds__(kConvThreads) gdn_conv_silu_kernel(ConvParams p) {
+    constexpr int V = 16 / sizeof(E);
+    using Vec = uint4;
+    const int cg = blockIdx.x * kConvThreads + threadIdx.x;
+    const int c0 = cg * V;
+    if (c0 >= p.C) return;
+    const int b = blockIdx.z;
+    const int64_t t0 = (int64_t)blockIdx.y * kConvTokens;
+    if (t0 >= p.T) return;
+
+    float w[V][kConvK];
+    const E* wp = reinterpret_cast<const E*>(p.w);
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+#pragma unroll
+        for (int j = 0; j < kConvK; ++j) w[i][j] = Elem<E>::ld(wp[(int64_t)(c0 + i) * p.w_sc + j]);
+
+    const E* xb = reinterpret_cast<const E*>(p.x) + (int64_t)b * p.x_sb + c0;
+    E* ob = reinterpret_cast<E*>(p.out) + (int64_t)b * p.o_sb + c0;
+    float win[kConvK - 1][V];  // inputs t-3, t-2, t-1
+#pragma unroll
+    for (int k = 0; k < kConvK - 1; ++k) {
+        const int64_t t = t0 - (kConvK - 1) + k;
+        if (t >= 0) {
+            const Vec u = *reinterpret_cast<const Vec*>(xb + t * p.x_st);
+            const E* e = reinterpret_cast<const E*>(&u);
+#pragma unroll
+            for (int i = 0; i < V; ++i) win[k][i] = Elem<E>::ld(e[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < V; ++i) win[k][i] = 0.f;
+        }
+    }
+    const int64_t t1 = (t0 + kConvTokens < p.T) ? t0 + kConvTokens : p.T;
+    for (int64_t t = t0; t < t1; ++t) {
+        const Vec u = *reinterpret_cast<const Vec*>(xb + t * p.x_st);
+        const E* e = reinterpret_cast<const E*>(&u);
+        Vec r;
+        E* re = reinterpret_cast<E*>(&r);
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            const float xi = Elem<E>::ld(e[i]);
+            re[i] = Elem<E>::st(conv_silu<E>(w[i], win[0][i], win[1][i], win[2][i], xi));
+            win[0][i] = win[1][i];
+            win[1][i] = win[2][i];
+            win[2][i] = xi;
+        }
+        *reinterpret_cast<Vec*>(ob + t * p.o_st) = r;
+    }
+    // the cache's conv state: the last K raw inputs, zero-padded on the left when T < K (:346-348)
+    if (p.state && blockIdx.y == gridDim.y - 1) {
+        E* sb = reinterpret_cast<E*>(p.state) + (int64_t)b * p.s_sb;
+#pragma unroll
+        for (int k = 0; k < kConvK; ++k) {
+            const int64_t t = p.T - kConvK + k;
+            float v[V];
+            if (t >= 0) {
+                const Vec u = *reinterpret_cast<const Vec*>(xb + t * p.x_st);
+                const E* e = reinterpret_cast<const E*>(&u);
+#pragma unroll
+                for (int i = 0; i < V; ++i) v[i] = Elem<E>::ld(e[i]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < V; ++i) v[i] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < V; ++i) sb[(int64_t)(c0 + i) * p.s_sc + k] = Elem<E>::st(v[i]);
+        }
+    }
+}
+
+// Decode: thread = one (sequence, channel); the K-wide state slides over the T new tokens
+// (torch_causal_conv1d_update: cat([state, x]), keep the last K, conv without padding, :95-98).
+template <typename E>
+__global__ void __launch_bounds__(256) gdn_conv_update_kernel(ConvParams p) {
+    const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    if (i >= (int64_t)p.B * p.C) return;
+    const int b = (int)(i / p.C), c = (int)(i % p.C);
+    const E* wp = reinterpret_cast<const E*>(p.w) + (int64_t)c * p.w_sc;
+    float w[kConvK], s[kConvK];
+    E* sp = reinterpret_cast<E*>(p.state) + (int64_t)b * p.s_sb + (int64_t)c * p.s_sc;
+#pragma unroll
+    for (int j = 0; j < kConvK; ++j) {
+        w[j] = Elem<E>::ld(wp[j]);
+        s[j] = Elem<E>::ld(sp[j]);
+    }
+    const E* xp = reinterpret_cast<const E*>(p.x) + (int64_t)b * p.x_sb + c;
+    E* op = reinterpret_cast<E*>(p.out) + (int64_t)b * p.o_sb + c;
+    for (int64_t t = 0; t < p.T; ++t) {
+        const float xn = Elem<E>::ld(xp[t * p.x_st]);
+        op[t * p.o_st] = Elem<E>::st(conv_silu<E>(w, s[1], s[2], s[3], xn));
+        s[0] = s[1];
+        s[1] = s[2];
+        s[2] = s[3];
+        s[3] = xn;
+    }
+#pragma unroll
+    for (int j = 0; j < kConvK; ++j) sp[j] = Elem<E>::st(s[j]);
+}
+
+struct GateParams {
+    View3 a, b;          // [B,T,H]
+    const void* A_log;   // [H]
+    const void* dt_bias; // [H]
+    int64_t A_st, dt_st;
+    int p_dtype;         // of A_log and dt_bias
+    View3 g, beta;       // outputs: g (any float dtype; fp32 as the reference), beta (b's dtype in the reference)
+    int B, H;
+    int64_t T;
+};
+
+// beta = sigmoid(b) rounded to beta's dtype; g = -exp(A_log) softplus(a + dt_bias) in fp32 (:377-379).
+__global__ void __launch_bounds__(256) gdn_gates_kernel(GateParams p) {
+    const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    if (i >= (int64_t)p.B * p.T * p.H) return;
+    const int h = (int)(i % p.H);
+    const int64_t t = (i / p.H) % p.T;
+    const int b = (int)(i / ((int64_t)p.H * p.T));
+    const float a = load_elem(p.a.p, (int64_t)b * p.a.sb + t * p.a.st + (int64_t)h * p.a.sh, p.a.dtype);
+    const float bb = load_elem(p.b.p, (int64_t)b * p.b.sb + t * p.b.st + (int64_t)h * p.b.sh, p.b.dtype);
+    const float A_log = load_elem(p.A_log, (int64_t)h * p.A_st, p.p_dtype);
+    const float dt = load_elem(p.dt_bias, (int64_t)h * p.dt_st, p.p_dtype);
+    const float x = a + dt;
+    const float sp = x > 20.f ? x : log1pf(expf(x));  // softplus, beta 1, threshold 20
+    store_elem(const_cast<void*>(p.g.p), (int64_t)b * p.g.sb + t * p.g.st + (int64_t)h * p.g.sh, p.g.dtype, -expf(A_log) * sp);
+    store_elem(const_cast<void*>(p.beta.p), (int64_t)b * p.beta.sb + t * p.beta.st + (int64_t)h * p.beta.sh, p.beta.dtype,
+               1.0f / (1.0f + expf(-bb)));
+}
+
+struct NormParams {
+    const void* x;      // [N, D] rows
+    int64_t x_sr;
+    const void* gate;   // [N, D]
+    int64_t g_sr;
+    const void* w;      // [D]
+    void* out;          // [N, D]
+    int64_t o_sr;
+    int64_t N;
+    float eps;
+};
+
+constexpr int kNormD = 128;  // head_v_dim
+
+// Qwen3_5RMSNormGated (:62-71), one warp per row, 4 elements per lane:
+//   n = round(x * rsqrt(mean(x^2) + eps)); wn = round(weight * n); out = round(wn * silu(gate)).
+template <typename E>
+__global__ void __launch_bounds__(256) gdn_rms_norm_gated_kernel(NormParams p) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= p.N) return;
+    const E* xr = reinterpret_cast<const E*>(p.x) + row * p.x_sr + 4 * lane;
+    const E* gr = reinterpret_cast<const E*>(p.gate) + row * p.g_sr + 4 * lane;
+    const E* wr = reinterpret_cast<const E*>(p.w) + 4 * lane;
+    float h[4], z[4], w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        h[e] = Elem<E>::ld(xr[e]);
+        z[e] = Elem<E>::ld(gr[e]);
+        w[e] = Elem<E>::ld(wr[e]);
+    }
+    double ss = 0.0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += (double)h[e] * (double)h[e];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float var = (float)(ss / kNormD);
+    const float inv = 1.0f / sqrtf(var + p.eps);
+    E* orow = reinterpret_cast<E*>(p.out) + row * p.o_sr + 4 * lane;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float n = Elem<E>::rnd(h[e] * inv);
+        const float wn = Elem<E>::rnd(w[e] * n);
+        const float sz = z[e] / (1.0f + expf(-z[e]));
+        orow[e] = Elem<E>::st(wn * sz);
+    }
+}
+
+}  // namespace
+
+
+// ---------------------------------------------------------------------------------------- host side
+
+namespace {
+
+size_t esz(int dtype) { return dtype == GDN_F32 ? 4 : 2; }
+bool float_dtype(int d) { return d == GDN_F32 || d == GDN_BF16 || d == GDN_F16; }
+
+int bad(const char* fmt, const char* name) { return set_last_error(GDN_ERR_INVALID_ARGUMENT, fmt, name); }
+
+// [d0, d1, d2] view with a contiguous last dim (shape checked against `want`, -1 = any).
+int check_view(const char* name, const gdn_tensor* t, int ndim, const int64_t* want) {
+    if (!t) return bad("%s is NULL", name);
+    if (t->ndim != ndim) return set_last_error(GDN_ERR_INVALID_ARGUMENT, "%s must be %d-D, got ndim=%d", name, ndim, t->ndim);
+    if (!float_dtype(t->dtype)) return set_last_error(GDN_ERR_INVALID_ARGUMENT, "%s has unsupported dtype code %d", name, t->dtype);
+    for (int i = 0; i < ndim; ++i) {
+        if (t->shape[i] < 0) return bad("%s has a negative dimension", name);
+        if (want[i] >= 0 && t->shape[i] != want[i])
+            return set_last_error(GDN_ERR_INVALID_ARGUMENT, "%s: dim %d is %lld, expected %lld", name, i,
+                                  (long long)t->shape[i], (long long)want[i]);
+    }
+    if (t->stride[ndim - 1] != 1) return bad("%s: the last dimension must be contiguous", name);
+    int64_t n = 1;
+    for (int i = 0; i < ndim; ++i) n *= t->shape[i];
+    if (n > 0 && !t->data) return bad("%s has a NULL data pointer", name);
+    return GDN_OK;
+}
+
+// The 16-byte vector path of the prefill convolution: base and row strides on 16-byte boundaries.
+bool vec16(const gdn_tensor* t) {
+    const int64_t v = 16 / (int64_t)esz(t->dtype);
+    if (reinterpret_cast<uintptr_t>(t->data) & 15) return false;
+    for (int i = 0; i < t->ndim - 1; ++i)
+        if (t->stride[i] % v) return false;
+    return true;
+}
+
+int conv_checks(const gdn_tensor* x, const gdn_tensor* weight, const gdn_tensor* out, const gdn_tensor* state,
+                bool state_required, ConvParams* p) {
+    int rc;
+    const int64_t any3[3] = {-1, -1, -1};
+    if ((rc = check_view("x", x, 3, any3))) return rc;
+    const int64_t B = x->shape[0], T = x->shape[1], C = x->shape[2];
+    const int64_t wshape[2] = {C, kConvK};
+    if ((rc = check_view("weight", weight, 2, wshape))) return rc;
+    const int64_t oshape[3] = {B, T, C};
+    if ((rc = check_view("out", out, 3, oshape))) return rc;
+    if (state || state_required) {
+        const int64_t sshape[3] = {B, C, kConvK};
+        if ((rc = check_view("conv_state", state, 3, sshape))) return rc;
+    }
+    if (weight->dtype != x->dtype || out->dtype != x->dtype || (state && state->dtype != x->dtype))
+        return set_last_error(GDN_ERR_UNSUPPORTED, "x, weight, out and conv_state must share one dtype");
+    if (B * C > 0x7fffffffLL) return bad("%s: B*C too large", "x");
+    const char* xb = reinterpret_cast<const char*>(x->data);
+    const char* ob = reinterpret_cast<const char*>(out->data);
+    if (B * T * C > 0 && xb == ob) return bad("%s must not alias x", "out");
+    *p = ConvParams{};
+    p->x = x->data;
+    p->x_sb = x->stride[0];
+    p->x_st = x->stride[1];
+    p->w = weight->data;
+    p->w_sc = weight->stride[0];
+    p->out = out->data;
+    p->o_sb = out->stride[0];
+    p->o_st = out->stride[1];
+    p->state = state ? state->data : nullptr;
+    p->s_sb = state ? state->stride[0] : 0;
+    p->s_sc = state ? state->stride[1] : 0;
+    p->B = (int)B;
+    p->C = (int)C;
+    p->T = T;
+    p->dtype = x->dtype;
+    return GDN_OK;
+}
+
+template <typename E>
+cudaError_t launch_conv_silu(const ConvParams& p, cudaStream_t st) {
+    constexpr int V = 16 / sizeof(E);
+    dim3 grid((unsigned)((p.C / V + kConvThreads - 1) / kConvThreads), (unsigned)((p.T + kConvTokens - 1) / kConvTokens),
+              (unsigned)p.B);
+    gdn_conv_silu_kernel<E><<<grid, kConvThreads, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename E>
+cudaError_t launch_conv_update(const ConvParams& p, cudaStream_t st) {
+    const int64_t n = (int64_t)p.B * p.C;
+    gdn_conv_update_kernel<E><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+template <typename E>
+cudaError_t launch_norm(const NormParams& p, cudaStream_t st) {
+    gdn_rms_norm_gated_kernel<E><<<(unsigned)((p.N + 7) / 8), 256, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+int launched(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) return set_last_error(GDN_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+    note_launch();
+    return GDN_OK;
+}
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" {
+
+int gdn_causal_conv1d_silu(const gdn_tensor* x, const gdn_tensor* weight, gdn_tensor* out, gdn_tensor* conv_state,
+                           void* stream) {
+    gdn::ConvParams p;
+    int rc = gdn::conv_checks(x, weight, out, conv_state, false, &p);
+    if (rc) return rc;
+    if (!gdn::vec16(x) || !gdn::vec16(out) || p.C % (int64_t)(16 / gdn::esz(p.dtype)))
+        return gdn::set_last_error(GDN_ERR_UNSUPPORTED,
+                                   "x and out need 16-byte aligned rows and C a multiple of 16 bytes of elements");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if ((int64_t)p.B * p.C == 0) return GDN_OK;
+    if (p.T == 0) {  // no tokens: the conv state is all padding
+        if (!conv_state) return GDN_OK;
+        if (conv_state->stride[1] != gdn::kConvK || conv_state->stride[0] != (int64_t)p.C * gdn::kConvK)
+            return gdn::set_last_error(GDN_ERR_UNSUPPORTED, "an empty sequence needs a packed conv_state");
+        cudaError_t e = cudaMemsetAsync(conv_state->data, 0, (size_t)p.B * p.C * gdn::kConvK * gdn::esz(p.dtype), st);
+        return e == cudaSuccess ? GDN_OK : gdn::set_last_error(GDN_ERR_CUDA, "conv_state reset: %s", cudaGetErrorName(e));
+    }
+    cudaError_t e = p.dtype == GDN_BF16  ? gdn::launch_conv_silu<__nv_bfloat16>(p, st)
+                    : p.dtype == GDN_F16 ? gdn::launch_conv_silu<__half>(p, st)
+                                         : gdn::launch_conv_silu<float>(p, st);
+    return gdn::launched(e, "conv1d launch");
+}
+
+int gdn_causal_conv1d_update(const gdn_tensor* x, gdn_tensor* conv_state, const gdn_tensor* weight, gdn_tensor* out,
+                             void* stream) {
+    gdn::ConvParams p;
+    int rc = gdn::conv_checks(x, weight, out, conv_state, true, &p);
+    if (rc) return rc;
+    if ((int64_t)p.B * p.C == 0 || p.T == 0) return GDN_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = p.dtype == GDN_BF16  ? gdn::launch_conv_update<__nv_bfloat16>(p, st)
+                    : p.dtype == GDN_F16 ? gdn::launch_conv_update<__half>(p, st)
+                                         : gdn::launch_conv_update<float>(p, st);
+    return gdn::launched(e, "conv1d update launch");
+}
+
+int gdn_gates(const gdn_tensor* a, const gdn_tensor* b, const gdn_tensor* A_log, const gdn_tensor* dt_bias,
+              gdn_tensor* g, gdn_tensor* beta, void* stream) {
+    int rc;
+    const int64_t any3[3] = {-1, -1, -1};
+    if ((rc = gdn::check_view("a", a, 3, any3))) return rc;
+    const int64_t shp[3] = {a->shape[0], a->shape[1], a->shape[2]};
+    const int64_t hshape[1] = {a->shape[2]};
+    if ((rc = gdn::check_view("b", b, 3, shp)) || (rc = gdn::check_view("A_log", A_log, 1, hshape)) ||
+        (rc = gdn::check_view("dt_bias", dt_bias, 1, hshape)) || (rc = gdn::check_view("g", g, 3, shp)) ||
+        (rc = gdn::check_view("beta", beta, 3, shp)))
+        return rc;
+    if (A_log->dtype != dt_bias->dtype) return gdn::set_last_error(GDN_ERR_UNSUPPORTED, "A_log and dt_bias must share one dtype");
+    const int64_t n = shp[0] * shp[1] * shp[2];
+    if (n == 0) return GDN_OK;
+    gdn::GateParams p{};
+    p.a = {a->data, a->stride[0], a->stride[1], a->stride[2], a->dtype};
+    p.b = {b->data, b->stride[0], b->stride[1], b->stride[2], b->dtype};
+    p.A_log = A_log->data;
+    p.dt_bias = dt_bias->data;
+    p.A_st = 1;
+    p.dt_st = 1;
+    p.p_dtype = A_log->dtype;
+    p.g = {g->data, g->stride[0], g->stride[1], g->stride[2], g->dtype};
+    p.beta = {beta->data, beta->stride[0], beta->stride[1], beta->stride[2], beta->dtype};
+    p.B = (int)shp[0];
+    p.T = shp[1];
+    p.H = (int)shp[2];
+    gdn::gdn_gates_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+    return gdn::launched(cudaGetLastError(), "gates launch");
+}
+
+int gdn_rms_norm_gated(const gdn_tensor* x, const gdn_tensor* gate, const gdn_tensor* weight, float eps,
+                       gdn_tensor* out, void* stream) {
+    int rc;
+    const int64_t rows[2] = {-1, gdn::kNormD};
+    if ((rc = gdn::check_view("x", x, 2, rows))) return rc;
+    const int64_t shp[2] = {x->shape[0], gdn::kNormD};
+    const int64_t wshape[1] = {gdn::kNormD};
+    if ((rc = gdn::check_view("gate", gate, 2, shp)) || (rc = gdn::check_view("weight", weight, 1, wshape)) ||
+        (rc = gdn::check_view("out", out, 2, shp)))
+        return rc;
+    if (gate->dtype != x->dtype || weight->dtype != x->dtype || out->dtype != x->dtype)
+        return gdn::set_last_error(GDN_ERR_UNSUPPORTED, "x, gate, weight and out must share one dtype");
+    if (!(eps >= 0.f)) return gdn::set_last_error(GDN_ERR_INVALID_ARGUMENT, "eps must be >= 0");
+    if (x->shape[0] == 0) return GDN_OK;
+    gdn::NormParams p{x->data, x->stride[0], gate->data, gate->stride[0], weight->data, out->data, out->stride[0],
+                      x->shape[0], eps};
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = x->dtype == GDN_BF16  ? gdn::launch_norm<__nv_bfloat16>(p, st)
+                    : x->dtype == GDN_F16 ? gdn::launch_norm<__half>(p, st)
+                                          : gdn::launch_norm<float>(p, st);
+    return gdn::launched(e, "gated RMS norm launch");
+}
+
+}  // extern "C"

@@ -76,7 +76,8 @@ def run_rec(q, k, v, g, beta, state, in_dtype, l2=True, ofs=True):
     return o.float().cpu().numpy(), (None if s is None else s.cpu().numpy())
 
 
-GOLDEN_FILES = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz")) if not os.path.basename(p).startswith("config1"))
+GOLDEN_FILES = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
+                      if not os.path.basename(p).startswith(("config1", "layer_")))  # layer_*: test_gpu_layer.py
 
 
 @pytest.mark.parametrize("path", GOLDEN_FILES, ids=[os.path.basename(p)[:-4] for p in GOLDEN_FILES])
