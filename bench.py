@@ -168,6 +168,58 @@ class L2Flush:
         self.r.sum(dtype=self.acc)
 
 
+def time_layer_kernels(torch, lib, flush, device, T, H, Bd, peak, reps=20):
+    """Device time and GB/s of the layer steps around the rule (Qwen3.5 GatedDeltaNet, C = 3 H 128
+    channels): prefill conv1d+SiLU and gated RMS norm at B=1, T tokens; gates; decode conv update at Bd."""
+    from llms_from_scratch_b200 import layer
+    C, D = 3 * H * 128, 128
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5)
+    bf = torch.bfloat16
+    mixed = torch.randn(1, T, C, device=device, generator=gen).to(bf)
+    w = (0.5 * torch.randn(C, 4, device=device, generator=gen)).to(bf)
+    st = torch.empty(1, C, 4, dtype=bf, device=device)
+    a = torch.randn(1, T, H, device=device, generator=gen).to(bf)
+    b = torch.randn(1, T, H, device=device, generator=gen).to(bf)
+    A_log = torch.log(torch.rand(H, device=device, generator=gen) * 15 + 0.5).to(bf)
+    dt = torch.randn(H, device=device, generator=gen).to(bf)
+    o = torch.randn(T * H, D, device=device, generator=gen).to(bf)
+    z = torch.randn(T * H, D, device=device, generator=gen).to(bf)
+    nw = torch.ones(D, dtype=bf, device=device)
+    xd = torch.randn(Bd, C, 1, device=device, generator=gen).to(bf)
+    sd = torch.randn(Bd, C, 4, device=device, generator=gen).to(bf)
+    legs = {
+        "conv1d_silu": (lambda: layer.causal_conv1d_silu(mixed, w, conv_state=st), 2 * 2 * T * C + 2 * C * 4 * 2,
+                        f"B=1 T={T} C={C}"),
+        "gates": (lambda: layer.gates(a, b, A_log, dt), T * H * (2 + 2 + 4 + 2), f"B=1 T={T} H={H}"),
+        "rms_norm_gated": (lambda: layer.rms_norm_gated(o, z, nw, 1e-6), 3 * T * H * D * 2, f"rows={T * H} D={D}"),
+        "conv1d_update": (lambda: layer.causal_conv1d_update(xd, sd, w, None, "silu"),
+                          Bd * C * (2 + 2 + 2 * 4 * 2) + C * 4 * 2, f"B={Bd} T=1 C={C}"),
+    }
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for e in ev:
+        e.record()
+    torch.cuda.synchronize()
+    arr = (ctypes.c_void_p * 2)(*[e.cuda_event for e in ev])
+    res = {}
+    for name, (fn, nbytes, shape) in legs.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for i in range(reps):
+            flush(i)
+            lib.gdn_set_phase_events(arr, 2)
+            fn()
+            lib.gdn_set_phase_events(None, 0)
+            torch.cuda.synchronize()
+            ts.append(ev[0].elapsed_time(ev[1]))
+        ms = statistics.median(ts)
+        res[name] = {"shape": shape, "ms": ms, "bytes": nbytes, "achieved_gbs": nbytes / (ms / 1e3) / 1e9,
+                     "frac_hbm": nbytes / (ms / 1e3) / 1e9 / peak}
+    return res
+
+
 def make_inputs(torch, B, T, H, seed, device):
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
@@ -457,6 +509,8 @@ def main():
         dec_times.append(dec_ev[0].elapsed_time(dec_ev[1]))
     dec_ms = statistics.median(dec_times)
     dec_bytes = Bd * H * (2 * STATE_BYTES + 4 * D * 2 + 8)
+    peak_l, _ = load_peaks()
+    layer_kernels = time_layer_kernels(torch, lib, flush, device, T, H, Bd, peak_l)
 
     # ---- roofline of the dominant kernel
     peak, peak_kind = load_peaks()
@@ -500,6 +554,7 @@ def main():
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "gpu_launches": launches,
             "clocks": clocks.summary(t_soak, t_end),
+            "layer_kernels": layer_kernels,
             "decode_step": {"workload": f"recurrent step B={Bd} H={H} (one GatedDeltaNet layer)",
                             "ms": dec_ms, "achieved_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
                             "frac_hbm": dec_bytes / (dec_ms / 1e3) / 1e9 / peak},

@@ -7,6 +7,11 @@
  *   fast_chunk_gated_delta_rule      qwen3_5_cutedsl_kernels.py:462-473
  *   torch_chunk_gated_delta_rule     qwen3_5_transformers.py:110-120
  *   torch_recurrent_gated_delta_rule qwen3_5_transformers.py:190-192
+ * and the layer steps on either side of the rule (Qwen3_5GatedDeltaNet.forward):
+ *   prefill conv1d + SiLU            qwen3_5_transformers.py:346-356
+ *   torch_causal_conv1d_update       qwen3_5_transformers.py:85-101
+ *   gates g, beta                    qwen3_5_transformers.py:377-379
+ *   Qwen3_5RMSNormGated              qwen3_5_transformers.py:56-71
  *
  * Conventions (same as the reference):
  *   query, key   [B, T, H, Dk]      value, out  [B, T, H, Dv]
@@ -221,7 +226,8 @@ GDN_API int gdn_rms_norm_gated(const gdn_tensor* x, const gdn_tensor* gate, cons
  * gdn_set_phase_events: when `events` is non-NULL, every later call on this
  * host thread records events[0] on its stream before its first kernel and
  * events[i] after its i-th kernel (i = 1..n-1 must cover the kernels of the
- * call: 2 for the chunked forward, 1 for the recurrent rule).  Entries are
+ * call: 2 for the chunked forward, 1 for the recurrent rule and each layer
+ * step).  Entries are
  * cudaEvent_t handles.  Pass NULL to stop. */
 GDN_API uint64_t gdn_launch_count(void);
 GDN_API void gdn_set_phase_events(void* const* events, int n);

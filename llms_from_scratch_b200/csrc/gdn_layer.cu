@@ -13,9 +13,11 @@
 // of tokens with the three previous inputs in registers.
 //
 // Numerics follow the reference's bf16 ops, each result rounded to the layer
-// dtype once: the conv sum (four exact bf16 products, accumulated in double in
-// tap order), then SiLU in fp32; the norm's mean of squares in double, IEEE sqrt
-// and division, then the three roundings of Qwen3_5RMSNormGated.
+// dtype once: the conv sum (bf16 x bf16 products are exact in fp32, accumulated
+// with FMAs in tap order), then SiLU in fp32; the norm's mean of squares in fp32,
+// then the three roundings of Qwen3_5RMSNormGated.  SiLU and sigmoid use the
+// fast exponential and division; against an exactly computed fp32 value that can
+// move a bf16 rounding by one unit in rare cases (measured in the tests).
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 
@@ -24,7 +26,7 @@ namespace {
 
 constexpr int kConvK = 4;          // linear_conv_kernel_dim of Qwen3.5
 constexpr int kConvThreads = 128;  // channel groups per CTA
-constexpr int kConvTokens = 16;    // tokens per thread (prefill)
+constexpr int kConvTokens = 8;     // tokens per thread (prefill), all their loads issued at once
 
 struct ConvParams {
     const void* x;       // [B,T,C], channels contiguous
@@ -41,47 +43,66 @@ struct ConvParams {
 };
 
 template <typename E> struct Elem;
+// Per-dtype load / store / round-to-dtype, with pair forms (one packed conversion for two values).
 template <> struct Elem<__nv_bfloat16> {
     static __device__ __forceinline__ float ld(const __nv_bfloat16& v) { return __bfloat162float(v); }
     static __device__ __forceinline__ __nv_bfloat16 st(float x) { return __float2bfloat16_rn(x); }
     static __device__ __forceinline__ float rnd(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+    static __device__ __forceinline__ void rnd2(float& a, float& b) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        a = __low2float(h);
+        b = __high2float(h);
+    }
+    static __device__ __forceinline__ void st2(__nv_bfloat16* dst, float a, float b) {
+        *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(a, b);
+    }
 };
 template <> struct Elem<__half> {
     static __device__ __forceinline__ float ld(const __half& v) { return __half2float(v); }
     static __device__ __forceinline__ __half st(float x) { return __float2half_rn(x); }
     static __device__ __forceinline__ float rnd(float x) { return __half2float(__float2half_rn(x)); }
+    static __device__ __forceinline__ void rnd2(float& a, float& b) {
+        const __half2 h = __floats2half2_rn(a, b);
+        a = __low2float(h);
+        b = __high2float(h);
+    }
+    static __device__ __forceinline__ void st2(__half* dst, float a, float b) {
+        *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(a, b);
+    }
 };
 template <> struct Elem<float> {
     static __device__ __forceinline__ float ld(const float& v) { return v; }
     static __device__ __forceinline__ float st(float x) { return x; }
     static __device__ __forceinline__ float rnd(float x) { return x; }
+    static __device__ __forceinline__ void rnd2(float&, float&) {}
+    static __device__ __forceinline__ void st2(float* dst, float a, float b) {
+        dst[0] = a;
+        dst[1] = b;
+    }
 };
 
-// F.silu on a tensor of the layer dtype: computed in fp32, rounded once.
-template <typename E>
-__device__ __forceinline__ float silu_rounded(float y) {
-    return Elem<E>::rnd(y / (1.0f + expf(-y)));
-}
+// x * sigmoid(x) in fp32 (F.silu computes in fp32 for 16-bit tensors).
+__device__ __forceinline__ float silu_f32(float y) { return __fdividef(y, 1.0f + __expf(-y)); }
 
-// conv output of one channel: sum_j w_j x_j (exact products, double accumulation in tap order),
-// rounded to the layer dtype, then SiLU rounded again (:356 / :97-98).
+// conv output of one channel: sum_j w_j x_j in tap order, rounded to the layer dtype, then SiLU
+// rounded again (:356 / :97-98).
 template <typename E>
 __device__ __forceinline__ float conv_silu(const float (&w)[kConvK], float x0, float x1, float x2, float x3) {
-    double acc = 0.0;
-    acc += (double)w[0] * (double)x0;
-    acc += (double)w[1] * (double)x1;
-    acc += (double)w[2] * (double)x2;
-    acc += (double)w[3] * (double)x3;
-    return silu_rounded<E>(Elem<E>::rnd((float)acc));
+    float acc = w[0] * x0;
+    acc = fmaf(w[1], x1, acc);
+    acc = fmaf(w[2], x2, acc);
+    acc = fmaf(w[3], x3, acc);
+    return Elem<E>::rnd(silu_f32(Elem<E>::rnd(acc)));
 }
 
-// Prefill: thread = V consecutive channels x kConvTokens tokens.  16-byte loads and stores of the
-// channel vector per token; the three inputs before the run come from the previous tokens (zero
-// before t = 0, the conv's left padding).
+// Prefill: thread = V consecutive channels (8 bytes) x kConvTokens tokens.  The run's loads (and the
+// three inputs before it: zero before t = 0, the conv's left padding) are all in flight before the
+// first output; each input is converted to fp32 once and slides through a three-deep window.  A warp
+// covers 32 x 8 contiguous bytes of channels per token.
 template <typename E>
 __global__ void __launch_bounds__(kConvThreads) gdn_conv_silu_kernel(ConvParams p) {
-    constexpr int V = 16 / sizeof(E);
-    using Vec = uint4;
+    constexpr int V = 8 / sizeof(E);
+    using Vec = uint2;
     const int cg = blockIdx.x * kConvThreads + threadIdx.x;
     const int c0 = cg * V;
     if (c0 >= p.C) return;
@@ -89,6 +110,15 @@ __global__ void __launch_bounds__(kConvThreads) gdn_conv_silu_kernel(ConvParams 
     const int64_t t0 = (int64_t)blockIdx.y * kConvTokens;
     if (t0 >= p.T) return;
 
+    const E* xb = reinterpret_cast<const E*>(p.x) + (int64_t)b * p.x_sb + c0;
+    E* ob = reinterpret_cast<E*>(p.out) + (int64_t)b * p.o_sb + c0;
+    constexpr int N = kConvTokens + kConvK - 1;  // inputs t0-3 .. t0+kConvTokens-1
+    Vec xs[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+        const int64_t t = t0 - (kConvK - 1) + k;
+        xs[k] = (t >= 0 && t < p.T) ? *reinterpret_cast<const Vec*>(xb + t * p.x_st) : make_uint2(0u, 0u);
+    }
     float w[V][kConvK];
     const E* wp = reinterpret_cast<const E*>(p.w);
 #pragma unroll
@@ -96,35 +126,35 @@ __global__ void __launch_bounds__(kConvThreads) gdn_conv_silu_kernel(ConvParams 
 #pragma unroll
         for (int j = 0; j < kConvK; ++j) w[i][j] = Elem<E>::ld(wp[(int64_t)(c0 + i) * p.w_sc + j]);
 
-    const E* xb = reinterpret_cast<const E*>(p.x) + (int64_t)b * p.x_sb + c0;
-    E* ob = reinterpret_cast<E*>(p.out) + (int64_t)b * p.o_sb + c0;
-    float win[kConvK - 1][V];  // inputs t-3, t-2, t-1
+    float win[kConvK - 1][V];  // inputs t-3, t-2, t-1 in fp32
 #pragma unroll
     for (int k = 0; k < kConvK - 1; ++k) {
-        const int64_t t = t0 - (kConvK - 1) + k;
-        if (t >= 0) {
-            const Vec u = *reinterpret_cast<const Vec*>(xb + t * p.x_st);
-            const E* e = reinterpret_cast<const E*>(&u);
+        const E* e = reinterpret_cast<const E*>(&xs[k]);
 #pragma unroll
-            for (int i = 0; i < V; ++i) win[k][i] = Elem<E>::ld(e[i]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < V; ++i) win[k][i] = 0.f;
-        }
+        for (int i = 0; i < V; ++i) win[k][i] = Elem<E>::ld(e[i]);
     }
-    const int64_t t1 = (t0 + kConvTokens < p.T) ? t0 + kConvTokens : p.T;
-    for (int64_t t = t0; t < t1; ++t) {
-        const Vec u = *reinterpret_cast<const Vec*>(xb + t * p.x_st);
-        const E* e = reinterpret_cast<const E*>(&u);
+#pragma unroll
+    for (int k = kConvK - 1; k < N; ++k) {
+        const int64_t t = t0 - (kConvK - 1) + k;
+        if (t >= p.T) break;
+        const E* e = reinterpret_cast<const E*>(&xs[k]);
         Vec r;
         E* re = reinterpret_cast<E*>(&r);
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-            const float xi = Elem<E>::ld(e[i]);
-            re[i] = Elem<E>::st(conv_silu<E>(w[i], win[0][i], win[1][i], win[2][i], xi));
-            win[0][i] = win[1][i];
-            win[1][i] = win[2][i];
-            win[2][i] = xi;
+        for (int i = 0; i < V; i += 2) {  // channel pairs: one packed rounding for the conv, one for the output
+            const float x0 = Elem<E>::ld(e[i]), x1 = Elem<E>::ld(e[i + 1]);
+            float y0 = fmaf(w[i][3], x0, fmaf(w[i][2], win[2][i], fmaf(w[i][1], win[1][i], w[i][0] * win[0][i])));
+            float y1 = fmaf(w[i + 1][3], x1,
+                            fmaf(w[i + 1][2], win[2][i + 1], fmaf(w[i + 1][1], win[1][i + 1], w[i + 1][0] * win[0][i + 1])));
+            Elem<E>::rnd2(y0, y1);
+            Elem<E>::st2(re + i, silu_f32(y0), silu_f32(y1));
+#pragma unroll
+            for (int c = i; c < i + 2; ++c) {
+                win[0][c] = win[1][c];
+                win[1][c] = win[2][c];
+            }
+            win[2][i] = x0;
+            win[2][i + 1] = x1;
         }
         *reinterpret_cast<Vec*>(ob + t * p.o_st) = r;
     }
@@ -205,7 +235,7 @@ __global__ void __launch_bounds__(256) gdn_gates_kernel(GateParams p) {
     const float sp = x > 20.f ? x : log1pf(expf(x));  // softplus, beta 1, threshold 20
     store_elem(const_cast<void*>(p.g.p), (int64_t)b * p.g.sb + t * p.g.st + (int64_t)h * p.g.sh, p.g.dtype, -expf(A_log) * sp);
     store_elem(const_cast<void*>(p.beta.p), (int64_t)b * p.beta.sb + t * p.beta.st + (int64_t)h * p.beta.sh, p.beta.dtype,
-               1.0f / (1.0f + expf(-bb)));
+               __fdividef(1.0f, 1.0f + __expf(-bb)));
 }
 
 struct NormParams {
@@ -222,8 +252,58 @@ struct NormParams {
 
 constexpr int kNormD = 128;  // head_v_dim
 
-// Qwen3_5RMSNormGated (:62-71), one warp per row, 4 elements per lane:
+// Qwen3_5RMSNormGated (:62-71):
 //   n = round(x * rsqrt(mean(x^2) + eps)); wn = round(weight * n); out = round(wn * silu(gate)).
+// Vector form: each lane owns 16 bytes of a row (8 bf16), 128 / V lanes per row, several rows per warp.
+template <typename E>
+__device__ __forceinline__ void norm_finish(float (&h)[16 / sizeof(E)], const float (&z)[16 / sizeof(E)],
+                                            const float (&w)[16 / sizeof(E)], float inv, float (&o)[16 / sizeof(E)]) {
+#pragma unroll
+    for (int e = 0; e < (int)(16 / sizeof(E)); ++e) {
+        const float n = Elem<E>::rnd(h[e] * inv);
+        const float wn = Elem<E>::rnd(w[e] * n);
+        o[e] = wn * silu_f32(z[e]);
+    }
+}
+
+template <typename E>
+__global__ void __launch_bounds__(256) gdn_rms_norm_gated_vec_kernel(NormParams p) {
+    constexpr int V = 16 / sizeof(E);       // elements per lane
+    constexpr int LPR = kNormD / V;         // lanes per row (16 for bf16, 32 for fp32)
+    constexpr int RPW = 32 / LPR;           // rows per warp
+    const int lane = threadIdx.x & 31;
+    const int sub = lane / LPR, l = lane % LPR;
+    const int64_t row = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * RPW + sub;
+    const bool live = row < p.N;
+    const int64_t r = live ? row : 0;
+    const uint4 xu = *reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(p.x) + r * p.x_sr + V * l);
+    const uint4 gu = *reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(p.gate) + r * p.g_sr + V * l);
+    const uint4 wu = *reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(p.w) + V * l);
+    const E* xe = reinterpret_cast<const E*>(&xu);
+    const E* ge = reinterpret_cast<const E*>(&gu);
+    const E* we = reinterpret_cast<const E*>(&wu);
+    float h[V], z[V], w[V], o[V];
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+        h[e] = Elem<E>::ld(xe[e]);
+        z[e] = Elem<E>::ld(ge[e]);
+        w[e] = Elem<E>::ld(we[e]);
+        ss = fmaf(h[e], h[e], ss);
+    }
+#pragma unroll
+    for (int o2 = LPR / 2; o2 > 0; o2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o2);
+    const float inv = rsqrtf(ss * (1.0f / kNormD) + p.eps);
+    norm_finish<E>(h, z, w, inv, o);
+    if (!live) return;
+    uint4 ou;
+    E* oe = reinterpret_cast<E*>(&ou);
+#pragma unroll
+    for (int e = 0; e < V; ++e) oe[e] = Elem<E>::st(o[e]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<E*>(p.out) + row * p.o_sr + V * l) = ou;
+}
+
+// Scalar form for rows that are not 16-byte aligned: one warp per row, 4 elements per lane.
 template <typename E>
 __global__ void __launch_bounds__(256) gdn_rms_norm_gated_kernel(NormParams p) {
     const int lane = threadIdx.x & 31;
@@ -233,26 +313,23 @@ __global__ void __launch_bounds__(256) gdn_rms_norm_gated_kernel(NormParams p) {
     const E* gr = reinterpret_cast<const E*>(p.gate) + row * p.g_sr + 4 * lane;
     const E* wr = reinterpret_cast<const E*>(p.w) + 4 * lane;
     float h[4], z[4], w[4];
+    float ss = 0.f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         h[e] = Elem<E>::ld(xr[e]);
         z[e] = Elem<E>::ld(gr[e]);
         w[e] = Elem<E>::ld(wr[e]);
+        ss = fmaf(h[e], h[e], ss);
     }
-    double ss = 0.0;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) ss += (double)h[e] * (double)h[e];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float var = (float)(ss / kNormD);
-    const float inv = 1.0f / sqrtf(var + p.eps);
+    const float inv = rsqrtf(ss * (1.0f / kNormD) + p.eps);
     E* orow = reinterpret_cast<E*>(p.out) + row * p.o_sr + 4 * lane;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         const float n = Elem<E>::rnd(h[e] * inv);
         const float wn = Elem<E>::rnd(w[e] * n);
-        const float sz = z[e] / (1.0f + expf(-z[e]));
-        orow[e] = Elem<E>::st(wn * sz);
+        orow[e] = Elem<E>::st(wn * silu_f32(z[e]));
     }
 }
 
@@ -336,7 +413,7 @@ int conv_checks(const gdn_tensor* x, const gdn_tensor* weight, const gdn_tensor*
 
 template <typename E>
 cudaError_t launch_conv_silu(const ConvParams& p, cudaStream_t st) {
-    constexpr int V = 16 / sizeof(E);
+    constexpr int V = 8 / sizeof(E);
     dim3 grid((unsigned)((p.C / V + kConvThreads - 1) / kConvThreads), (unsigned)((p.T + kConvTokens - 1) / kConvTokens),
               (unsigned)p.B);
     gdn_conv_silu_kernel<E><<<grid, kConvThreads, 0, st>>>(p);
@@ -351,8 +428,13 @@ cudaError_t launch_conv_update(const ConvParams& p, cudaStream_t st) {
 }
 
 template <typename E>
-cudaError_t launch_norm(const NormParams& p, cudaStream_t st) {
-    gdn_rms_norm_gated_kernel<E><<<(unsigned)((p.N + 7) / 8), 256, 0, st>>>(p);
+cudaError_t launch_norm(const NormParams& p, bool vec, cudaStream_t st) {
+    if (vec) {
+        constexpr int rows_per_cta = 8 * (32 / (kNormD / (16 / (int)sizeof(E))));
+        gdn_rms_norm_gated_vec_kernel<E><<<(unsigned)((p.N + rows_per_cta - 1) / rows_per_cta), 256, 0, st>>>(p);
+    } else {
+        gdn_rms_norm_gated_kernel<E><<<(unsigned)((p.N + 7) / 8), 256, 0, st>>>(p);
+    }
     return cudaGetLastError();
 }
 
@@ -384,10 +466,13 @@ int gdn_causal_conv1d_silu(const gdn_tensor* x, const gdn_tensor* weight, gdn_te
         cudaError_t e = cudaMemsetAsync(conv_state->data, 0, (size_t)p.B * p.C * gdn::kConvK * gdn::esz(p.dtype), st);
         return e == cudaSuccess ? GDN_OK : gdn::set_last_error(GDN_ERR_CUDA, "conv_state reset: %s", cudaGetErrorName(e));
     }
+    gdn::phase_event(0, st);
     cudaError_t e = p.dtype == GDN_BF16  ? gdn::launch_conv_silu<__nv_bfloat16>(p, st)
                     : p.dtype == GDN_F16 ? gdn::launch_conv_silu<__half>(p, st)
                                          : gdn::launch_conv_silu<float>(p, st);
-    return gdn::launched(e, "conv1d launch");
+    rc = gdn::launched(e, "conv1d launch");
+    gdn::phase_event(1, st);
+    return rc;
 }
 
 int gdn_causal_conv1d_update(const gdn_tensor* x, gdn_tensor* conv_state, const gdn_tensor* weight, gdn_tensor* out,
@@ -397,10 +482,13 @@ int gdn_causal_conv1d_update(const gdn_tensor* x, gdn_tensor* conv_state, const 
     if (rc) return rc;
     if ((int64_t)p.B * p.C == 0 || p.T == 0) return GDN_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    gdn::phase_event(0, st);
     cudaError_t e = p.dtype == GDN_BF16  ? gdn::launch_conv_update<__nv_bfloat16>(p, st)
                     : p.dtype == GDN_F16 ? gdn::launch_conv_update<__half>(p, st)
                                          : gdn::launch_conv_update<float>(p, st);
-    return gdn::launched(e, "conv1d update launch");
+    rc = gdn::launched(e, "conv1d update launch");
+    gdn::phase_event(1, st);
+    return rc;
 }
 
 int gdn_gates(const gdn_tensor* a, const gdn_tensor* b, const gdn_tensor* A_log, const gdn_tensor* dt_bias,
@@ -430,8 +518,12 @@ int gdn_gates(const gdn_tensor* a, const gdn_tensor* b, const gdn_tensor* A_log,
     p.B = (int)shp[0];
     p.T = shp[1];
     p.H = (int)shp[2];
-    gdn::gdn_gates_kernel<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
-    return gdn::launched(cudaGetLastError(), "gates launch");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    gdn::phase_event(0, st);
+    gdn::gdn_gates_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p);
+    rc = gdn::launched(cudaGetLastError(), "gates launch");
+    gdn::phase_event(1, st);
+    return rc;
 }
 
 int gdn_rms_norm_gated(const gdn_tensor* x, const gdn_tensor* gate, const gdn_tensor* weight, float eps,
@@ -451,10 +543,14 @@ int gdn_rms_norm_gated(const gdn_tensor* x, const gdn_tensor* gate, const gdn_te
     gdn::NormParams p{x->data, x->stride[0], gate->data, gate->stride[0], weight->data, out->data, out->stride[0],
                       x->shape[0], eps};
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t e = x->dtype == GDN_BF16  ? gdn::launch_norm<__nv_bfloat16>(p, st)
-                    : x->dtype == GDN_F16 ? gdn::launch_norm<__half>(p, st)
-                                          : gdn::launch_norm<float>(p, st);
-    return gdn::launched(e, "gated RMS norm launch");
+    gdn::phase_event(0, st);
+    const bool vec = gdn::vec16(x) && gdn::vec16(gate) && gdn::vec16(out) && gdn::vec16(weight);
+    cudaError_t e = x->dtype == GDN_BF16  ? gdn::launch_norm<__nv_bfloat16>(p, vec, st)
+                    : x->dtype == GDN_F16 ? gdn::launch_norm<__half>(p, vec, st)
+                                          : gdn::launch_norm<float>(p, vec, st);
+    rc = gdn::launched(e, "gated RMS norm launch");
+    gdn::phase_event(1, st);
+    return rc;
 }
 
 }  // extern "C"

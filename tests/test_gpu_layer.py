@@ -1,12 +1,16 @@
 """Parity of the layer kernels (gdn_layer.cu, through the C ABI) with the layer
 oracle and the reference's fixtures.
 
-bf16 results may differ from the oracle by one bf16 unit in the last place, and
-rarely: the conv sums and the norm's mean of squares are computed exactly as the
-oracle computes them, but the fp32 exp inside SiLU/sigmoid differs from numpy's
-in its last bits, which can flip a bf16 rounding.  The bar written here: every
-element within one bf16 ulp and at most 0.1% of elements off at all.  g (fp32)
-within 1e-6 relative.  Pure copies (the conv state) are bit-exact.
+16-bit results may differ from the oracle, rarely: the kernels sum in fp32 (the
+conv's 16-bit products are exact there, their 4-term sum is not) and use the fast
+exp, division and rsqrt for SiLU, sigmoid and the norm, which differ from the
+oracle's fp32/fp64 values in their last bits and can flip a 16-bit rounding.  A
+flip in the conv's intermediate rounding passes through SiLU, whose slope near
+y = -4 turns one unit of a large y into several units of the small output.  The
+bar written here: at most 0.1% of elements differ at all, and all of them within
+the path's 16-bit tolerance (max-abs 2e-2, rel-L2 5e-3).  fp32 results within
+1e-5 relative (the path's fp32 tolerance is 1e-4); g (accurate exp and log1p)
+within 1e-6.  Pure copies (the conv state) are bit-exact.
 """
 import glob
 import os
@@ -39,20 +43,18 @@ def host(t):
     return t.float().cpu().numpy()
 
 
-def assert_ulp(ours, ref, in_dtype="bf16", what=""):
+def assert_close16(ours, ref, in_dtype="bf16", what=""):
     ours = np.asarray(ours, np.float32)
     ref = np.asarray(ref, np.float32)
     assert ours.shape == ref.shape, what
     if in_dtype == "fp32":
-        np.testing.assert_allclose(ours, ref, rtol=2e-6, atol=1e-7, err_msg=what)
+        np.testing.assert_allclose(ours, ref, rtol=1e-5, atol=1e-6, err_msg=what)
         return
-    mant = 7 if in_dtype == "bf16" else 10
-    mag = np.maximum(np.abs(ref), np.float32(2.0 ** -126))
-    ulp = np.exp2(np.floor(np.log2(mag)) - mant)
     d = np.abs(ours - ref)
-    assert np.all(d <= ulp * 1.0001), f"{what}: max diff {d.max():.3e} beyond one ulp"
     frac = float(np.mean(d > 0))
-    assert frac <= 1e-3, f"{what}: {frac:.2e} of elements off by an ulp"
+    assert frac <= 1e-3, f"{what}: {frac:.2e} of elements differ"
+    assert d.max() <= 2e-2, f"{what}: max-abs {d.max():.3e}"
+    assert np.linalg.norm(d) <= 5e-3 * max(np.linalg.norm(ref), 1e-30), f"{what}: rel-L2 beyond 5e-3"
 
 
 def _layer():
@@ -66,7 +68,7 @@ def test_prefill_conv_golden(path):
     st = torch.full((z["x"].shape[0], z["x"].shape[2], 4), 7.0, dtype=torch.bfloat16, device="cuda")
     y = _layer().causal_conv1d_silu(dev(z["x"]), dev(z["weight"]), conv_state=st)
     torch.cuda.synchronize()
-    assert_ulp(host(y), z["out"], what="conv out")
+    assert_close16(host(y), z["out"], what="conv out")
     np.testing.assert_array_equal(host(st), z["conv_state"])
 
 
@@ -77,7 +79,7 @@ def test_decode_conv_update_golden(path):
     y = _layer().causal_conv1d_update(dev(z["x"]).transpose(1, 2), st, dev(z["weight"]), None, "silu")
     torch.cuda.synchronize()
     assert y.shape == (z["x"].shape[0], z["x"].shape[2], z["x"].shape[1])
-    assert_ulp(host(y.transpose(1, 2)), z["out"], what="update out")
+    assert_close16(host(y.transpose(1, 2)), z["out"], what="update out")
     np.testing.assert_array_equal(host(st), z["new_state"])
 
 
@@ -87,14 +89,14 @@ def test_gates_golden():
     torch.cuda.synchronize()
     assert g.dtype == torch.float32 and beta.dtype == torch.bfloat16
     np.testing.assert_allclose(host(g), z["g"], rtol=1e-6, atol=0)
-    assert_ulp(host(beta), z["beta"], what="beta")
+    assert_close16(host(beta), z["beta"], what="beta")
 
 
 def test_rms_norm_gated_golden():
     z = np.load(os.path.join(GOLDEN, "layer_rmsnorm_gated.npz"))
     o = _layer().rms_norm_gated(dev(z["x"]), dev(z["gate"]), dev(z["weight"]), float(z["eps"]))
     torch.cuda.synchronize()
-    assert_ulp(host(o), z["out"], what="norm")
+    assert_close16(host(o), z["out"], what="norm")
 
 
 @pytest.mark.parametrize("in_dtype", ["bf16", "fp32", "fp16"])
@@ -107,7 +109,7 @@ def test_prefill_conv_vs_oracle(in_dtype, B, T, C):
     y = _layer().causal_conv1d_silu(dev(x, in_dtype), dev(w, in_dtype), conv_state=st)
     torch.cuda.synchronize()
     ry, rs = L.causal_conv1d_silu(x, w, in_dtype)
-    assert_ulp(host(y), ry, in_dtype, "conv out")
+    assert_close16(host(y), ry, in_dtype, "conv out")
     np.testing.assert_array_equal(host(st), rs)
 
 
@@ -161,7 +163,7 @@ def test_gates_vs_oracle(in_dtype):
     torch.cuda.synchronize()
     rg, rb = L.gates(a, b, A_log, dt, in_dtype)
     np.testing.assert_allclose(host(g), rg, rtol=1e-6, atol=1e-30)
-    assert_ulp(host(beta), rb, in_dtype, "beta")
+    assert_close16(host(beta), rb, in_dtype, "beta")
 
 
 @pytest.mark.parametrize("in_dtype", ["bf16", "fp32"])
@@ -179,7 +181,7 @@ def test_rms_norm_gated_vs_oracle_and_strided_rows(in_dtype):
     wide[:, 64:192] = dev(x, in_dtype)
     o2 = lay.rms_norm_gated(wide[:, 64:192], dev(z, in_dtype), dev(w, in_dtype), 1e-6)
     torch.cuda.synchronize()
-    assert_ulp(host(o), ref, in_dtype, "norm")
+    assert_close16(host(o), ref, in_dtype, "norm")
     assert torch.equal(o, o2)
     m = lay.RMSNormGated(128, eps=1e-6).cuda()
     with torch.no_grad():
