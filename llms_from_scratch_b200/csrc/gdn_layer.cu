@@ -81,8 +81,16 @@ template <> struct Elem<float> {
     }
 };
 
-// x * sigmoid(x) in fp32 (F.silu computes in fp32 for 16-bit tensors).
-__device__ __forceinline__ float silu_f32(float y) { return __fdividef(y, 1.0f + __expf(-y)); }
+// x * sigmoid(x) in fp32 (F.silu computes in fp32 for 16-bit tensors), from e^-y = 2^(-y log2 e) and
+// 1 / (1 + e^-y) on the hardware's approximate base-2 exponential and reciprocal.  For very negative y
+// the denominator overflows to inf and the result is -0, the limit; inputs are finite.
+__device__ __forceinline__ float silu_f32(float y) {
+    constexpr float kLog2e = 1.4426950408889634f;  // log2(e)
+    float e, r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-y * kLog2e));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+    return y * r;
+}
 
 // conv output of one channel: sum_j w_j x_j in tap order, rounded to the layer dtype, then SiLU
 // rounded again (:356 / :97-98).
