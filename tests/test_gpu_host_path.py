@@ -45,7 +45,7 @@ def _device_call(q, k, v, g, b, s0):
 
 
 @pytest.mark.parametrize("B,T,H,dtype,slice_tokens,pin,with_state", [
-    (1, 4096, 16, torch.bfloat16, 0, True, True),      # the bench shape, default slices (8 x 512)
+    (1, 4096, 16, torch.bfloat16, 0, True, True),      # the bench shape, default slices (4 x 1024)
     (2, 1000, 4, torch.bfloat16, 256, True, True),     # ragged last slice, batch stride
     (3, 130, 2, torch.bfloat16, 64, True, False),      # 3 slices, the last of 2 tokens, zero start state
     (1, 700, 3, torch.float32, 128, True, True),       # fp32 inputs: the CUDA-core kernels per slice
