@@ -146,6 +146,31 @@ GDN_API int gdn_chunk_gated_delta_rule_host(const gdn_tensor* query, const gdn_t
 GDN_API size_t gdn_chunk_host_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int qkv_dtype,
                                               int64_t slice_tokens);
 
+/* Packed variable-length sequences (prefill of a batch of prompts).
+ *
+ * The reference's op has no varlen form: its vLLM patch falls back to FLA when
+ * cu_seqlens holds more than one sequence (vllm_inference.py:97-108).  This is
+ * the interface vLLM's ChunkGatedDeltaRule hands to its kernels: q/k/v/g/beta
+ * are [1, T, H, *] with sequence n at tokens [cu_seqlens[n], cu_seqlens[n+1]);
+ * every sequence starts its own chunks, its own state (initial_state and
+ * final_state [num_seqs,H,Dk,Dv] fp32, NULL = zeros / not written) and gives
+ * exactly the results of a separate gdn_chunk_gated_delta_rule call on it.
+ *   cu_seqlens  DEVICE int32 [num_seqs + 1], 0 = cu[0] <= cu[1] <= ... <= cu[num_seqs] = T;
+ *               read on the device only (no host synchronisation).  Offsets that
+ *               break this set device error bit 8 and no chunk is processed.
+ *   workspace   >= gdn_chunk_varlen_workspace_bytes(T, num_seqs, ...) bytes, 256-byte aligned.
+ * bf16 q/k/v/out with 16-byte aligned rows only (GDN_ERR_UNSUPPORTED otherwise). */
+GDN_API int gdn_chunk_gated_delta_rule_varlen(const gdn_tensor* query, const gdn_tensor* key,
+                                              const gdn_tensor* value, const gdn_tensor* g, const gdn_tensor* beta,
+                                              const int32_t* cu_seqlens, int64_t num_seqs, int chunk_size,
+                                              const float* initial_state, int output_final_state,
+                                              int use_qk_l2norm_in_kernel, gdn_tensor* out, float* final_state,
+                                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes of gdn_chunk_gated_delta_rule_varlen (T = total tokens). */
+GDN_API size_t gdn_chunk_varlen_workspace_bytes(int64_t T, int64_t num_seqs, int64_t H, int64_t Dk, int64_t Dv,
+                                                int qkv_dtype);
+
 /* Sequence parallelism: one long sequence split into contiguous time shards,
  * one shard per GPU.  No counterpart in the reference, which runs the chunk
  * loop on one device (qwen3_5_cutedsl_kernels.py:427-453); these two calls are
@@ -234,7 +259,8 @@ GDN_API void gdn_set_phase_events(void* const* events, int n);
 
 /* Sticky error bits of the current device.  A kernel whose bounded wait on an
  * internal barrier gives up (a bug, never expected) sets a bit here and exits
- * cleanly instead of hanging: 1 = chunk prep, 2 = chunk scan.  Synchronous;
+ * cleanly instead of hanging: 1 = chunk prep, 2 = chunk scan.  8 = packed
+ * sequence offsets that were not a valid cu_seqlens.  Synchronous;
  * `clear` != 0 resets the word. */
 GDN_API unsigned int gdn_device_error(int clear);
 

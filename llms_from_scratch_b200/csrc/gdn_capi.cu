@@ -255,6 +255,78 @@ int gdn_chunk_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* key, c
     return e == cudaSuccess ? GDN_OK : cuda_fail(e, "chunk kernels launch");
 }
 
+size_t gdn_chunk_varlen_workspace_bytes(int64_t T, int64_t N, int64_t H, int64_t Dk, int64_t Dv, int qkv_dtype) {
+    (void)Dk;
+    (void)Dv;
+    (void)qkv_dtype;
+    if (T < 0 || N <= 0 || H <= 0) return 0;
+    const int64_t max_chunks = (T + gdn::kChunk - 1) / gdn::kChunk + N;
+    const size_t header = ((size_t)(N + 1 + max_chunks) * sizeof(int) + 255) & ~size_t(255);
+    return header + (size_t)(max_chunks * H) * (size_t)gdn::kTcChunkBytes;
+}
+
+int gdn_chunk_gated_delta_rule_varlen(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
+                                      const gdn_tensor* g, const gdn_tensor* beta, const int32_t* cu_seqlens,
+                                      int64_t num_seqs, int chunk_size, const float* initial_state,
+                                      int output_final_state, int use_qk_l2norm_in_kernel, gdn_tensor* out,
+                                      float* final_state, void* workspace, size_t workspace_bytes, void* stream) {
+    g_last_error.clear();
+    if (chunk_size != gdn::kChunk)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "chunk_size must be %d, got %d", gdn::kChunk, chunk_size);
+    int64_t B, T, H;
+    int rc = check_common(query, key, value, g, beta, out, initial_state, output_final_state, final_state, &B, &T, &H);
+    if (rc) return rc;
+    if (B != 1) return fail(GDN_ERR_INVALID_ARGUMENT, "packed sequences need B == 1, got B=%lld", (long long)B);
+    if (num_seqs <= 0 || num_seqs > 0x7fffffffLL || T > 0x7fffffffLL || num_seqs * H > 0x7fffffffLL)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "num_seqs must be in [1, 2^31) and T < 2^31");
+    if (!cu_seqlens) return fail(GDN_ERR_INVALID_ARGUMENT, "cu_seqlens is NULL");
+    if (H > 0 && !tc_eligible(query, key, value, out))
+        return fail(GDN_ERR_UNSUPPORTED, "packed sequences need bf16 q/k/v/out with 16-byte aligned rows");
+    if ((rc = check_device())) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    float* hT = output_final_state ? final_state : nullptr;
+    if (H == 0) return GDN_OK;
+    if (T == 0) return empty_sequence(num_seqs, H, initial_state, hT, st);
+    const size_t need = gdn_chunk_varlen_workspace_bytes(T, num_seqs, H, gdn::kDk, gdn::kDv, query->dtype);
+    if (!workspace || workspace_bytes < need)
+        return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace ? workspace_bytes : 0);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(GDN_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int64_t max_chunks = (T + gdn::kChunk - 1) / gdn::kChunk + num_seqs;
+    const size_t header = ((size_t)(num_seqs + 1 + max_chunks) * sizeof(int) + 255) & ~size_t(255);
+    int* tables = reinterpret_cast<int*>(workspace);
+    gdn::ChunkParams p{};
+    p.q = view4(query);
+    p.k = view4(key);
+    p.v = view4(value);
+    p.g = view3(g);
+    p.beta = view3(beta);
+    p.out = out->data;
+    p.out_sb = out->stride[0];
+    p.out_st = out->stride[1];
+    p.out_sh = out->stride[2];
+    p.out_dtype = out->dtype;
+    p.h0 = initial_state;
+    p.hT = hT;
+    p.ws = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(workspace) + header);
+    p.B = 1;
+    p.H = (int)H;
+    p.T = T;
+    p.NC = (int)((T + gdn::kChunk - 1) / gdn::kChunk);
+    p.l2norm = use_qk_l2norm_in_kernel ? 1 : 0;
+    p.err = device_error_word(dev);
+    p.cu_seqlens = cu_seqlens;
+    p.chunk_base = tables;
+    p.chunk_seq = tables + num_seqs + 1;
+    p.N = (int)num_seqs;
+    p.max_chunks = (int)max_chunks;
+    cudaError_t e = gdn::launch_varlen_tables(p, st);
+    if (e == cudaSuccess) e = gdn::launch_chunk_tc(p, st);
+    return e == cudaSuccess ? GDN_OK : cuda_fail(e, "packed-sequence chunk kernels launch");
+}
+
 int gdn_recurrent_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
                                    const gdn_tensor* g, const gdn_tensor* beta, const float* initial_state,
                                    int output_final_state, int use_qk_l2norm_in_kernel, gdn_tensor* out,

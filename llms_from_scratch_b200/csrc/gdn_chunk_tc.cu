@@ -172,13 +172,28 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     const int quad = warp & 3, half = warp >> 2;  // TMEM lane quadrant, column half
     // Chunks run latest first across all heads (block i -> chunk NC-1 - i/(B*H)), so the records the scan
     // reads first are the ones written last, still in L2 when the scan starts (a long sequence's records
-    // do not all fit).
-    const int BH = p.B * p.H;
-    const int c = p.NC - 1 - (int)(blockIdx.x / BH);
-    const int bh = (int)(blockIdx.x % BH);
-    const int64_t chunk = (int64_t)bh * p.NC + c;  // record index
-    const int b = bh / p.H, h = bh % p.H;
-    const int64_t t0 = (int64_t)c * kChunk;
+    // do not all fit).  t0 is the chunk's first token, t_lim the end of its sequence.
+    int b, h;
+    int64_t chunk, t0, t_lim;  // record index, token range
+    if (!p.cu_seqlens) {
+        const int BH = p.B * p.H;
+        const int c = p.NC - 1 - (int)(blockIdx.x / BH);
+        const int bh = (int)(blockIdx.x % BH);
+        chunk = (int64_t)bh * p.NC + c;
+        b = bh / p.H;
+        h = bh % p.H;
+        t0 = (int64_t)c * kChunk;
+        t_lim = p.T;
+    } else {  // packed sequences: global chunk j (latest first), record j * H + h; the grid is a bound
+        const int j = p.max_chunks - 1 - (int)(blockIdx.x / p.H);
+        h = (int)(blockIdx.x % p.H);
+        if (j >= p.chunk_base[p.N]) return;  // the whole CTA, before any barrier
+        const int n = p.chunk_seq[j];
+        b = 0;
+        chunk = (int64_t)j * p.H + h;
+        t0 = (int64_t)p.cu_seqlens[n] + (int64_t)(j - p.chunk_base[n]) * kChunk;
+        t_lim = p.cu_seqlens[n + 1];
+    }
     const float scale = rsqrtf((float)kDk);
     unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
 
@@ -188,7 +203,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         const int tsr = i >> 10, row = (i >> 4) & 63, piece = i & 15;
         const View4& V = tsr == 0 ? p.q : (tsr == 1 ? p.k : p.v);
         const int64_t t = t0 + row;
-        const bool in = t < p.T;
+        const bool in = t < t_lim;
         const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(V.p) + (int64_t)b * V.sb +
                                    (in ? t : t0) * V.st + (int64_t)h * V.sh + 8 * piece;
         cp_async16(sm + P_RAW + (tsr * kChunk + row) * 256 + piece * 16, src, in ? 16u : 0u);
@@ -202,10 +217,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         mbar_init(&ms.bar, 1);
         fence_mbar_init();
     }
-    if (tid < kChunk) {  // g, beta of the chunk (rows past T are the zero padding)
+    if (tid < kChunk) {  // g, beta of the chunk (rows past the sequence's end are the zero padding)
         const int64_t t = t0 + tid;
         float gv = 0.f, bv = 0.f;
-        if (t < p.T) {
+        if (t < t_lim) {
             gv = load_elem(p.g.p, (int64_t)b * p.g.sb + t * p.g.st + (int64_t)h * p.g.sh, p.g.dtype);
             bv = load_elem(p.beta.p, (int64_t)b * p.beta.sb + t * p.beta.st + (int64_t)h * p.beta.sh, p.beta.dtype);
         }
@@ -250,7 +265,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
 #pragma unroll
         for (int rr = 0; rr < kRows; ++rr) {
             const int r = warp + 8 * (4 * batch + rr);
-            if (p.l2norm && t0 + r < p.T) {
+            if (p.l2norm && t0 + r < t_lim) {
                 const float iq = round_to(rsqrtf(round_to(round_to(ss[2 * rr], GDN_BF16) + 1e-6f, GDN_BF16)), GDN_BF16);
                 const float ik = round_to(rsqrtf(round_to(round_to(ss[2 * rr + 1], GDN_BF16) + 1e-6f, GDN_BF16)), GDN_BF16);
 #pragma unroll
@@ -690,11 +705,12 @@ __device__ __forceinline__ bool scan_aborted(const ScanMisc& ms) {
 
 // o_c rows 16w..16w+15 of this CTA's 32 columns: o = Q'S (accumulator) + o0 (stage smem).
 __device__ __forceinline__ void scan_store_output(const ChunkParams& p, const unsigned char* st, const float (&o)[32],
-                                                  int c, int warp, int lane, int b, int h, int dv0) {
+                                                  int64_t t0, int64_t t_lim, int warp, int lane, int b, int h,
+                                                  int dv0) {
     if (lane >= 16) return;
     const int tok = 16 * warp + lane;
-    const int64_t t = (int64_t)c * kChunk + tok;
-    if (t >= p.T) return;
+    const int64_t t = t0 + tok;
+    if (t >= t_lim) return;
     float ov[32];
 #pragma unroll
     for (int q4 = 0; q4 < 8; ++q4) {
@@ -723,13 +739,26 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     ScanMisc& ms = *reinterpret_cast<ScanMisc*>(sm + S_MISC);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int bh = blockIdx.x;
-    const int b = bh / p.H, h = bh % p.H;
+    const int bh = blockIdx.x;  // (sequence, head): also the state's [Dk, Dv] block
+    const int h = bh % p.H;
     const int dvt = blockIdx.y & 3;  // 32-column slice of the state (and of b / o0)
     const bool summary = p.scan_mode == 1;
     const bool transition = summary && blockIdx.y < 4;  // state starts from I, b ignored
     const int dv0 = dvt * kTcDvTile;
-    const unsigned char* wbase = reinterpret_cast<const unsigned char*>(p.ws) + (int64_t)bh * p.NC * kTcChunkBytes;
+    // chunk c of this sequence: record rec0 + c * rec_step, tokens tbase + 64 c .. (below t_lim)
+    int b = bh / p.H, NC = p.NC;
+    int64_t rec0 = (int64_t)bh * p.NC, rec_step = 1, tbase = 0, t_lim = p.T;
+    if (p.cu_seqlens) {
+        const int n = bh / p.H;
+        b = 0;
+        NC = p.chunk_base[n + 1] - p.chunk_base[n];
+        rec0 = (int64_t)p.chunk_base[n] * p.H + h;
+        rec_step = p.H;
+        tbase = p.cu_seqlens[n];
+        t_lim = p.cu_seqlens[n + 1];
+    }
+    const unsigned char* wsb = reinterpret_cast<const unsigned char*>(p.ws);
+    auto record = [&](int c) { return wsb + (rec0 + (int64_t)c * rec_step) * kTcChunkBytes; };
 
     if (tid == 0) {
         for (int s = 0; s < 2; ++s) {
@@ -763,7 +792,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
         const uint64_t dM = make_sdesc(sbase, 16, 1024, kSwizzle128B);
         const uint64_t dQ = make_sdesc(sbase + S_OFF_Q, 16, 1024, kSwizzle128B);
         const uint64_t dS = make_sdesc(sbase + S_STILE, 16384, 1024, kSwizzle128B);
-        for (int c = 0; c < p.NC; ++c) {
+        for (int c = 0; c < NC; ++c) {
             const int s = c & 1;
             named_bar_sync(kScanBarS, kScanBarCount);  // S_c is in operand tile s
             bool go = ok && !scan_aborted(ms);
@@ -798,10 +827,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             uint64_t* empty = mq ? ms.empty_mq : ms.empty_bo;
             const uint32_t bytes = mq ? 32768 + 16384 : 16384 + 8192;
             int issued = 0;
-            for (int c = 0; c < p.NC; ++c) {
+            for (int c = 0; c < NC; ++c) {
                 const int s = c & 1;
-                if (mq && c + kScanPrefetch < p.NC) {
-                    const unsigned char* pre = wbase + (int64_t)(c + kScanPrefetch) * kTcChunkBytes;
+                if (mq && c + kScanPrefetch < NC) {
+                    const unsigned char* pre = record(c + kScanPrefetch);
                     bulk_prefetch_l2(pre + kTcM, 32768 + 16384);
                     bulk_prefetch_l2(pre + kTcB + dvt * 16384, 16384);
                     bulk_prefetch_l2(pre + kTcO0 + dvt * 8192, 8192);
@@ -811,7 +840,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                     ok = false;
                     break;
                 }
-                const unsigned char* rec = wbase + (int64_t)c * kTcChunkBytes;
+                const unsigned char* rec = record(c);
                 unsigned char* st = sm + s * S_STAGE;
                 mbar_arrive_expect_tx(&full[s], bytes);
                 if (mq) {
@@ -851,9 +880,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
 #pragma unroll
         for (int q8 = 0; q8 < kTcDvTile / 8; ++q8) store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
         fence_proxy_async_smem();
-        named_bar_arrive(kScanBarS, kScanBarCount);  // S_0 for chunk 0
+        if (NC > 0) named_bar_arrive(kScanBarS, kScanBarCount);  // S_0 for chunk 0 (a sequence may be empty)
 
-        for (int c = 0; c < p.NC; ++c) {
+        for (int c = 0; c < NC; ++c) {
             const int s = c & 1;
             const unsigned char* st = sm + s * S_STAGE;
             // ---- S_{c+1} = M_c S_c + b_c (the sequential path)
@@ -876,7 +905,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                     S[4 * q4 + 3] = d[4 * q4 + 3] + bb.w;
                 }
             }
-            if (c + 1 < p.NC) {
+            if (c + 1 < NC) {
                 if (ok) {  // tile (c+1) % 2 was last read by chunk c-1's MMAs, complete before chunk c's state product
 #pragma unroll
                     for (int q8 = 0; q8 < kTcDvTile / 8; ++q8)
@@ -894,7 +923,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                 float o[32];
                 tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + s)), o);
                 tmem_ld_wait();
-                if (!summary) scan_store_output(p, st, o, c, warp, lane, b, h, dv0);
+                if (!summary) scan_store_output(p, st, o, tbase + (int64_t)c * kChunk, t_lim, warp, lane, b, h, dv0);
                 tc_fence_before();
             }
             if (!ok) ms.abort = 1;
@@ -917,13 +946,63 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     if (warp == 0) tmem_dealloc(tm, kScanTmemCols);
 }
 
+// Packed sequences: chunk_base[n] = sum_{m<n} ceil(T_m / 64) and chunk_seq[j] = the sequence of global
+// chunk j, from the device's cu_seqlens, so the host never reads the offsets.  One CTA: each thread
+// counts the chunks of a contiguous run of sequences, a block scan turns the counts into bases, and
+// each thread writes its run.  Offsets that do not start at 0, decrease, or end at T set
+// kErrBadSeqlens and leave zero chunks (every base 0), so the prep and scan do nothing.
+__global__ void __launch_bounds__(256) gdn_varlen_tables(ChunkParams p, int* chunk_base, int* chunk_seq) {
+    __shared__ int part[256];
+    __shared__ int bad;
+    const int tid = threadIdx.x, N = p.N;
+    if (tid == 0) bad = 0;
+    __syncthreads();
+    for (int n = tid; n <= N; n += 256) {
+        const int v = p.cu_seqlens[n];
+        if ((n == 0 && v != 0) || (n == N && (int64_t)v != p.T) || (n < N && p.cu_seqlens[n + 1] < v)) bad = 1;
+    }
+    __syncthreads();
+    const int per = (N + 255) / 256;
+    const int n0 = min(N, tid * per), n1 = min(N, n0 + per);
+    int local = 0;
+    if (!bad)
+        for (int n = n0; n < n1; ++n) local += (p.cu_seqlens[n + 1] - p.cu_seqlens[n] + kChunk - 1) / kChunk;
+    part[tid] = local;
+    __syncthreads();
+    for (int o = 1; o < 256; o <<= 1) {  // inclusive block scan
+        const int v = tid >= o ? part[tid - o] : 0;
+        __syncthreads();
+        part[tid] += v;
+        __syncthreads();
+    }
+    const bool ok = !bad && part[255] <= p.max_chunks;
+    int base = ok ? part[tid] - local : 0;
+    for (int n = n0; n < n1; ++n) {
+        chunk_base[n] = base;
+        const int nc = ok ? (p.cu_seqlens[n + 1] - p.cu_seqlens[n] + kChunk - 1) / kChunk : 0;
+        for (int c = 0; c < nc; ++c) chunk_seq[base + c] = n;
+        base += nc;
+    }
+    if (tid == 0) {
+        chunk_base[N] = ok ? part[255] : 0;
+        if (!ok) report(p.err, kErrBadSeqlens);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_varlen_tables(const ChunkParams& p, cudaStream_t stream) {
+    gdn_varlen_tables<<<1, 256, 0, stream>>>(p, const_cast<int*>(p.chunk_base), const_cast<int*>(p.chunk_seq));
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) note_launch();
+    return e;
+}
 
 cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream) {
     static_assert(P_SMEM <= 227 * 1024 && S_SMEM <= 227 * 1024, "shared memory budget");
     cudaError_t e = cudaFuncSetAttribute(gdn_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM);
     if (e != cudaSuccess) return e;
-    const int64_t nchunks = (int64_t)p.B * p.H * p.NC;
+    const int64_t nchunks = p.cu_seqlens ? (int64_t)p.max_chunks * p.H : (int64_t)p.B * p.H * p.NC;
     gdn_prep_tc<<<(unsigned)nchunks, kPrepThreads, P_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
@@ -933,7 +1012,7 @@ cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream) {
 cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(gdn_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
     if (e != cudaSuccess) return e;
-    dim3 grid((unsigned)(p.B * p.H), (p.scan_mode == 1 ? 2 : 1) * (kDv / kTcDvTile));
+    dim3 grid((unsigned)((p.cu_seqlens ? p.N : p.B) * p.H), (p.scan_mode == 1 ? 2 : 1) * (kDv / kTcDvTile));
     gdn_scan_tc<<<grid, kScanThreads, S_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();

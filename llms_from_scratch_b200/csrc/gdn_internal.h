@@ -45,6 +45,17 @@ struct ChunkParams {
     // from I, b ignored), slices 4-7 the local final state (state started from 0) to hT2.
     int scan_mode;
     float* hT2;
+    // Packed variable-length batch (tensor-core path; B == 1): sequence n is tokens
+    // [cu_seqlens[n], cu_seqlens[n+1]) of the T axis and its chunks start at its first
+    // token.  Global chunk j belongs to sequence chunk_seq[j], which starts at global
+    // chunk chunk_base[n]; records sit at (j * H + h).  Both tables are built on the
+    // device (launch_varlen_tables).  cu_seqlens == null: fixed length, records at
+    // ((b * H + h) * NC + c).  h0 / hT are then [N,H,Dk,Dv].
+    const int* cu_seqlens;
+    const int* chunk_base;  // [N + 1]
+    const int* chunk_seq;   // [max_chunks]
+    int N;                  // sequences
+    int max_chunks;         // ceil(T / 64) + N: bound of sum_n ceil(T_n / 64), the prep's grid
 };
 
 struct RecurrentParams {
@@ -69,7 +80,7 @@ void note_launch();
 cudaError_t phase_event(int index, cudaStream_t stream);
 
 // Error bits a kernel ORs into the device error word.
-enum : unsigned int { kErrTimeoutPrep = 1u, kErrTimeoutScan = 2u };
+enum : unsigned int { kErrTimeoutPrep = 1u, kErrTimeoutScan = 2u, kErrBadSeqlens = 8u };
 
 cudaError_t launch_chunk_simt(const ChunkParams& p, cudaStream_t stream);
 cudaError_t launch_chunk_tc(const ChunkParams& p, cudaStream_t stream);
@@ -77,6 +88,9 @@ cudaError_t launch_chunk_tc(const ChunkParams& p, cudaStream_t stream);
 // (in p.scan_mode) -- the sequence-parallel entry points run them separately.
 cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream);
 cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream);
+// Varlen: builds chunk_base / chunk_seq from cu_seqlens (one CTA); bad offsets set kErrBadSeqlens and
+// leave zero chunks, so nothing runs.
+cudaError_t launch_varlen_tables(const ChunkParams& p, cudaStream_t stream);
 cudaError_t launch_recurrent(const RecurrentParams& p, cudaStream_t stream);
 
 }  // namespace gdn

@@ -264,3 +264,59 @@ def fast_recurrent_gated_delta_rule(
     if out.dtype != out_dtype:
         out = out.to(out_dtype)
     return out, final
+
+
+def chunk_varlen_workspace_bytes(T: int, num_seqs: int, H: int, Dk: int = 128, Dv: int = 128,
+                                 dtype: torch.dtype = torch.bfloat16) -> int:
+    """Device bytes ``chunk_gated_delta_rule_varlen`` needs (``gdn_chunk_varlen_workspace_bytes``)."""
+    return int(_lib.load().gdn_chunk_varlen_workspace_bytes(T, num_seqs, H, Dk, Dv, _DTYPES.get(dtype, _lib.GDN_F32)))
+
+
+def chunk_gated_delta_rule_varlen(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    g: torch.Tensor,
+    beta: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    initial_state: Optional[torch.Tensor] = None,
+    output_final_state: bool = False,
+    use_qk_l2norm_in_kernel: bool = False,
+    workspace: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Chunked rule over packed sequences: ``query [1, T, H, Dk]`` holds sequence n at tokens
+    ``cu_seqlens[n] .. cu_seqlens[n+1]`` (``cu_seqlens`` int32 on the device, read there only).  Each
+    sequence has its own chunks and state (``initial_state`` / ``final_state`` ``[N, H, Dk, Dv]`` fp32)
+    and gets exactly the results of a separate ``fast_chunk_gated_delta_rule`` call.  bf16 q/k/v."""
+    q = _as_kernel_tensor(query, "query", 4)
+    k = _as_kernel_tensor(key, "key", 4)
+    v = _as_kernel_tensor(value, "value", 4)
+    gg = _as_kernel_tensor(g, "g", 3)
+    bb = _as_kernel_tensor(beta, "beta", 3)
+    if not isinstance(cu_seqlens, torch.Tensor) or cu_seqlens.device != q.device or cu_seqlens.dim() != 1:
+        raise RuntimeError("cu_seqlens must be a 1-D tensor on the inputs' device")
+    for name, x in (("key", k), ("value", v), ("g", gg), ("beta", bb)):
+        if x.device != q.device:
+            raise RuntimeError(f"{name} is on {x.device}, query on {q.device}")
+    cu = cu_seqlens.to(torch.int32).contiguous()
+    N = cu.numel() - 1
+    B, T, H, Dk = q.shape
+    Dv = v.shape[-1]
+    h0 = _state_in(initial_state, N, H, Dk, Dv, q.device)
+    out = torch.empty((B, T, H, Dv), dtype=q.dtype, device=q.device)
+    final = torch.empty((N, H, Dk, Dv), dtype=torch.float32, device=q.device) if output_final_state else None
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        need = lib.gdn_chunk_varlen_workspace_bytes(T, max(N, 1), H, Dk, Dv, _DTYPES[q.dtype])
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty((max(need, 1),), dtype=torch.uint8, device=q.device)
+        dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
+        rc = lib.gdn_chunk_gated_delta_rule_varlen(
+            ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(dg), ctypes.byref(db),
+            cu.data_ptr(), N, 64, h0.data_ptr() if h0 is not None else None, int(bool(output_final_state)),
+            int(bool(use_qk_l2norm_in_kernel)), ctypes.byref(do), final.data_ptr() if final is not None else None,
+            workspace.data_ptr(), workspace.numel(), torch.cuda.current_stream(q.device).cuda_stream)
+        _lib.check(rc)
+    if out.dtype != query.dtype:
+        out = out.to(query.dtype)
+    return out, final

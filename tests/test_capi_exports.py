@@ -162,6 +162,47 @@ def test_host_workspace_size(lib):
     assert f(1, 100, 1, 128, 128, _lib.GDN_BF16, 0) == f(1, 128, 1, 128, 128, _lib.GDN_BF16, 0)
 
 
+def _call_varlen(lib, q, k, v, g, b, out, cu=0x2000, num_seqs=2, chunk=64):
+    return lib.gdn_chunk_gated_delta_rule_varlen(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v), ctypes.byref(g),
+                                                 ctypes.byref(b), cu, num_seqs, chunk, None, 0, 1,
+                                                 ctypes.byref(out), None, 0x100000, 1 << 40, None)
+
+
+@pytest.mark.parametrize("case,status,needle", [
+    ("batch", _lib.GDN_ERR_INVALID_ARGUMENT, "B == 1"),
+    ("num_seqs", _lib.GDN_ERR_INVALID_ARGUMENT, "num_seqs"),
+    ("null", _lib.GDN_ERR_INVALID_ARGUMENT, "cu_seqlens is NULL"),
+    ("chunk", _lib.GDN_ERR_INVALID_ARGUMENT, "chunk_size must be 64"),
+    ("fp32", _lib.GDN_ERR_UNSUPPORTED, "bf16"),
+])
+def test_varlen_entry_rejects_bad_arguments_before_any_cuda_call(lib, case, status, needle):
+    B, T, H = (2 if case == "batch" else 1), 300, 2
+    dt = _lib.GDN_F32 if case == "fp32" else _lib.GDN_BF16
+    q, k, v, out = (_t([B, T, H, 128], dt) for _ in range(4))
+    g, b = _t([B, T, H], _lib.GDN_F32), _t([B, T, H], _lib.GDN_F32)
+    kw = {}
+    if case == "num_seqs":
+        kw["num_seqs"] = 0
+    elif case == "null":
+        kw["cu"] = None
+    elif case == "chunk":
+        kw["chunk"] = 32
+    rc = _call_varlen(lib, q, k, v, g, b, out, **kw)
+    assert rc == status
+    assert needle in lib.gdn_last_error().decode()
+
+
+def test_varlen_workspace_size(lib):
+    f = lib.gdn_chunk_varlen_workspace_bytes
+    rec = 147456  # one tensor-core chunk record: M (32 KB) + Q' (16 KB) + b (64 KB) + o0 (32 KB)
+    # tables (N + 1 bases, one sequence id per chunk) rounded to 256 B, then ceil(T/64) + N records per head
+    assert f(1000, 3, 4, 128, 128, _lib.GDN_BF16) == 256 + (16 + 3) * 4 * rec
+    assert f(64, 1, 1, 128, 128, _lib.GDN_BF16) == 256 + 2 * rec
+    big = f(100000, 500, 16, 128, 128, _lib.GDN_BF16)
+    header = (4 * (501 + 1563 + 500) + 255) // 256 * 256
+    assert big == header + (1563 + 500) * 16 * rec
+
+
 def test_final_state_pointer_required(lib):
     B, T, H = 1, 8, 1
     q, k, v, out = (_t([B, T, H, 128]) for _ in range(4))
