@@ -59,6 +59,9 @@ def parse_args():
                     help="config 5: one sequence of --sp-T tokens (B=1) split in time across the ranks")
     ap.add_argument("--sp-T", type=int, default=131072)
     ap.add_argument("--decode-batch", type=int, default=32, help="sequences of the decode-kernel leg")
+    ap.add_argument("--fla", action="store_true",
+                    help="also time vLLM's FLA prefill (its default GatedDeltaNet kernels) on the headline and packed "
+                         "workloads, for comparison")
     return ap.parse_args()
 
 
@@ -218,6 +221,77 @@ def time_layer_kernels(torch, lib, flush, device, T, H, Bd, peak, reps=20):
         res[name] = {"shape": shape, "ms": ms, "bytes": nbytes, "achieved_gbs": nbytes / (ms / 1e3) / 1e9,
                      "frac_hbm": nbytes / (ms / 1e3) / 1e9 / peak}
     return res
+
+
+PACKED_LENGTHS = (4096, 37, 2000, 5000, 64, 129, 5058)  # 16,384 tokens in 7 ragged sequences
+
+
+def _cold_median(torch, fn, flush, reps):
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for i in range(reps):
+        flush(i)
+        ev[0].record()
+        fn()
+        ev[1].record()
+        torch.cuda.synchronize()
+        ts.append(ev[0].elapsed_time(ev[1]))
+    return statistics.median(ts)
+
+
+def time_packed(torch, flush, device, H, peak, fla=None, reps=20):
+    """Packed variable-length prefill (cu_seqlens, the vLLM serving layout): one call over PACKED_LENGTHS,
+    against the same sequences as separate calls; with ``fla`` also vLLM's FLA on the same packed batch."""
+    from llms_from_scratch_b200 import chunk_gated_delta_rule_varlen, chunk_varlen_workspace_bytes
+    from llms_from_scratch_b200 import fast_chunk_gated_delta_rule
+    T, N = sum(PACKED_LENGTHS), len(PACKED_LENGTHS)
+    q, k, v, g, beta, _ = make_inputs(torch, 1, T, H, seed=17, device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(18)
+    s0 = torch.randn(N, H, D, D, device=device, generator=gen) * 0.02
+    edges = [0]
+    for n in PACKED_LENGTHS:
+        edges.append(edges[-1] + n)
+    cu = torch.tensor(edges, dtype=torch.int32, device=device)
+    ws = torch.empty(chunk_varlen_workspace_bytes(T, N, H), dtype=torch.uint8, device=device)
+
+    def packed():
+        return chunk_gated_delta_rule_varlen(q, k, v, g, beta, cu, initial_state=s0, output_final_state=True,
+                                             use_qk_l2norm_in_kernel=True, workspace=ws)
+
+    def separate():
+        for n in range(N):
+            a, b = edges[n], edges[n + 1]
+            fast_chunk_gated_delta_rule(q[:, a:b], k[:, a:b], v[:, a:b], g[:, a:b], beta[:, a:b],
+                                        initial_state=s0[n:n + 1], output_final_state=True,
+                                        use_qk_l2norm_in_kernel=True)
+
+    nbytes = T * H * BYTES_PER_TOKEN_HEAD + 2 * N * H * STATE_BYTES
+    res = {"workload": f"packed prefill, {N} sequences {list(PACKED_LENGTHS)} = {T} tokens, H={H}, bf16, "
+                       "l2norm in kernel, start and final states",
+           "tokens": T, "algorithmic_bytes": nbytes}
+    for name, fn in (("packed_call", packed), ("separate_calls", separate)):
+        ms = _cold_median(torch, fn, flush, reps)
+        res[name] = {"ms": ms, "tok_s": T / (ms / 1e3), "frac_hbm": nbytes / (ms / 1e3) / 1e9 / peak}
+    if fla is not None:
+        s_vk = s0.transpose(-1, -2).contiguous()
+        ms = _cold_median(torch, lambda: fla(q=q, k=k, v=v, g=g, beta=beta, initial_state=s_vk,
+                                             output_final_state=True, cu_seqlens=cu,
+                                             use_qk_l2norm_in_kernel=True), flush, reps)
+        res["vllm_fla"] = {"ms": ms, "tok_s": T / (ms / 1e3), "frac_hbm": nbytes / (ms / 1e3) / 1e9 / peak}
+    return res
+
+
+def load_fla():
+    """vLLM 0.22's FLA chunk_gated_delta_rule, or None with the reason."""
+    try:
+        from vllm.model_executor.layers.fla.ops import chunk_gated_delta_rule
+        return chunk_gated_delta_rule, None
+    except Exception as e:  # vLLM absent or not importable
+        return None, f"{type(e).__name__}: {e}"[:200]
 
 
 def make_inputs(torch, B, T, H, seed, device):
@@ -511,6 +585,19 @@ def main():
     dec_bytes = Bd * H * (2 * STATE_BYTES + 4 * D * 2 + 8)
     peak_l, _ = load_peaks()
     layer_kernels = time_layer_kernels(torch, lib, flush, device, T, H, Bd, peak_l)
+    fla, fla_err = load_fla() if args.fla else (None, None)
+    packed = time_packed(torch, flush, device, H, peak_l, fla=fla)
+    fla_headline = None
+    if args.fla:
+        if fla is None:
+            fla_headline = {"unavailable": fla_err}
+        else:
+            s_vk = s0.transpose(-1, -2).contiguous()
+            fla_ms = _cold_median(torch, lambda: fla(q=q, k=k, v=v, g=g, beta=beta, initial_state=s_vk,
+                                                     output_final_state=True, use_qk_l2norm_in_kernel=True),
+                                  flush, 20)
+            fla_headline = {"workload": f"B={B} T={T} H={H} (the headline workload)", "ms": fla_ms,
+                            "tok_s": B * T / (fla_ms / 1e3)}
 
     # ---- roofline of the dominant kernel
     peak, peak_kind = load_peaks()
@@ -555,11 +642,14 @@ def main():
             "gpu_launches": launches,
             "clocks": clocks.summary(t_soak, t_end),
             "layer_kernels": layer_kernels,
+            "packed_prefill": packed,
             "decode_step": {"workload": f"recurrent step B={Bd} H={H} (one GatedDeltaNet layer)",
                             "ms": dec_ms, "achieved_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
                             "frac_hbm": dec_bytes / (dec_ms / 1e3) / 1e9 / peak},
             "cpu_baseline": cpu,
         }
+        if fla_headline is not None:
+            line["vllm_fla"] = fla_headline
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
