@@ -194,6 +194,23 @@ GDN_API int gdn_chunk_sp_finish(const gdn_tensor* query, const gdn_tensor* key, 
                                 gdn_tensor* out, float* final_state, const void* workspace, size_t workspace_bytes,
                                 void* stream);
 
+/* Backward of gdn_chunk_gated_delta_rule (the reference is inference-only; these are the gradients
+ * autograd takes through its torch forward, qwen3_5_transformers.py:110-187).  Given the forward's
+ * inputs and the gradients of its outputs (d_out [B,T,H,Dv], any float dtype) and of its final state
+ * (d_final_state [B,H,Dk,Dv] fp32, or NULL for none), writes dq, dk, dv [B,T,H,D] and dg, dbeta
+ * [B,T,H] in their descriptors' dtypes and, if dh0 is not NULL, the gradient of the initial state
+ * (fp32 [B,H,Dk,Dv]).  Computes in fp32 on CUDA cores (forward recompute, a reverse state scan and
+ * three per-chunk kernels); the workspace holds both the recomputed forward and the chunk gradients.
+ * Replaces: torch autograd through torch_chunk_gated_delta_rule (qwen3_5_transformers.py:110-187). */
+GDN_API size_t gdn_chunk_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv,
+                                             int qkv_dtype);
+GDN_API int gdn_chunk_gated_delta_rule_bwd(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
+                                           const gdn_tensor* g, const gdn_tensor* beta, const gdn_tensor* d_out,
+                                           int chunk_size, const float* initial_state, const float* d_final_state,
+                                           int use_qk_l2norm_in_kernel, gdn_tensor* dq, gdn_tensor* dk,
+                                           gdn_tensor* dv, gdn_tensor* dg, gdn_tensor* dbeta, float* dh0,
+                                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* Token-by-token recurrent rule (decode step when T == 1).
  *
  * Replaces torch_recurrent_gated_delta_rule(query, key, value, g, beta,

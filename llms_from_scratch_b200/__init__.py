@@ -7,6 +7,9 @@ The CUDA library ``libgdn_b200.so`` is built in-tree by
 """
 
 from .ops import (  # noqa: F401
+    chunk_bwd_workspace_bytes,
+    chunk_gated_delta_rule,
+    chunk_gated_delta_rule_bwd,
     chunk_gated_delta_rule_varlen,
     chunk_host_workspace_bytes,
     chunk_varlen_workspace_bytes,
@@ -19,4 +22,5 @@ from .ops import (  # noqa: F401
 
 __all__ = ["fast_chunk_gated_delta_rule", "fast_recurrent_gated_delta_rule", "chunk_workspace_bytes",
            "chunk_host_workspace_bytes", "chunk_gated_delta_rule_varlen", "chunk_varlen_workspace_bytes",
+           "chunk_gated_delta_rule", "chunk_gated_delta_rule_bwd", "chunk_bwd_workspace_bytes",
            "get_backend", "l2norm"]

@@ -52,6 +52,9 @@ SIGNATURES = {
     "gdn_chunk_gated_delta_rule_varlen": (c_int, [_P, _P, _P, _P, _P, c_void_p, c_int64, c_int, c_void_p, c_int, c_int,
                                                   _P, c_void_p, c_void_p, c_size_t, c_void_p]),
     "gdn_chunk_varlen_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int64, c_int]),
+    "gdn_chunk_gated_delta_rule_bwd": (c_int, [_P, _P, _P, _P, _P, _P, c_int, c_void_p, c_void_p, c_int, _P, _P, _P,
+                                               _P, _P, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "gdn_chunk_bwd_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int64, c_int]),
     "gdn_causal_conv1d_silu": (c_int, [_P, _P, _P, _P, c_void_p]),
     "gdn_causal_conv1d_update": (c_int, [_P, _P, _P, _P, c_void_p]),
     "gdn_gates": (c_int, [_P, _P, _P, _P, _P, _P, c_void_p]),

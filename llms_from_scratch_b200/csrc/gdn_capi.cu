@@ -327,6 +327,86 @@ int gdn_chunk_gated_delta_rule_varlen(const gdn_tensor* query, const gdn_tensor*
     return e == cudaSuccess ? GDN_OK : cuda_fail(e, "packed-sequence chunk kernels launch");
 }
 
+size_t gdn_chunk_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv, int qkv_dtype) {
+    (void)Dk;
+    (void)Dv;
+    (void)qkv_dtype;
+    if (B <= 0 || T <= 0 || H <= 0) return 0;
+    const int64_t NC = (T + gdn::kChunk - 1) / gdn::kChunk;
+    return (size_t)(B * H * NC) * (size_t)(gdn::kWsChunkFloats + gdn::kBwChunkFloats) * sizeof(float);
+}
+
+int gdn_chunk_gated_delta_rule_bwd(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
+                                   const gdn_tensor* g, const gdn_tensor* beta, const gdn_tensor* d_out, int chunk_size,
+                                   const float* initial_state, const float* d_final_state, int use_qk_l2norm_in_kernel,
+                                   gdn_tensor* dq, gdn_tensor* dk, gdn_tensor* dv, gdn_tensor* dg, gdn_tensor* dbeta,
+                                   float* dh0, void* workspace, size_t workspace_bytes, void* stream) {
+    g_last_error.clear();
+    if (chunk_size != gdn::kChunk)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "chunk_size must be %d, got %d", gdn::kChunk, chunk_size);
+    int64_t B, T, H;
+    int rc = check_common(query, key, value, g, beta, d_out, initial_state, 0, nullptr, &B, &T, &H);
+    if (rc) return rc;
+    if ((rc = check4("dq", dq, B, T, H, gdn::kDk))) return rc;
+    if ((rc = check4("dk", dk, B, T, H, gdn::kDk))) return rc;
+    if ((rc = check4("dv", dv, B, T, H, gdn::kDv))) return rc;
+    if ((rc = check3("dg", dg, B, T, H))) return rc;
+    if ((rc = check3("dbeta", dbeta, B, T, H))) return rc;
+    if ((rc = check_device())) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (B * H == 0) return GDN_OK;
+    if (T == 0) {  // no tokens: the initial state's gradient is the final state's
+        if (!dh0) return GDN_OK;
+        const size_t bytes = (size_t)B * H * gdn::kDk * gdn::kDv * sizeof(float);
+        cudaError_t e = d_final_state ? cudaMemcpyAsync(dh0, d_final_state, bytes, cudaMemcpyDeviceToDevice, st)
+                                      : cudaMemsetAsync(dh0, 0, bytes, st);
+        return e == cudaSuccess ? GDN_OK : cuda_fail(e, "initial-state gradient copy");
+    }
+    const size_t need = gdn_chunk_bwd_workspace_bytes(B, T, H, gdn::kDk, gdn::kDv, query->dtype);
+    if (!workspace || workspace_bytes < need)
+        return fail(GDN_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace ? workspace_bytes : 0);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(GDN_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    gdn::ChunkParams f{};
+    f.q = view4(query);
+    f.k = view4(key);
+    f.v = view4(value);
+    f.g = view3(g);
+    f.beta = view3(beta);
+    f.h0 = initial_state;
+    f.B = (int)B;
+    f.H = (int)H;
+    f.T = T;
+    f.NC = (int)((T + gdn::kChunk - 1) / gdn::kChunk);
+    f.l2norm = use_qk_l2norm_in_kernel ? 1 : 0;
+    f.err = device_error_word(dev);
+    gdn::BwdParams p{};
+    p.q = f.q;
+    p.k = f.k;
+    p.v = f.v;
+    p.g = f.g;
+    p.beta = f.beta;
+    p.dout = view4(d_out);
+    p.h0 = initial_state;
+    p.dhT = d_final_state;
+    p.dh0 = dh0;
+    p.dq = {dq->data, dq->stride[0], dq->stride[1], dq->stride[2], dq->dtype};
+    p.dk = {dk->data, dk->stride[0], dk->stride[1], dk->stride[2], dk->dtype};
+    p.dv = {dv->data, dv->stride[0], dv->stride[1], dv->stride[2], dv->dtype};
+    p.dg = {dg->data, dg->stride[0], dg->stride[1], dg->stride[2], dg->dtype};
+    p.dbeta = {dbeta->data, dbeta->stride[0], dbeta->stride[1], dbeta->stride[2], dbeta->dtype};
+    p.fws = reinterpret_cast<float*>(workspace);
+    p.bws = p.fws + (size_t)(B * H * f.NC) * gdn::kWsChunkFloats;
+    p.B = f.B;
+    p.H = f.H;
+    p.NC = f.NC;
+    p.T = T;
+    p.l2norm = f.l2norm;
+    cudaError_t e = gdn::launch_chunk_bwd(f, p, st);
+    return e == cudaSuccess ? GDN_OK : cuda_fail(e, "backward kernels launch");
+}
+
 int gdn_recurrent_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
                                    const gdn_tensor* g, const gdn_tensor* beta, const float* initial_state,
                                    int output_final_state, int use_qk_l2norm_in_kernel, gdn_tensor* out,

@@ -230,6 +230,14 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_simt(ChunkParams p) {
             *reinterpret_cast<float4*>(&s.U[i][q4]) = *reinterpret_cast<const float4*>(ws + kWsU + i * kDv + dv0 + q4);
         }
         const float gamma = ws[kWsGamma];
+        if (p.states) {  // S at the start of chunk c (S is stable here: the last update precedes the barrier above)
+            float* dst = p.states + ((int64_t)bh * p.NC + c) * p.states_stride;
+            for (int idx = tid; idx < kDk * kScanDv / 4; idx += kThreads) {
+                const int d = idx / (kScanDv / 4), c4 = (idx % (kScanDv / 4)) * 4;
+                *reinterpret_cast<float4*>(dst + (int64_t)d * kDv + dv0 + c4) =
+                    *reinterpret_cast<const float4*>(&s.S[d][c4]);
+            }
+        }
         __syncthreads();
 
         // v_new = u - w S  (:173-174)
@@ -270,7 +278,7 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_simt(ChunkParams p) {
                 o[0] += av * v4.x; o[1] += av * v4.y; o[2] += av * v4.z; o[3] += av * v4.w;
             }
             const int64_t t = (int64_t)c * kChunk + r;
-            if (t < p.T) {
+            if (p.out && t < p.T) {
                 const int64_t ob = (int64_t)b * p.out_sb + t * p.out_st + (int64_t)h * p.out_sh + dv0 + cq;
 #pragma unroll
                 for (int e = 0; e < 4; ++e) store_elem(p.out, ob + e, p.out_dtype, a[e] + o[e]);

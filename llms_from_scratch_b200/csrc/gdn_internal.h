@@ -56,7 +56,57 @@ struct ChunkParams {
     const int* chunk_seq;   // [max_chunks]
     int N;                  // sequences
     int max_chunks;         // ceil(T / 64) + N: bound of sum_n ceil(T_n / 64), the prep's grid
+    // CUDA-core scan only: when set, the state at the start of every chunk is written to
+    // states + ((b*H + h)*NC + c) * states_stride as [Dk][Dv] fp32 (the backward's forward
+    // recompute); out may then be null.
+    float* states;
+    int64_t states_stride;
 };
+
+// ---------------------------------------------------------------- backward
+// Per-chunk backward workspace (floats), after the forward's kWsChunkFloats region of every chunk.
+constexpr int64_t kBwS = 0;                    // S_c, the state at the chunk's start          [Dk][Dv]
+constexpr int64_t kBwDSe = kBwS + kDk * kDv;   // dS_{c+1}, gradient at the chunk's end       [Dk][Dv]
+constexpr int64_t kBwDVn = kBwDSe + kDk * kDv; // dv_new = Kd dS_{c+1} + Aqk^T do             [64][Dv]
+constexpr int64_t kBwVn = kBwDVn + kChunk * kDv;   // v_new = u - w S_c                       [64][Dv]
+constexpr int64_t kBwDQg = kBwVn + kChunk * kDv;   // d(q e^gc Dk^-1/2) = do S_c^T            [64][Dk]
+constexpr int64_t kBwDW = kBwDQg + kChunk * kDk;   // dw = -dv_new S_c^T                      [64][Dk]
+constexpr int64_t kBwDKd = kBwDW + kChunk * kDk;   // d(k e^(gc_last-gc)) = v_new dS_{c+1}^T  [64][Dk]
+constexpr int64_t kBwDKp = kBwDKd + kChunk * kDk;  // dk^ through beta e^gc k^                [64][Dk]
+constexpr int64_t kBwDL = kBwDKp + kChunk * kDk;   // dL (strictly lower)                     [64][64]
+constexpr int64_t kBwDA = kBwDL + kChunk * kChunk; // dAqk (lower incl. diagonal)             [64][64]
+constexpr int64_t kBwSmall = kBwDA + kChunk * kChunk;  // [0] <S_c, dS_{c+1}>, [64..] dbeta part, [128..] dgc part
+constexpr int64_t kBwChunkFloats = kBwSmall + 192;
+
+struct Out4 {
+    void* p;
+    int64_t sb, st, sh;
+    int dtype;
+};
+struct Out3 {
+    void* p;
+    int64_t sb, st, sh;
+    int dtype;
+};
+
+struct BwdParams {
+    View4 q, k, v, dout;
+    View3 g, beta;
+    const float* h0;    // [B,H,Dk,Dv] or null
+    const float* dhT;   // gradient of the final state, or null
+    float* dh0;         // gradient of the initial state, or null
+    Out4 dq, dk, dv;
+    Out3 dg, dbeta;
+    float* fws;         // forward workspace: kWsChunkFloats per chunk (CUDA-core prep layout)
+    float* bws;         // backward workspace: kBwChunkFloats per chunk
+    int B, H, NC;
+    int64_t T;
+    int l2norm;
+};
+
+// Backward of the chunked rule (CUDA-core, fp32): forward recompute (prep + scan recording the
+// chunk-start states), reverse state scan, then three per-chunk gradient kernels.
+cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStream_t stream);
 
 struct RecurrentParams {
     View4 q, k, v;

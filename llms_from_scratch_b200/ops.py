@@ -320,3 +320,92 @@ def chunk_gated_delta_rule_varlen(
     if out.dtype != query.dtype:
         out = out.to(query.dtype)
     return out, final
+
+
+def chunk_bwd_workspace_bytes(B: int, T: int, H: int, Dk: int = 128, Dv: int = 128,
+                              dtype: torch.dtype = torch.bfloat16) -> int:
+    """Device bytes ``chunk_gated_delta_rule_bwd`` needs (``gdn_chunk_bwd_workspace_bytes``)."""
+    return int(_lib.load().gdn_chunk_bwd_workspace_bytes(B, T, H, Dk, Dv, _DTYPES.get(dtype, _lib.GDN_F32)))
+
+
+def chunk_gated_delta_rule_bwd(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    g: torch.Tensor,
+    beta: torch.Tensor,
+    d_out: torch.Tensor,
+    initial_state: Optional[torch.Tensor] = None,
+    d_final_state: Optional[torch.Tensor] = None,
+    use_qk_l2norm_in_kernel: bool = False,
+    chunk_size: int = 64,
+    workspace: Optional[torch.Tensor] = None,
+):
+    """Gradients of ``fast_chunk_gated_delta_rule``: returns ``(dq, dk, dv, dg, dbeta, dh0)`` for outputs
+    receiving ``d_out`` and the final state receiving ``d_final_state`` (None = not used), each gradient in
+    its input's dtype (``dh0`` fp32, None without ``initial_state``).  The reference has no backward; these
+    are the gradients autograd takes through its torch forward (qwen3_5_transformers.py:110-187)."""
+    q = _as_kernel_tensor(query, "query", 4)
+    k = _as_kernel_tensor(key, "key", 4)
+    v = _as_kernel_tensor(value, "value", 4)
+    gg = _as_kernel_tensor(g, "g", 3)
+    bb = _as_kernel_tensor(beta, "beta", 3)
+    do = _as_kernel_tensor(d_out, "d_out", 4)
+    B, T, H, Dk = q.shape
+    Dv = v.shape[-1]
+    dev = q.device
+    for name, x in (("key", k), ("value", v), ("g", gg), ("beta", bb), ("d_out", do)):
+        if x.device != dev:
+            raise RuntimeError(f"{name} is on {x.device}, query on {dev}")
+    h0 = _state_in(initial_state, B, H, Dk, Dv, dev)
+    dhT = _state_in(d_final_state, B, H, Dk, Dv, dev)
+    dq = torch.empty(q.shape, dtype=q.dtype, device=dev)
+    dk = torch.empty(k.shape, dtype=k.dtype, device=dev)
+    dv = torch.empty(v.shape, dtype=v.dtype, device=dev)
+    dg = torch.empty(gg.shape, dtype=gg.dtype, device=dev)
+    db = torch.empty(bb.shape, dtype=bb.dtype, device=dev)
+    dh0 = torch.empty((B, H, Dk, Dv), dtype=torch.float32, device=dev) if initial_state is not None else None
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        need = lib.gdn_chunk_bwd_workspace_bytes(B, T, H, Dk, Dv, _DTYPES[q.dtype])
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty((max(need, 1),), dtype=torch.uint8, device=dev)
+        descs = [_desc(x) for x in (q, k, v, gg, bb, do, dq, dk, dv, dg, db)]
+        rc = lib.gdn_chunk_gated_delta_rule_bwd(
+            *[ctypes.byref(d) for d in descs[:6]], int(chunk_size), h0.data_ptr() if h0 is not None else None,
+            dhT.data_ptr() if dhT is not None else None, int(bool(use_qk_l2norm_in_kernel)),
+            *[ctypes.byref(d) for d in descs[6:]], dh0.data_ptr() if dh0 is not None else None,
+            workspace.data_ptr(), workspace.numel(), torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(rc)
+    cast = lambda x, ref: x if x.dtype == ref.dtype else x.to(ref.dtype)  # noqa: E731
+    return (cast(dq, query), cast(dk, key), cast(dv, value), cast(dg, g), cast(db, beta), dh0)
+
+
+class _ChunkRule(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, initial_state, output_final_state, use_qk_l2norm_in_kernel):
+        o, s = fast_chunk_gated_delta_rule(q, k, v, g, beta, initial_state=initial_state,
+                                           output_final_state=output_final_state,
+                                           use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+        ctx.save_for_backward(q, k, v, g, beta, initial_state)
+        ctx.l2 = use_qk_l2norm_in_kernel
+        ctx.has_state = initial_state is not None
+        return o, s
+
+    @staticmethod
+    def backward(ctx, d_out, d_state):
+        q, k, v, g, beta, h0 = ctx.saved_tensors
+        grads = chunk_gated_delta_rule_bwd(q, k, v, g, beta, d_out.contiguous(),
+                                           initial_state=h0 if ctx.has_state else None,
+                                           d_final_state=d_state, use_qk_l2norm_in_kernel=ctx.l2)
+        dh0 = grads[5]
+        if ctx.has_state and dh0 is not None and dh0.dtype != h0.dtype:
+            dh0 = dh0.to(h0.dtype)
+        return grads[0], grads[1], grads[2], grads[3], grads[4], dh0, None, None
+
+
+def chunk_gated_delta_rule(query, key, value, g, beta, initial_state=None, output_final_state=False,
+                           use_qk_l2norm_in_kernel=False):
+    """Differentiable form of ``fast_chunk_gated_delta_rule`` (same arguments and outputs): its backward runs
+    ``chunk_gated_delta_rule_bwd``.  For training; the drop-in itself, like the reference's, has no backward."""
+    return _ChunkRule.apply(query, key, value, g, beta, initial_state, output_final_state, use_qk_l2norm_in_kernel)

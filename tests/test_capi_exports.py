@@ -203,6 +203,41 @@ def test_varlen_workspace_size(lib):
     assert big == header + (1563 + 500) * 16 * rec
 
 
+@pytest.mark.parametrize("case,needle", [
+    ("chunk", "chunk_size must be 64"),
+    ("dq", "dq must be 4-D"),
+    ("dg", "dg has shape"),
+    ("dout", "out has shape"),
+])
+def test_bwd_entry_rejects_bad_arguments_before_any_cuda_call(lib, case, needle):
+    B, T, H = 1, 70, 2
+    q, k, v, do = (_t([B, T, H, 128]) for _ in range(4))
+    dq, dk, dv = (_t([B, T, H, 128]) for _ in range(3))
+    g, b, dg, db = (_t([B, T, H], _lib.GDN_F32) for _ in range(4))
+    chunk = 64
+    if case == "chunk":
+        chunk = 16
+    elif case == "dq":
+        dq = _t([B, T, H])
+    elif case == "dg":
+        dg = _t([B, T + 1, H], _lib.GDN_F32)
+    elif case == "dout":
+        do = _t([B, T - 1, H, 128])
+    rc = lib.gdn_chunk_gated_delta_rule_bwd(*(ctypes.byref(x) for x in (q, k, v, g, b, do)), chunk, None, None, 1,
+                                            *(ctypes.byref(x) for x in (dq, dk, dv, dg, db)), None, 0x100000,
+                                            1 << 40, None)
+    assert rc == _lib.GDN_ERR_INVALID_ARGUMENT
+    assert needle in lib.gdn_last_error().decode()
+
+
+def test_bwd_workspace_size(lib):
+    f = lib.gdn_chunk_bwd_workspace_bytes
+    assert f(1, 0, 4, 128, 128, _lib.GDN_BF16) == 0
+    # forward record (36,928 floats) + backward record (90,304 floats) per (b, h, chunk)
+    assert f(1, 64, 1, 128, 128, _lib.GDN_BF16) == (36928 + 90304) * 4
+    assert f(2, 4096, 16, 128, 128, _lib.GDN_F32) == 2 * 16 * 64 * (36928 + 90304) * 4
+
+
 def test_final_state_pointer_required(lib):
     B, T, H = 1, 8, 1
     q, k, v, out = (_t([B, T, H, 128]) for _ in range(4))
