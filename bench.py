@@ -285,6 +285,47 @@ def time_packed(torch, flush, device, H, peak, fla=None, reps=20):
     return res
 
 
+def time_backward(torch, lib, flush, device, T, H, reps=10):
+    """Backward of the chunked rule at B=1, T, H (bf16 q/k/v, fp32 g/beta/states, l2norm in kernel, gradients
+    of the outputs and of the final state): device time of the whole call and of each of its launches."""
+    from llms_from_scratch_b200 import chunk_bwd_workspace_bytes, chunk_gated_delta_rule_bwd
+    q, k, v, g, beta, s0 = make_inputs(torch, 1, T, H, seed=31, device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(32)
+    do = torch.randn(1, T, H, D, device=device, generator=gen).bfloat16()
+    dhT = torch.randn(1, H, D, D, device=device, generator=gen)
+    ws = torch.empty(chunk_bwd_workspace_bytes(1, T, H), dtype=torch.uint8, device=device)
+
+    def fn():
+        return chunk_gated_delta_rule_bwd(q, k, v, g, beta, do, initial_state=s0, d_final_state=dhT,
+                                          use_qk_l2norm_in_kernel=True, workspace=ws)
+
+    names = ["fwd_prep", "fwd_scan_states", "bwd_scan", "bwd_states", "bwd_wy", "bwd_grads"]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+    for e in ev:
+        e.record()
+    torch.cuda.synchronize()
+    arr = (ctypes.c_void_p * 7)(*[e.cuda_event for e in ev])
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    parts = {n: [] for n in names}
+    total = []
+    for i in range(reps):
+        flush(i)
+        lib.gdn_set_phase_events(arr, 7)
+        fn()
+        lib.gdn_set_phase_events(None, 0)
+        torch.cuda.synchronize()
+        for j, n in enumerate(names):
+            parts[n].append(ev[j].elapsed_time(ev[j + 1]))
+        total.append(ev[0].elapsed_time(ev[6]))
+    ms = statistics.median(total)
+    return {"workload": f"chunk backward B=1 T={T} H={H}, bf16 q/k/v and d_out, fp32 g/beta/states, l2norm in "
+                        "kernel, d_final_state given; fp32 CUDA-core kernels",
+            "ms": ms, "tok_s": T / (ms / 1e3), "kernels_ms": {n: statistics.median(parts[n]) for n in names}}
+
+
 def load_fla():
     """vLLM 0.22's FLA chunk_gated_delta_rule, or None with the reason."""
     try:
@@ -587,6 +628,7 @@ def main():
     layer_kernels = time_layer_kernels(torch, lib, flush, device, T, H, Bd, peak_l)
     fla, fla_err = load_fla() if args.fla else (None, None)
     packed = time_packed(torch, flush, device, H, peak_l, fla=fla)
+    backward = time_backward(torch, lib, flush, device, T, H)
     fla_headline = None
     if args.fla:
         if fla is None:
@@ -643,6 +685,7 @@ def main():
             "clocks": clocks.summary(t_soak, t_end),
             "layer_kernels": layer_kernels,
             "packed_prefill": packed,
+            "backward": backward,
             "decode_step": {"workload": f"recurrent step B={Bd} H={H} (one GatedDeltaNet layer)",
                             "ms": dec_ms, "achieved_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
                             "frac_hbm": dec_bytes / (dec_ms / 1e3) / 1e9 / peak},

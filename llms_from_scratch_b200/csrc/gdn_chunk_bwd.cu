@@ -120,16 +120,17 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_scan(BwdParams p) {
         const float* fw = p.fws + ci * kWsChunkFloats;
         float* bw = p.bws + ci * kBwChunkFloats;
         __syncthreads();  // the previous chunk's readers are done; dS is final
-        for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
+        for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {  // asynchronous: all pieces in flight
             const int i = idx >> 5, d4 = (idx & 31) * 4;
-            st4(&s.W[i][d4], ld4(fw + kWsW + i * kDk + d4));
-            st4(&s.Qg[i][d4], ld4(fw + kWsQg + i * kDk + d4));
-            st4(&s.Kd[i][d4], ld4(fw + kWsKd + i * kDk + d4));
+            cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
+            cp_async16_rec(&s.Qg[i][d4], fw + kWsQg + i * kDk + d4);
+            cp_async16_rec(&s.Kd[i][d4], fw + kWsKd + i * kDk + d4);
         }
         for (int idx = tid; idx < kChunk * kChunk / 4; idx += kThreads) {
             const int i = idx >> 4, j4 = (idx & 15) * 4;
-            st4(&s.A[i][j4], ld4(fw + kWsAqk + i * kChunk + j4));
+            cp_async16_rec(&s.A[i][j4], fw + kWsAqk + i * kChunk + j4);
         }
+        cp_async_commit_rec();
         for (int idx = tid; idx < kChunk * kScanDv; idx += kThreads) {
             const int i = idx / kScanDv, cc = idx % kScanDv;
             const int64_t t = (int64_t)c * kChunk + i;
@@ -142,6 +143,7 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_scan(BwdParams p) {
             st4(bw + kBwDSe + (int64_t)d * kDv + dv0 + c4, ld4(&s.dS[d][c4]));
         }
         const float gamma = fw[kWsGamma];
+        cp_async_wait_rec();
         __syncthreads();
         {  // dv_new = Kd dS + Aqk^T do (Aqk is lower incl. the diagonal: rows j >= r)
             float a[4] = {0.f, 0.f, 0.f, 0.f};
@@ -225,9 +227,10 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_states(BwdParams p) {
     float* bw = p.bws + ci * kBwChunkFloats;
     for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
         const int i = idx >> 5, d4 = (idx & 31) * 4;
-        st4(&s.W[i][d4], ld4(fw + kWsW + i * kDk + d4));
-        st4(&s.dVn[i][d4], ld4(bw + kBwDVn + i * kDv + d4));
+        cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
+        cp_async16_rec(&s.dVn[i][d4], bw + kBwDVn + i * kDv + d4);
     }
+    cp_async_commit_rec();
     for (int i = warp; i < kChunk; i += kThreads / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.dO[i][0]);
 
     const int ty = tid >> 4, tx = tid & 15, c0 = 4 * tx, c1 = 64 + 4 * tx;
@@ -243,12 +246,17 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_states(BwdParams p) {
         for (int idx = tid; idx < 32 * kDv / 4; idx += kThreads) {
             const int rr = idx >> 5, d4 = (idx & 31) * 4;
             const int64_t row = 32 * slab + rr;
-            const float4 sv = ld4(bw + kBwS + row * kDv + d4), ev = ld4(bw + kBwDSe + row * kDv + d4);
-            st4(&s.S[rr][d4], sv);
-            st4(&s.E[rr][d4], ev);
+            cp_async16_rec(&s.S[rr][d4], bw + kBwS + row * kDv + d4);
+            cp_async16_rec(&s.E[rr][d4], bw + kBwDSe + row * kDv + d4);
+        }
+        cp_async_commit_rec();
+        cp_async_wait_rec();
+        __syncthreads();
+        for (int idx = tid; idx < 32 * kDv / 4; idx += kThreads) {  // <S_c, dS_{c+1}> over the slab
+            const int rr = idx >> 5, d4 = (idx & 31) * 4;
+            const float4 sv = ld4(&s.S[rr][d4]), ev = ld4(&s.E[rr][d4]);
             dgam += sv.x * ev.x + sv.y * ev.y + sv.z * ev.z + sv.w * ev.w;
         }
-        __syncthreads();
         // v_new partial: acc += w[:, slab] S[slab, :]
         for (int kk = 0; kk < 32; ++kk) {
             const float4 s0 = ld4(&s.S[kk][c0]), s1 = ld4(&s.S[kk][c1]);
@@ -301,8 +309,10 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_states(BwdParams p) {
         __syncthreads();
         for (int idx = tid; idx < 32 * kDv / 4; idx += kThreads) {
             const int rr = idx >> 5, d4 = (idx & 31) * 4;
-            st4(&s.E[rr][d4], ld4(bw + kBwDSe + (int64_t)(32 * slab + rr) * kDv + d4));
+            cp_async16_rec(&s.E[rr][d4], bw + kBwDSe + (int64_t)(32 * slab + rr) * kDv + d4);
         }
+        cp_async_commit_rec();
+        cp_async_wait_rec();
         __syncthreads();
         float k8[8];
 #pragma unroll
@@ -412,9 +422,11 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_wy(BwdParams p) {
     }
     for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
         const int i = idx >> 5, d4 = (idx & 31) * 4;
-        st4(&s.U[i][d4], ld4(fw + kWsU + i * kDv + d4));
-        st4(&s.W[i][d4], ld4(fw + kWsW + i * kDk + d4));
+        cp_async16_rec(&s.U[i][d4], fw + kWsU + i * kDv + d4);
+        cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
     }
+    cp_async_commit_rec();
+    cp_async_wait_rec();
     __syncthreads();
     {  // dv = beta d(beta v); d beta, d gc and the k^ term of d(beta e^gc k^)
         const int cols[2] = {4 * tx, 64 + 4 * tx};
@@ -487,9 +499,11 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_wy(BwdParams p) {
     __syncthreads();  // u and w are read: v_new and do replace them
     for (int idx = tid; idx < kChunk * kDv / 4; idx += kThreads) {
         const int i = idx >> 5, d4 = (idx & 31) * 4;
-        st4(&s.U[i][d4], ld4(bw + kBwVn + i * kDv + d4));
+        cp_async16_rec(&s.U[i][d4], bw + kBwVn + i * kDv + d4);
     }
+    cp_async_commit_rec();
     for (int i = warp; i < kChunk; i += kThreads / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.W[i][0]);
+    cp_async_wait_rec();
     __syncthreads();
     {  // dAqk = incl(do v_new^T)
         float a[4][4];
@@ -560,13 +574,15 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
     }
     for (int idx = tid; idx < kChunk * kChunk / 4; idx += kThreads) {
         const int i = idx >> 4, j4 = (idx & 15) * 4;
-        st4(&s.P[i][j4], ld4(bw + kBwDA + i * kChunk + j4));
-        st4(&s.G[i][j4], ld4(bw + kBwDL + i * kChunk + j4));
+        cp_async16_rec(&s.P[i][j4], bw + kBwDA + i * kChunk + j4);
+        cp_async16_rec(&s.G[i][j4], bw + kBwDL + i * kChunk + j4);
     }
+    cp_async_commit_rec();
     if (tid < kChunk) {
         s.dbeta[tid] = bw[kBwSmall + 64 + tid];
         s.dgc[tid] = bw[kBwSmall + 128 + tid];
     }
+    cp_async_wait_rec();  // dAqk and dL landed; chunk_gates' barriers publish them
     chunk_gates(p, b, h, t0, s.gc, s.beta, s.egc, s.ekd);  // ends with a barrier
 
     const int ty = tid >> 4, tx = tid & 15;
@@ -627,8 +643,10 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
     }
     for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
         const int i = idx >> 5, d4 = (idx & 31) * 4;
-        st4(&s.X[i][d4], ld4(bw + kBwDQg + i * kDk + d4));
+        cp_async16_rec(&s.X[i][d4], bw + kBwDQg + i * kDk + d4);
     }
+    cp_async_commit_rec();
+    cp_async_wait_rec();
     __syncthreads();
     if (tid < kChunk) {  // every add to one address comes from one thread, in program order: deterministic
         float cs = 0.f;
@@ -681,8 +699,10 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
     __syncthreads();  // dQg is read: dKd replaces it
     for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
         const int i = idx >> 5, d4 = (idx & 31) * 4;
-        st4(&s.X[i][d4], ld4(bw + kBwDKd + i * kDk + d4));
+        cp_async16_rec(&s.X[i][d4], bw + kBwDKd + i * kDk + d4);
     }
+    cp_async_commit_rec();
+    cp_async_wait_rec();
     __syncthreads();
     {  // + e^(gc_last - gc) dKd + the beta e^gc term; dgc -= Kd . dKd, dgc_last += sum Kd . dKd
         float dgl = 0.f;
@@ -801,19 +821,23 @@ cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStr
         if ((e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)k.smem)) != cudaSuccess)
             return e;
     const unsigned nchunks = (unsigned)((int64_t)p.B * p.H * p.NC);
+    // phase events 0-2 come from the forward recompute (before / after its prep, after its scan)
     gdn_bwd_scan<<<dim3((unsigned)(p.B * p.H), kDv / kScanDv), kThreads, sizeof(BwdScanSmem), stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
+    if ((e = phase_event(3, stream)) != cudaSuccess) return e;
     gdn_bwd_states<<<nchunks, kThreads, sizeof(StatesSmem), stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
+    if ((e = phase_event(4, stream)) != cudaSuccess) return e;
     gdn_bwd_wy<<<nchunks, kThreads, sizeof(WySmem), stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
+    if ((e = phase_event(5, stream)) != cudaSuccess) return e;
     gdn_bwd_grads<<<nchunks, kThreads, sizeof(GradSmem), stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
-    return cudaSuccess;
+    return phase_event(6, stream);
 }
 
 }  // namespace gdn

@@ -215,21 +215,24 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_simt(ChunkParams p) {
     for (int c = 0; c < p.NC; ++c) {
         const float* ws = p.ws + ((int64_t)bh * p.NC + c) * kWsChunkFloats;
         __syncthreads();  // previous chunk's readers of the tiles are done
+        // the chunk's tiles, every 16-byte piece in flight at once (asynchronous copies, no register round trip)
         for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
             const int i = idx >> 5, d4 = (idx & 31) * 4;
-            *reinterpret_cast<float4*>(&s.W[i][d4]) = *reinterpret_cast<const float4*>(ws + kWsW + i * kDk + d4);
-            *reinterpret_cast<float4*>(&s.Qg[i][d4]) = *reinterpret_cast<const float4*>(ws + kWsQg + i * kDk + d4);
-            *reinterpret_cast<float4*>(&s.Kd[i][d4]) = *reinterpret_cast<const float4*>(ws + kWsKd + i * kDk + d4);
+            cp_async16_rec(&s.W[i][d4], ws + kWsW + i * kDk + d4);
+            cp_async16_rec(&s.Qg[i][d4], ws + kWsQg + i * kDk + d4);
+            cp_async16_rec(&s.Kd[i][d4], ws + kWsKd + i * kDk + d4);
         }
         for (int idx = tid; idx < kChunk * kChunk / 4; idx += kThreads) {
             const int i = idx >> 4, j4 = (idx & 15) * 4;
-            *reinterpret_cast<float4*>(&s.A[i][j4]) = *reinterpret_cast<const float4*>(ws + kWsAqk + i * kChunk + j4);
+            cp_async16_rec(&s.A[i][j4], ws + kWsAqk + i * kChunk + j4);
         }
         {
             const int i = tid >> 2, q4 = (tid & 3) * 4;
-            *reinterpret_cast<float4*>(&s.U[i][q4]) = *reinterpret_cast<const float4*>(ws + kWsU + i * kDv + dv0 + q4);
+            cp_async16_rec(&s.U[i][q4], ws + kWsU + i * kDv + dv0 + q4);
         }
+        cp_async_commit_rec();
         const float gamma = ws[kWsGamma];
+        cp_async_wait_rec();
         if (p.states) {  // S at the start of chunk c (S is stable here: the last update precedes the barrier above)
             float* dst = p.states + ((int64_t)bh * p.NC + c) * p.states_stride;
             for (int idx = tid; idx < kDk * kScanDv / 4; idx += kThreads) {
