@@ -199,8 +199,10 @@ GDN_API int gdn_chunk_sp_finish(const gdn_tensor* query, const gdn_tensor* key, 
  * inputs and the gradients of its outputs (d_out [B,T,H,Dv], any float dtype) and of its final state
  * (d_final_state [B,H,Dk,Dv] fp32, or NULL for none), writes dq, dk, dv [B,T,H,D] and dg, dbeta
  * [B,T,H] in their descriptors' dtypes and, if dh0 is not NULL, the gradient of the initial state
- * (fp32 [B,H,Dk,Dv]).  Computes in fp32 on CUDA cores (forward recompute, a reverse state scan and
- * three per-chunk kernels); the workspace holds both the recomputed forward and the chunk gradients.
+ * (fp32 [B,H,Dk,Dv]).  Forward recompute, a reverse state scan and three per-chunk kernels; with bf16
+ * q/k/v/d_out (16-byte aligned rows) the recompute's state scan and the reverse scan run on the tensor
+ * cores (bf16 operands, fp32 accumulation), otherwise everything runs in fp32 on CUDA cores.  The
+ * workspace holds the recomputed forward and the chunk gradients.
  * Replaces: torch autograd through torch_chunk_gated_delta_rule (qwen3_5_transformers.py:110-187). */
 GDN_API size_t gdn_chunk_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Dk, int64_t Dv,
                                              int qkv_dtype);

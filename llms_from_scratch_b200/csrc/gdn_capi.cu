@@ -333,7 +333,9 @@ size_t gdn_chunk_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H, int64_t Dk
     (void)qkv_dtype;
     if (B <= 0 || T <= 0 || H <= 0) return 0;
     const int64_t NC = (T + gdn::kChunk - 1) / gdn::kChunk;
-    return (size_t)(B * H * NC) * (size_t)(gdn::kWsChunkFloats + gdn::kBwChunkFloats) * sizeof(float);
+    // CUDA-core forward tiles + backward records + the tensor-core forward records (bf16 inputs)
+    return (size_t)(B * H * NC) * ((size_t)(gdn::kWsChunkFloats + gdn::kBwChunkFloats) * sizeof(float) +
+                                   (size_t)gdn::kTcChunkBytes);
 }
 
 int gdn_chunk_gated_delta_rule_bwd(const gdn_tensor* query, const gdn_tensor* key, const gdn_tensor* value,
@@ -398,6 +400,11 @@ int gdn_chunk_gated_delta_rule_bwd(const gdn_tensor* query, const gdn_tensor* ke
     p.dbeta = {dbeta->data, dbeta->stride[0], dbeta->stride[1], dbeta->stride[2], dbeta->dtype};
     p.fws = reinterpret_cast<float*>(workspace);
     p.bws = p.fws + (size_t)(B * H * f.NC) * gdn::kWsChunkFloats;
+    // bf16 q/k/v/d_out with 16-byte aligned rows: the forward recompute and the reverse scan on the tensor cores
+    p.tc_records = tc_eligible(query, key, value, d_out)
+                       ? reinterpret_cast<void*>(p.bws + (size_t)(B * H * f.NC) * gdn::kBwChunkFloats)
+                       : nullptr;
+    p.err = f.err;
     p.B = f.B;
     p.H = f.H;
     p.NC = f.NC;

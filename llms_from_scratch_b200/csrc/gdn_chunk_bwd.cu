@@ -225,16 +225,91 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_states(BwdParams p) {
     const int64_t t0 = (int64_t)c * kChunk;
     const float* fw = p.fws + ci * kWsChunkFloats;
     float* bw = p.bws + ci * kBwChunkFloats;
-    for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
-        const int i = idx >> 5, d4 = (idx & 31) * 4;
-        cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
-        cp_async16_rec(&s.dVn[i][d4], bw + kBwDVn + i * kDv + d4);
-    }
-    cp_async_commit_rec();
-    for (int i = warp; i < kChunk; i += kThreads / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.dO[i][0]);
-
     const int ty = tid >> 4, tx = tid & 15, c0 = 4 * tx, c1 = 64 + 4 * tx;
     const int ri = tid >> 2, cs = tid & 3;
+    for (int i = warp; i < kChunk; i += kThreads / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.dO[i][0]);
+    if (p.tc_records) {
+        // The tensor-core reverse scan leaves dv_new to this kernel: dv_new = Kd dS_{c+1} + Aqk^T do, with
+        // Kd staged in the dv_new tile and Aqk in the S slab (as [64][64]) until dv_new replaces them.
+        float* sA = &s.S[0][0];
+        for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
+            const int i = idx >> 5, d4 = (idx & 31) * 4;
+            cp_async16_rec(&s.dVn[i][d4], fw + kWsKd + i * kDk + d4);
+        }
+        for (int idx = tid; idx < kChunk * kChunk / 4; idx += kThreads) cp_async16_rec(sA + 4 * idx, fw + kWsAqk + 4 * idx);
+        cp_async_commit_rec();
+        cp_async_wait_rec();
+        __syncthreads();
+        float dvn[4][8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dvn[r][e] = 0.f;
+        for (int j = 0; j < kChunk; ++j) {  // Aqk^T do: Aqk is lower incl. the diagonal (j >= i)
+            const float4 o0 = ld4(&s.dO[j][c0]), o1 = ld4(&s.dO[j][c1]);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const float a = sA[j * kChunk + ty + 16 * r];
+                dvn[r][0] += a * o0.x;
+                dvn[r][1] += a * o0.y;
+                dvn[r][2] += a * o0.z;
+                dvn[r][3] += a * o0.w;
+                dvn[r][4] += a * o1.x;
+                dvn[r][5] += a * o1.y;
+                dvn[r][6] += a * o1.z;
+                dvn[r][7] += a * o1.w;
+            }
+        }
+        for (int slab = 0; slab < 4; ++slab) {  // + Kd dS_{c+1}, 32 rows of dS at a time
+            __syncthreads();
+            for (int idx = tid; idx < 32 * kDv / 4; idx += kThreads) {
+                const int rr = idx >> 5, d4 = (idx & 31) * 4;
+                cp_async16_rec(&s.E[rr][d4], bw + kBwDSe + (int64_t)(32 * slab + rr) * kDv + d4);
+            }
+            cp_async_commit_rec();
+            cp_async_wait_rec();
+            __syncthreads();
+            for (int kk = 0; kk < 32; ++kk) {
+                const float4 e0 = ld4(&s.E[kk][c0]), e1 = ld4(&s.E[kk][c1]);
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const float kd = s.dVn[ty + 16 * r][32 * slab + kk];
+                    dvn[r][0] += kd * e0.x;
+                    dvn[r][1] += kd * e0.y;
+                    dvn[r][2] += kd * e0.z;
+                    dvn[r][3] += kd * e0.w;
+                    dvn[r][4] += kd * e1.x;
+                    dvn[r][5] += kd * e1.y;
+                    dvn[r][6] += kd * e1.z;
+                    dvn[r][7] += kd * e1.w;
+                }
+            }
+        }
+        __syncthreads();  // every reader of Kd is done
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int i = ty + 16 * r;
+            const float4 v0 = make_float4(dvn[r][0], dvn[r][1], dvn[r][2], dvn[r][3]);
+            const float4 v1 = make_float4(dvn[r][4], dvn[r][5], dvn[r][6], dvn[r][7]);
+            st4(&s.dVn[i][c0], v0);
+            st4(&s.dVn[i][c1], v1);
+            st4(bw + kBwDVn + i * kDv + c0, v0);
+            st4(bw + kBwDVn + i * kDv + c1, v1);
+        }
+        for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
+            const int i = idx >> 5, d4 = (idx & 31) * 4;
+            cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
+        }
+        cp_async_commit_rec();
+    } else {
+        for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
+            const int i = idx >> 5, d4 = (idx & 31) * 4;
+            cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
+            cp_async16_rec(&s.dVn[i][d4], bw + kBwDVn + i * kDv + d4);
+        }
+        cp_async_commit_rec();
+    }
+
     float acc[4][8];
 #pragma unroll
     for (int r = 0; r < 4; ++r)
@@ -801,14 +876,26 @@ cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStr
     static_assert(sizeof(BwdScanSmem) <= 227 * 1024 && sizeof(StatesSmem) <= 227 * 1024, "smem");
     static_assert(sizeof(WySmem) <= 227 * 1024 && sizeof(GradSmem) <= 227 * 1024, "smem");
     cudaError_t e;
-    // forward recompute: the CUDA-core prep and scan, the scan recording S_c into the backward workspace
+    // forward recompute, the scan recording S_c into every chunk's backward record
     ChunkParams f = fwd;
-    f.ws = p.fws;
     f.out = nullptr;
     f.hT = nullptr;
-    f.states = p.bws + kBwS;  // S_c into every chunk's backward record
+    f.states = p.bws + kBwS;
     f.states_stride = kBwChunkFloats;
-    if ((e = launch_chunk_simt(f, stream)) != cudaSuccess) return e;
+    if (p.tc_records) {  // tensor-core prep + scan (records M, Q', b, o0), then the CUDA-core prep's tiles
+        f.ws = reinterpret_cast<float*>(p.tc_records);
+        if ((e = phase_event(0, stream)) != cudaSuccess) return e;
+        if ((e = launch_chunk_tc_prep(f, stream)) != cudaSuccess) return e;
+        if ((e = launch_chunk_tc_scan(f, stream)) != cudaSuccess) return e;
+        if ((e = phase_event(1, stream)) != cudaSuccess) return e;
+        f.ws = p.fws;
+        f.states = nullptr;
+        if ((e = launch_chunk_simt_prep(f, stream)) != cudaSuccess) return e;
+        if ((e = phase_event(2, stream)) != cudaSuccess) return e;
+    } else {  // the CUDA-core prep and scan (phase events 0-2 inside)
+        f.ws = p.fws;
+        if ((e = launch_chunk_simt(f, stream)) != cudaSuccess) return e;
+    }
     struct K {
         const void* fn;
         size_t smem;
@@ -821,10 +908,13 @@ cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStr
         if ((e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)k.smem)) != cudaSuccess)
             return e;
     const unsigned nchunks = (unsigned)((int64_t)p.B * p.H * p.NC);
-    // phase events 0-2 come from the forward recompute (before / after its prep, after its scan)
-    gdn_bwd_scan<<<dim3((unsigned)(p.B * p.H), kDv / kScanDv), kThreads, sizeof(BwdScanSmem), stream>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    note_launch();
+    if (p.tc_records) {
+        if ((e = launch_bwd_scan_tc(p, stream)) != cudaSuccess) return e;
+    } else {
+        gdn_bwd_scan<<<dim3((unsigned)(p.B * p.H), kDv / kScanDv), kThreads, sizeof(BwdScanSmem), stream>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        note_launch();
+    }
     if ((e = phase_event(3, stream)) != cudaSuccess) return e;
     gdn_bwd_states<<<nchunks, kThreads, sizeof(StatesSmem), stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;

@@ -885,6 +885,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
         for (int c = 0; c < NC; ++c) {
             const int s = c & 1;
             const unsigned char* st = sm + s * S_STAGE;
+            if (p.states) {  // S_c (fp32) for the backward: row dk, this CTA's 32 columns
+                float* dst = p.states + (rec0 + (int64_t)c * rec_step) * p.states_stride + (int64_t)dk * kDv + dv0;
+#pragma unroll
+                for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
+                    *reinterpret_cast<float4*>(dst + 4 * q4) =
+                        make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
+            }
             // ---- S_{c+1} = M_c S_c + b_c (the sequential path)
             if (ok && scan_aborted(ms)) ok = false;
             if (ok && (!mbar_wait(&ms.mma_s, c & 1, kWaitNs) || !mbar_wait(&ms.full_bo[s], (c >> 1) & 1, kWaitNs)))
@@ -923,7 +930,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                 float o[32];
                 tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + s)), o);
                 tmem_ld_wait();
-                if (!summary) scan_store_output(p, st, o, tbase + (int64_t)c * kChunk, t_lim, warp, lane, b, h, dv0);
+                if (!summary && p.out)
+                    scan_store_output(p, st, o, tbase + (int64_t)c * kChunk, t_lim, warp, lane, b, h, dv0);
                 tc_fence_before();
             }
             if (!ok) ms.abort = 1;
@@ -944,6 +952,202 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tm, kScanTmemCols);
+}
+
+// ============================================================================ reverse scan (backward)
+//
+// dS_c = M_c^T dS_{c+1} + Q'_c^T do_c over the forward's records, chunks in reverse: the transposed affine
+// map of the forward scan (the gradient of S_{c+1} = M_c S_c + b_c, o_c = Q'_c S_c + o0_c).  One CTA per
+// (b, h, 64-column half of Dv).  Warps 0-3 keep the fp32 gradient state (thread = row dk, 64 columns),
+// record dS_{c+1} for the chunk kernels and hand a bf16 copy to warp 6, which issues M^T dS (K = 128) and
+// Q'^T do (K = 64) into one TMEM accumulator from one elected lane of a converged warp; both transposes
+// are the forward's images read MN-major.  Warp 4 bulk-copies the M / Q' images (double-buffered, pulled
+// into L2 four chunks ahead), warp 5 stages do as a swizzled bf16 tile with cp.async (double-buffered).
+constexpr int kBsThreads = 224;
+constexpr int kBsMmaWarp = 6;
+constexpr uint32_t kBsBar = 2;              // named barrier: the state warps (128) arrive, the MMA warp waits
+constexpr uint32_t kBsBarCount = 160;
+constexpr uint32_t kBsTmemCols = 64;        // the 128 x 64 fp32 accumulator
+constexpr uint32_t B_STAGE = 49152;         // M image 32 KiB | Q' image 16 KiB
+constexpr uint32_t B_OFF_Q = 32768;
+constexpr uint32_t B_DO = 2 * B_STAGE;      // do tiles: bf16 [64 t][64 dv] swizzled, 8 KiB each, by parity
+constexpr uint32_t B_STILE = B_DO + 2 * 8192;  // dS operand tiles: bf16 [128 dk][64 dv] swizzled, by parity
+constexpr uint32_t B_MISC = B_STILE + 2 * 16384;
+constexpr uint32_t B_SMEM = B_MISC + 256 + 1024;
+
+struct BsMisc {
+    uint64_t full_mq[2], empty_mq[2], full_do[2], empty_do[2];
+    uint64_t mma;
+    uint32_t tmem;
+    int abort;
+};
+
+__device__ __forceinline__ bool bs_aborted(const BsMisc& ms) { return *reinterpret_cast<const volatile int*>(&ms.abort) != 0; }
+
+__global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    BsMisc& ms = *reinterpret_cast<BsMisc*>(sm + B_MISC);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
+    const int dv0 = blockIdx.y * 64;
+    const int NC = p.NC;
+    const unsigned char* recs = reinterpret_cast<const unsigned char*>(p.tc_records) + (int64_t)bh * NC * kTcChunkBytes;
+    if (tid == 0) {
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&ms.full_mq[s], 1);
+            mbar_init(&ms.empty_mq[s], 1);
+            mbar_init(&ms.full_do[s], 1);
+            mbar_init(&ms.empty_do[s], 1);
+        }
+        mbar_init(&ms.mma, 1);
+        ms.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&ms.tmem, kBsTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = ms.tmem;
+    const uint32_t sbase = smem_u32(sm);
+    bool ok = true;
+    // iteration it handles chunk c = NC - 1 - it with buffers it % 2
+
+    if (warp == kBsMmaWarp) {
+        const uint32_t leader = elect_one();
+        const uint32_t id = make_idesc_f16(128, 64, true, true, true);
+        for (int it = 0; it < NC; ++it) {
+            const int s = it & 1;
+            named_bar_sync(kBsBar, kBsBarCount);  // dS_{c+1} is in operand tile s
+            bool go = ok && !bs_aborted(ms);
+            if (go) go = mbar_wait(&ms.full_mq[s], (it >> 1) & 1, kWaitNs);
+            if (go) go = mbar_wait(&ms.full_do[s], (it >> 1) & 1, kWaitNs);
+            if (!__all_sync(0xffffffffu, go)) {
+                ok = false;
+                ms.abort = 1;
+                continue;
+            }
+            tc_fence_after();
+            const uint32_t mimg = sbase + s * B_STAGE, qimg = mimg + B_OFF_Q;
+            const uint32_t stile = sbase + B_STILE + s * 16384, dtile = sbase + B_DO + s * 8192;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)  // M^T dS: the M image (rows dk, 2 atom columns of k) read MN-major
+                mma_f16_if(leader, tm, make_sdesc(mimg + ks * 2048, 16384, 1024, kSwizzle128B),
+                           make_sdesc(stile + ks * 2048, 16384, 1024, kSwizzle128B), id, ks > 0);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)  // + Q'^T do: the Q' image (rows t, 2 atom columns of k) read MN-major
+                mma_f16_if(leader, tm, make_sdesc(qimg + ks * 2048, 8192, 1024, kSwizzle128B),
+                           make_sdesc(dtile + ks * 2048, 8192, 1024, kSwizzle128B), id, true);
+            mma_commit_if(leader, &ms.mma);
+            mma_commit_if(leader, &ms.empty_mq[s]);
+            mma_commit_if(leader, &ms.empty_do[s]);
+            __syncwarp();
+        }
+    } else if (warp == 4) {
+        if (lane == 0) {  // M / Q' images of the chunk's record
+            int issued = 0;
+            for (int it = 0; it < NC; ++it) {
+                const int s = it & 1, c = NC - 1 - it;
+                if (c >= kScanPrefetch) bulk_prefetch_l2(recs + (int64_t)(c - kScanPrefetch) * kTcChunkBytes, 49152);
+                if (bs_aborted(ms)) break;
+                if (it >= 2 && !mbar_wait(&ms.empty_mq[s], ((it >> 1) - 1) & 1, kWaitNs)) {
+                    ok = false;
+                    break;
+                }
+                const unsigned char* rec = recs + (int64_t)c * kTcChunkBytes;
+                mbar_arrive_expect_tx(&ms.full_mq[s], 49152);
+                bulk_g2s(sm + s * B_STAGE, rec + kTcM, 32768, &ms.full_mq[s]);
+                bulk_g2s(sm + s * B_STAGE + B_OFF_Q, rec + kTcQ, 16384, &ms.full_mq[s]);
+                ++issued;
+            }
+            // leave no copy in flight: wait for the last image of each stage to land
+            for (int it = (issued > 2 ? issued - 2 : 0); it < issued; ++it)
+                if (!mbar_wait(&ms.full_mq[it & 1], (it >> 1) & 1, kWaitNs)) ok = false;
+        }
+    } else if (warp == 5) {  // do tiles: rows t of the chunk, this CTA's 64 columns, zero past T
+        for (int it = 0; it < NC; ++it) {
+            const int s = it & 1, c = NC - 1 - it;
+            bool go = !bs_aborted(ms);
+            if (go && it >= 2) go = mbar_wait(&ms.empty_do[s], ((it >> 1) - 1) & 1, kWaitNs);
+            if (!__all_sync(0xffffffffu, go)) {
+                ok = false;
+                break;
+            }
+            unsigned char* tile = sm + B_DO + s * 8192;
+            for (int piece = lane; piece < kChunk * 8; piece += 32) {
+                const int row = piece >> 3, c8 = piece & 7;
+                const int64_t t = (int64_t)c * kChunk + row;
+                const bool in = t < p.T;
+                const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.dout.p) + (int64_t)b * p.dout.sb +
+                                           (in ? t : 0) * p.dout.st + (int64_t)h * p.dout.sh + dv0 + 8 * c8;
+                cp_async16(tile + sw128_offset(row, 8 * c8, 64), src, in ? 16u : 0u);
+            }
+            cp_async_commit();
+            cp_async_wait_all();
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ms.full_do[s]);
+        }
+    } else {  // warps 0-3: thread = row dk of the gradient state, 64 columns
+        const int dk = tid;
+        float S[64];
+        const int64_t srow = ((int64_t)bh * kDk + dk) * kDv + dv0;
+#pragma unroll
+        for (int q4 = 0; q4 < 16; ++q4) {
+            const float4 v = p.dhT ? *reinterpret_cast<const float4*>(p.dhT + srow + 4 * q4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            S[4 * q4] = v.x;
+            S[4 * q4 + 1] = v.y;
+            S[4 * q4 + 2] = v.z;
+            S[4 * q4 + 3] = v.w;
+        }
+        for (int it = 0; it < NC; ++it) {
+            const int s = it & 1, c = NC - 1 - it;
+            // dS_{c+1} (fp32) for the chunk kernels
+            float* dst = p.bws + ((int64_t)bh * NC + c) * kBwChunkFloats + kBwDSe + (int64_t)dk * kDv + dv0;
+#pragma unroll
+            for (int q4 = 0; q4 < 16; ++q4)
+                *reinterpret_cast<float4*>(dst + 4 * q4) = make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
+            if (ok) {  // tile s was last read by the MMAs of iteration it - 2, complete before iteration it - 1's
+#pragma unroll
+                for (int q8 = 0; q8 < 8; ++q8) store_bf16x8(sm + B_STILE + s * 16384, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
+                fence_proxy_async_smem();
+            }
+            tc_fence_before();
+            named_bar_arrive(kBsBar, kBsBarCount);
+            if (ok && bs_aborted(ms)) ok = false;
+            if (ok && !mbar_wait(&ms.mma, it & 1, kWaitNs)) ok = false;
+            ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+            if (ok) {
+                tc_fence_after();
+                float d[32];
+                tmem_ld32(tmem_addr(tm, 32 * warp, 0), d);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) S[e] = d[e];
+                tmem_ld32(tmem_addr(tm, 32 * warp, 32), d);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) S[32 + e] = d[e];
+                tc_fence_before();
+            }
+            if (!ok) ms.abort = 1;
+        }
+        if (ok && p.dh0) {
+#pragma unroll
+            for (int q4 = 0; q4 < 16; ++q4)
+                *reinterpret_cast<float4*>(p.dh0 + srow + 4 * q4) = make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
+        }
+    }
+    if (!ok) {
+        ms.abort = 1;
+        report(p.err, kErrTimeoutScan);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tm, kBsTmemCols);
 }
 
 // Packed sequences: chunk_base[n] = sum_{m<n} ceil(T_m / 64) and chunk_seq[j] = the sequence of global
@@ -1014,6 +1218,16 @@ cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)((p.cu_seqlens ? p.N : p.B) * p.H), (p.scan_mode == 1 ? 2 : 1) * (kDv / kTcDvTile));
     gdn_scan_tc<<<grid, kScanThreads, S_SMEM, stream>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    note_launch();
+    return cudaSuccess;
+}
+
+cudaError_t launch_bwd_scan_tc(const BwdParams& p, cudaStream_t stream) {
+    static_assert(B_SMEM <= 227 * 1024, "shared memory budget");
+    cudaError_t e = cudaFuncSetAttribute(gdn_bwd_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)B_SMEM);
+    if (e != cudaSuccess) return e;
+    gdn_bwd_scan_tc<<<dim3((unsigned)(p.B * p.H), kDv / 64), kBsThreads, B_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     return cudaSuccess;

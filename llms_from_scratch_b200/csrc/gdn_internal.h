@@ -99,6 +99,11 @@ struct BwdParams {
     Out3 dg, dbeta;
     float* fws;         // forward workspace: kWsChunkFloats per chunk (CUDA-core prep layout)
     float* bws;         // backward workspace: kBwChunkFloats per chunk
+    // Tensor-core records of the forward (kTcChunkBytes per chunk; bf16 q/k/v/d_out): when set, the
+    // forward recompute and the reverse scan run on the tensor cores and the chunk kernels form
+    // dv_new themselves.  Null: the CUDA-core scans.
+    void* tc_records;
+    unsigned int* err;
     int B, H, NC;
     int64_t T;
     int l2norm;
@@ -107,6 +112,11 @@ struct BwdParams {
 // Backward of the chunked rule (CUDA-core, fp32): forward recompute (prep + scan recording the
 // chunk-start states), reverse state scan, then three per-chunk gradient kernels.
 cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStream_t stream);
+// Reverse scan on the tensor cores over the forward's records (p.tc_records): dS_c = M_c^T dS_{c+1} +
+// Q'_c^T do_c; records dS_{c+1} per chunk and writes dh0.
+cudaError_t launch_bwd_scan_tc(const BwdParams& p, cudaStream_t stream);
+// The CUDA-core prep alone (u, w, Qg, Kd, Aqk, e^gc_last per chunk into p.ws).
+cudaError_t launch_chunk_simt_prep(const ChunkParams& p, cudaStream_t stream);
 
 struct RecurrentParams {
     View4 q, k, v;

@@ -233,9 +233,11 @@ def test_bwd_entry_rejects_bad_arguments_before_any_cuda_call(lib, case, needle)
 def test_bwd_workspace_size(lib):
     f = lib.gdn_chunk_bwd_workspace_bytes
     assert f(1, 0, 4, 128, 128, _lib.GDN_BF16) == 0
-    # forward record (36,928 floats) + backward record (90,304 floats) per (b, h, chunk)
-    assert f(1, 64, 1, 128, 128, _lib.GDN_BF16) == (36928 + 90304) * 4
-    assert f(2, 4096, 16, 128, 128, _lib.GDN_F32) == 2 * 16 * 64 * (36928 + 90304) * 4
+    # per (b, h, chunk): CUDA-core forward tiles (36,928 floats) + backward record (90,304 floats) + the
+    # tensor-core forward record (147,456 bytes)
+    per = (36928 + 90304) * 4 + 147456
+    assert f(1, 64, 1, 128, 128, _lib.GDN_BF16) == per
+    assert f(2, 4096, 16, 128, 128, _lib.GDN_F32) == 2 * 16 * 64 * per
 
 
 def test_final_state_pointer_required(lib):
