@@ -18,7 +18,7 @@
 // hi + lo pair of bf16 (two MMAs), so the prep is fp32-accurate.  The scan
 // feeds M_c, Q'_c and S_c to the MMA in bf16 and keeps S, b and o0 in fp32.
 //
-// gdn_prep_tc: one CTA (8 warps) per (batch, head, 64-token chunk), two CTAs per
+// gdn_prep_tc: one CTA (16 warps) per (batch, head, 64-token chunk), two CTAs per
 // SM (105 KB of shared memory each, one work region reused phase by phase), so
 // one CTA's memory and barrier waits overlap the other's work; the output images
 // leave with asynchronous bulk copies.  Operands that share a B matrix are
@@ -74,7 +74,10 @@ __device__ __forceinline__ void split_bf16(float x, float& hi, float& lo) {
 
 // ============================================================================ prep
 
-constexpr int kPrepThreads = 256;          // 8 warps; two CTAs share an SM
+constexpr int kPrepThreads = 512;          // 16 warps; two CTAs share an SM (32 warps to hide latency)
+constexpr int kPrepWarps = kPrepThreads / 32;
+constexpr int kL2Rows = 2;                              // rows a warp normalises together
+constexpr int kL2Batches = kChunk / (kL2Rows * kPrepWarps);
 constexpr uint32_t P_KQ = 0;               // bf16 [128 rows][128] swizzled: rows 0-63 k^, 64-127 q^ (atom columns 16 KiB apart)
 constexpr uint32_t P_V = 32768;            // bf16 [64 rows][128] swizzled v (atom columns 8 KiB apart)
 constexpr uint32_t P_W = 49152;            // work region, reused phase by phase:
@@ -169,7 +172,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     float(*sY)[16][16] = reinterpret_cast<float(*)[16][16]>(sm + P_Y3);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int quad = warp & 3, half = warp >> 2;  // TMEM lane quadrant, column half
+    const int quad = warp & 3, part = warp >> 2;  // TMEM lane quadrant, 16-column part of each 64
     // Chunks run latest first across all heads (block i -> chunk NC-1 - i/(B*H)), so the records the scan
     // reads first are the ones written last, still in L2 when the scan starts (a long sequence's records
     // do not all fit).  t0 is the chunk's first token, t_lim the end of its sequence.
@@ -231,17 +234,17 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     cp_async_wait_all();
     __syncthreads();
     // ---- 1. normalised rows -> swizzled bf16 tiles (qwen3_5_transformers.py:122-137).
-    //      Each warp owns 8 rows of the staged copy, in two batches of 4 whose 8 sums of squares
-    //      are reduced together.  The inverse norm uses rsqrtf before its
+    //      Each warp owns 4 rows of the staged copy, in batches of 2 whose 4 sums of squares are
+    //      reduced together.  The inverse norm uses rsqrtf before its
     //      bf16 rounding: it differs from a correctly rounded 1/sqrt only within ~2 fp32 ulp of a bf16
     //      rounding boundary (the reference's own CPU bf16 rsqrt is an estimate as well).
 #pragma unroll
-    for (int batch = 0; batch < 2; ++batch) {
-        constexpr int kRows = 4;
+    for (int batch = 0; batch < kL2Batches; ++batch) {
+        constexpr int kRows = kL2Rows;
         float q[kRows][4], k[kRows][4], v[kRows][4], ss[2 * kRows];
 #pragma unroll
         for (int rr = 0; rr < kRows; ++rr) {
-            const int row = warp + 8 * (4 * batch + rr);
+            const int row = warp + kPrepWarps * (kRows * batch + rr);
             load_bf16x4_smem(sm + P_RAW + (0 * kChunk + row) * 256 + 8 * lane, q[rr]);
             load_bf16x4_smem(sm + P_RAW + (1 * kChunk + row) * 256 + 8 * lane, k[rr]);
             load_bf16x4_smem(sm + P_RAW + (2 * kChunk + row) * 256 + 8 * lane, v[rr]);
@@ -264,7 +267,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         }
 #pragma unroll
         for (int rr = 0; rr < kRows; ++rr) {
-            const int r = warp + 8 * (4 * batch + rr);
+            const int r = warp + kPrepWarps * (kRows * batch + rr);
             if (p.l2norm && t0 + r < t_lim) {
                 const float iq = round_to(rsqrtf(round_to(round_to(ss[2 * rr], GDN_BF16) + 1e-6f, GDN_BF16)), GDN_BF16);
                 const float ik = round_to(rsqrtf(round_to(round_to(ss[2 * rr + 1], GDN_BF16) + 1e-6f, GDN_BF16)), GDN_BF16);
@@ -317,28 +320,28 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
 
     // ---- 3. L = -(beta_i G_k e^(gc_i-gc_j)) strictly lower (:152-153), Aqk = Dk^-1/2 G_q e^(gc_i-gc_j) causal (:172)
     if (!__syncthreads_or(!ok)) {
-        float gv[32];
-        tmem_ld32(tmem_addr(tm, 32 * quad, 32 * half), gv);
+        float gv[16];
+        tmem_ld16(tmem_addr(tm, 32 * quad, 16 * part), gv);
         tmem_ld_wait();
         const int r = 32 * quad + lane, i = r & 63;
         const float gci = ms.gc[i];
         if (r < 64) {
             const float bi = ms.beta[i];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int j = 32 * half + e;
+            for (int e = 0; e < 16; ++e) {
+                const int j = 16 * part + e;
                 sL[i][j] = (j < i) ? -(bi * gv[e]) * __expf(gci - ms.gc[j]) : 0.f;
             }
         } else {  // Aqk rows as the hi/lo bf16 A operand of step 5 (K-major, one atom column)
-            float a[32];
+            float a[16];
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int j = 32 * half + e;
+            for (int e = 0; e < 16; ++e) {
+                const int j = 16 * part + e;
                 a[e] = (j <= i) ? (scale * gv[e]) * __expf(gci - ms.gc[j]) : 0.f;
             }
 #pragma unroll
-            for (int q8 = 0; q8 < 4; ++q8)
-                store_split8(sm + P_AQK, sm + P_AQK + 8192, sw128_offset(i, 32 * half + 8 * q8, 64), a + 8 * q8);
+            for (int q8 = 0; q8 < 2; ++q8)
+                store_split8(sm + P_AQK, sm + P_AQK + 8192, sw128_offset(i, 16 * part + 8 * q8, 64), a + 8 * q8);
         }
     } else {
         ok = false;
@@ -450,19 +453,17 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     //      passes (hi.hi + hi.lo + lo.hi) into TMEM cols [0,64) (G is dead).  Rows of the M=64
     //      accumulator sit in lanes 0-15 of each 32-lane quadrant.
     if (ok) {
-        const int m = tid >> 2, c0 = 16 * (tid & 3);
-        float tv[16];
+        const int m = tid >> 3, c0 = 8 * (tid & 7);
+        float tv[8];
 #pragma unroll
-        for (int e4 = 0; e4 < 4; ++e4) {
+        for (int e4 = 0; e4 < 2; ++e4) {
             const float4 x = *reinterpret_cast<const float4*>(&sT[m][c0 + 4 * e4]);
             tv[4 * e4] = x.x;
             tv[4 * e4 + 1] = x.y;
             tv[4 * e4 + 2] = x.z;
             tv[4 * e4 + 3] = x.w;
         }
-#pragma unroll
-        for (int h8 = 0; h8 < 2; ++h8)
-            store_split8(sm + P_TT, sm + P_TT + 8192, sw128_offset(m, c0 + 8 * h8, 64), tv + 8 * h8);
+        store_split8(sm + P_TT, sm + P_TT + 8192, sw128_offset(m, c0, 64), tv);
     }
     fence_proxy_async_smem();
     __syncthreads();
@@ -482,17 +483,17 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);  // second completion of the barrier
     ok = !__syncthreads_or(!ok);
     tc_fence_after();
-    // Thread (quadrant, lane, half) holds 32 columns jc.. of one coefficient row ri: lanes 16-31 the row
+    // Thread (quadrant, lane, part) holds 16 columns jc.. of one coefficient row ri: lanes 16-31 the row
     // of T (-> X, Y), lanes 0-15 the row of Aqk T (-> Z, W).
     const bool top = lane >= 16;
-    const int ri = 16 * quad + (lane & 15), jc = 32 * half;
-    float cv[32];
+    const int ri = 16 * quad + (lane & 15), jc = 16 * part;
+    float cv[16];
     if (ok) {
-        tmem_ld32(tmem_addr(tm, 32 * quad, jc), cv);
+        tmem_ld16(tmem_addr(tm, 32 * quad, jc), cv);
         tmem_ld_wait();
         if (top) {
 #pragma unroll
-            for (int e4 = 0; e4 < 8; ++e4) {
+            for (int e4 = 0; e4 < 4; ++e4) {
                 const float4 x = *reinterpret_cast<const float4*>(&sT[ri][jc + 4 * e4]);
                 cv[4 * e4] = x.x;
                 cv[4 * e4 + 1] = x.y;
@@ -510,9 +511,9 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     const float rowc = top ? ms.ekd[ri] : 1.f;
     uint32_t ph = 1;
     for (int round = 0; round < 2 && ok; ++round) {
-        float x[32];  // row ri (X or Y) or 64+ri (Z or W)
+        float x[16];  // row ri (X or Y) or 64+ri (Z or W)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
+        for (int e = 0; e < 16; ++e) {
             const int j = jc + e;
             const float bj = ms.beta[j];
             const float bb = round == 0 ? bj * ms.egc[j] : bj;
@@ -521,7 +522,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         unsigned char* at_hi = sm + P_ATILE;
         unsigned char* at_lo = sm + P_ATILE + 16384;
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8)
+        for (int q8 = 0; q8 < 2; ++q8)
             store_split8(at_hi, at_lo, sw128_offset(top ? ri : 64 + ri, jc + 8 * q8, 128), x + 8 * q8);
         fence_proxy_async_smem();
         __syncthreads();
@@ -541,19 +542,19 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     if (ok) {
         const int r = 32 * quad + lane, i = r & 63;
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-            float v[32];
-            const int d0 = 64 * half + 32 * cc;
-            tmem_ld32(tmem_addr(tm, 32 * quad, d0), v);
+        for (int cc = 0; cc < 2; ++cc) {  // this thread's 32 columns, 16 at a time
+            float v[16];
+            const int d0 = 32 * part + 16 * cc;
+            tmem_ld16(tmem_addr(tm, 32 * quad, d0), v);
             tmem_ld_wait();
             if (r < 64) {  // P_X (MN-major B tile: rows = tokens)
 #pragma unroll
-                for (int q8 = 0; q8 < 4; ++q8)
+                for (int q8 = 0; q8 < 2; ++q8)
                     store_split8(sm + P_PX, sm + P_PX + 16384, sw128_offset(i, d0 + 8 * q8, 64), v + 8 * q8);
             } else {  // Q' = q^ Dk^-1/2 e^gc - Zk (the q e^gc S of :175 and -Aqk w S of :176 combined)
                 const float qs = scale * ms.egc[i];
 #pragma unroll
-                for (int q8 = 0; q8 < 4; ++q8) {
+                for (int q8 = 0; q8 < 2; ++q8) {
                     const uint32_t off = sw128_offset(64 + i, d0 + 8 * q8, 128);
                     const uint4 qu = *reinterpret_cast<const uint4*>(sm + P_KQ + off);
                     const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(&qu);
@@ -566,19 +567,19 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         }
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
-            float v[32];
-            const int d0 = 64 * half + 32 * cc;
-            tmem_ld32(tmem_addr(tm, 32 * quad, 128 + d0), v);
+            float v[16];
+            const int d0 = 32 * part + 16 * cc;
+            tmem_ld16(tmem_addr(tm, 32 * quad, 128 + d0), v);
             tmem_ld_wait();
             if (r < 64) {  // P_Y
 #pragma unroll
-                for (int q8 = 0; q8 < 4; ++q8)
+                for (int q8 = 0; q8 < 2; ++q8)
                     store_split8(sm + P_PYH, sm + P_PYL, sw128_offset(i, d0 + 8 * q8, 64), v + 8 * q8);
             } else {  // o0 = Aqk u, fp32 column tile d0/32, straight to the workspace
                 unsigned char* blk = wrec + kTcO0 + (d0 >> 5) * (64 * 128);
 #pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4)
-                    *reinterpret_cast<float4*>(blk + f32blk_offset(i, q4)) =
+                for (int q4 = 0; q4 < 4; ++q4)
+                    *reinterpret_cast<float4*>(blk + f32blk_offset(i, ((d0 & 31) >> 2) + q4)) =
                         make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
             }
         }
@@ -621,12 +622,12 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         const float gamma = ms.egc[kChunk - 1];
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
-            float v[32];
-            const int c0 = 64 * half + 32 * cc;
-            tmem_ld32(tmem_addr(tm, 32 * quad, c0), v);
+            float v[16];
+            const int c0 = 32 * part + 16 * cc;
+            tmem_ld16(tmem_addr(tm, 32 * quad, c0), v);
             tmem_ld_wait();
 #pragma unroll
-            for (int q8 = 0; q8 < 4; ++q8) {
+            for (int q8 = 0; q8 < 2; ++q8) {
                 const int col = c0 + 8 * q8;
                 float m[8];
 #pragma unroll
@@ -637,14 +638,14 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         const uint32_t btile[4] = {P_V, P_W, P_W + 16384, P_W + 32768};
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
-            float v[32];
-            const int c0 = 64 * half + 32 * cc;
-            tmem_ld32(tmem_addr(tm, 32 * quad, 128 + c0), v);
+            float v[16];
+            const int c0 = 32 * part + 16 * cc;
+            tmem_ld16(tmem_addr(tm, 32 * quad, 128 + c0), v);
             tmem_ld_wait();
             unsigned char* blk = sm + btile[c0 >> 5];
 #pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4)
-                *reinterpret_cast<float4*>(blk + f32blk_offset(dk, q4)) =
+            for (int q4 = 0; q4 < 4; ++q4)
+                *reinterpret_cast<float4*>(blk + f32blk_offset(dk, ((c0 & 31) >> 2) + q4)) =
                     make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
         }
     } else {
