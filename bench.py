@@ -626,9 +626,9 @@ def main():
     dec_bytes = Bd * H * (2 * STATE_BYTES + 4 * D * 2 + 8)
     peak_l, _ = load_peaks()
     layer_kernels = time_layer_kernels(torch, lib, flush, device, T, H, Bd, peak_l)
+    backward = time_backward(torch, lib, flush, device, T, H)
     fla, fla_err = load_fla() if args.fla else (None, None)
     packed = time_packed(torch, flush, device, H, peak_l, fla=fla)
-    backward = time_backward(torch, lib, flush, device, T, H)
     fla_headline = None
     if args.fla:
         if fla is None:

@@ -127,3 +127,4 @@ def test_bwd_strided_views_and_empty():
     e = chunk_gated_delta_rule_bwd(q[:, :0], k[:, :0], v[:, :0], g[:, :0], beta[:, :0], do[:, :0],
                                    initial_state=h0, d_final_state=dhT)
     assert torch.equal(e[5], dhT) and e[0].shape == (1, 0, 2, 128)
+
