@@ -916,9 +916,13 @@ cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStr
         note_launch();
     }
     if ((e = phase_event(3, stream)) != cudaSuccess) return e;
-    gdn_bwd_states<<<nchunks, kThreads, sizeof(StatesSmem), stream>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    note_launch();
+    if (p.tc_records) {  // bf16 mode: the state products on the tensor cores
+        if ((e = launch_bwd_states_tc(p, stream)) != cudaSuccess) return e;
+    } else {
+        gdn_bwd_states<<<nchunks, kThreads, sizeof(StatesSmem), stream>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        note_launch();
+    }
     if ((e = phase_event(4, stream)) != cudaSuccess) return e;
     gdn_bwd_wy<<<nchunks, kThreads, sizeof(WySmem), stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;

@@ -1151,6 +1151,267 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
     if (warp == 0) tmem_dealloc(tm, kBsTmemCols);
 }
 
+// ============================================================================ backward: state products
+//
+// Per chunk, on the tensor cores, the products of the backward that involve the chunk-start state S_c and
+// the end-state gradient dS' = dS_{c+1} (both fp32, entered as hi/lo bf16 pairs):
+//   (1) dv_new = Kd dS' + Aqk^T do          (M=64; Aqk^T is Aqk's rows read MN-major, do exact bf16)
+//   (2) v_new = u - w S                      (M=64)
+//   (3) [dQg; -dw] = [do; dv_new] S^T        (M=128)
+//   (4) dKd = v_new dS'^T                    (M=64)
+// S and dS' are staged once as swizzled bf16 [128 dk][128 dv] tiles: an MN-major B operand for (1)/(2)
+// (K = dk) and a K-major B operand for (3)/(4) (N = dk, K = dv).  Three MMA passes (hi.hi, hi.lo, lo.hi)
+// per fp32 x fp32 product keep them fp32-accurate.  One CTA of 256 threads per chunk.
+constexpr int kBtThreads = 256;
+constexpr uint32_t T_DS = 0;          // dS' hi | lo (32 KiB each): bf16 [128 dk][128 dv], atom columns of 16 KiB
+constexpr uint32_t T_S = 65536;       // S hi | lo, same layout
+constexpr uint32_t T_DOB = 131072;    // do as the B operand of (1): bf16 [64 t][128 dv], atom columns of 8 KiB;
+                                      // then v_new hi for (4)
+constexpr uint32_t T_A = 147456;      // A operands (80 KiB): (1)-(2) Kd hi|lo +0/+16K, Aqk hi|lo +32K/+40K, w hi|lo
+                                      // +48K/+64K; (3) [do; dv_new] hi|lo +0/+32K; (4) v_new lo +64K
+constexpr uint32_t T_MISC = T_A + 81920;
+constexpr uint32_t T_SMEM = T_MISC + 256 + 1024;
+constexpr uint32_t kBtTmemCols = 512;  // (1) [0,128)  (2) [128,256)  (3) [256,384)  (4) [384,512)
+
+struct BtMisc {
+    uint64_t bar;
+    uint32_t tmem;
+    float red[kBtThreads / 32];
+};
+
+__global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    BtMisc& ms = *reinterpret_cast<BtMisc*>(sm + T_MISC);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t ci = blockIdx.x;
+    const int c = (int)(ci % p.NC), bh = (int)(ci / p.NC), b = bh / p.H, h = bh % p.H;
+    const int64_t t0 = (int64_t)c * kChunk;
+    const float* fw = p.fws + ci * kWsChunkFloats;
+    float* bw = p.bws + ci * kBwChunkFloats;
+    if (tid == 0) {
+        mbar_init(&ms.bar, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&ms.tmem, kBtTmemCols);
+        tmem_relinquish();
+    }
+    // ---- staging: S and dS' (and <S, dS'>), Kd, Aqk, w as hi/lo tiles; do as an exact bf16 tile
+    // Loads are issued in batches (16 float4 per thread in flight) before any conversion: a store to shared
+    // memory between two global loads would otherwise serialise them.
+    float dgam = 0.f;
+    for (int base = tid; base < kDk * kDv / 8; base += 4 * kBtThreads) {  // S and dS': 8 groups of 8 per thread
+        float4 v[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int idx = base + u * kBtThreads, r = idx >> 4, c8 = (idx & 15) * 8;
+            v[u][0] = *reinterpret_cast<const float4*>(bw + kBwS + r * kDv + c8);
+            v[u][1] = *reinterpret_cast<const float4*>(bw + kBwS + r * kDv + c8 + 4);
+            v[u][2] = *reinterpret_cast<const float4*>(bw + kBwDSe + r * kDv + c8);
+            v[u][3] = *reinterpret_cast<const float4*>(bw + kBwDSe + r * kDv + c8 + 4);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int idx = base + u * kBtThreads, r = idx >> 4, c8 = (idx & 15) * 8;
+            const uint32_t off = sw128_offset(r, c8, 128);
+            const float sx[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w, v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+            const float ex[8] = {v[u][2].x, v[u][2].y, v[u][2].z, v[u][2].w, v[u][3].x, v[u][3].y, v[u][3].z, v[u][3].w};
+            store_split8(sm + T_S, sm + T_S + 32768, off, sx);
+            store_split8(sm + T_DS, sm + T_DS + 32768, off, ex);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dgam += sx[e] * ex[e];
+        }
+    }
+    {  // Kd and w: 4 groups each per thread; Aqk (rows j, columns t: the MN-major A^T): 2 groups
+        float4 v[4][4], a[2][2];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int idx = tid + u * kBtThreads, r = idx >> 4, c8 = (idx & 15) * 8;
+            v[u][0] = *reinterpret_cast<const float4*>(fw + kWsKd + r * kDk + c8);
+            v[u][1] = *reinterpret_cast<const float4*>(fw + kWsKd + r * kDk + c8 + 4);
+            v[u][2] = *reinterpret_cast<const float4*>(fw + kWsW + r * kDk + c8);
+            v[u][3] = *reinterpret_cast<const float4*>(fw + kWsW + r * kDk + c8 + 4);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int idx = tid + u * kBtThreads, r = idx >> 3, c8 = (idx & 7) * 8;
+            a[u][0] = *reinterpret_cast<const float4*>(fw + kWsAqk + r * kChunk + c8);
+            a[u][1] = *reinterpret_cast<const float4*>(fw + kWsAqk + r * kChunk + c8 + 4);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int idx = tid + u * kBtThreads, r = idx >> 4, c8 = (idx & 15) * 8;
+            const uint32_t off = sw128_offset(r, c8, 64);
+            const float kx[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w, v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+            const float wx[8] = {v[u][2].x, v[u][2].y, v[u][2].z, v[u][2].w, v[u][3].x, v[u][3].y, v[u][3].z, v[u][3].w};
+            store_split8(sm + T_A, sm + T_A + 16384, off, kx);
+            store_split8(sm + T_A + 49152, sm + T_A + 65536, off, wx);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int idx = tid + u * kBtThreads, r = idx >> 3, c8 = (idx & 7) * 8;
+            const float ax[8] = {a[u][0].x, a[u][0].y, a[u][0].z, a[u][0].w, a[u][1].x, a[u][1].y, a[u][1].z, a[u][1].w};
+            store_split8(sm + T_A + 32768, sm + T_A + 40960, sw128_offset(r, c8, 64), ax);
+        }
+    }
+    for (int idx = tid; idx < kChunk * kDv / 8; idx += kBtThreads) {  // do rows t (zero past T)
+        const int r = idx >> 4, c8 = (idx & 15) * 8;
+        const int64_t t = t0 + r;
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (t < p.T)
+            u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.dout.p) + (int64_t)b * p.dout.sb +
+                                                t * p.dout.st + (int64_t)h * p.dout.sh + c8);
+        *reinterpret_cast<uint4*>(sm + T_DOB + sw128_offset(r, c8, 64)) = u;
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = ms.tmem, sb = smem_u32(sm);
+    // pass p: (A hi, B hi), (A hi, B lo), (A lo, B hi)
+    const uint32_t pa[3] = {0u, 0u, 1u}, pb[3] = {0u, 1u, 0u};
+    if (tid == 0) {
+        const uint32_t id_kmn = make_idesc_f16(64, 128, false, true, true);  // A K-major, B MN-major
+        const uint32_t id_mnmn = make_idesc_f16(64, 128, true, true, true);  // A MN-major, B MN-major
+        // (1) Kd dS' + Aqk^T do -> [0,128)
+        bool acc = false;
+        for (int ps = 0; ps < 3; ++ps)
+            for (int ks = 0; ks < 8; ++ks, acc = true)
+                mma_f16(tm, make_sdesc(sb + T_A + pa[ps] * 16384 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024, kSwizzle128B),
+                        make_sdesc(sb + T_DS + pb[ps] * 32768 + ks * 2048, 16384, 1024, kSwizzle128B), id_kmn, acc);
+        for (int ps = 0; ps < 2; ++ps)
+            for (int ks = 0; ks < 4; ++ks)
+                mma_f16(tm, make_sdesc(sb + T_A + 32768 + ps * 8192 + ks * 2048, 8192, 1024, kSwizzle128B),
+                        make_sdesc(sb + T_DOB + ks * 2048, 8192, 1024, kSwizzle128B), id_mnmn, true);
+        // (2) w S -> [128,256)
+        acc = false;
+        for (int ps = 0; ps < 3; ++ps)
+            for (int ks = 0; ks < 8; ++ks, acc = true)
+                mma_f16(tm + 128, make_sdesc(sb + T_A + 49152 + pa[ps] * 16384 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024, kSwizzle128B),
+                        make_sdesc(sb + T_S + pb[ps] * 32768 + ks * 2048, 16384, 1024, kSwizzle128B), id_kmn, acc);
+        mma_commit(&ms.bar);
+    }
+    bool ok = mbar_wait(&ms.bar, 0, kWaitNs);
+    ok = !__syncthreads_or(!ok);
+    tc_fence_after();
+    // ---- dv_new, v_new from the accumulators (M=64: rows 16 q + l in lanes 32 q + l, l < 16); warps w and
+    //      w + 4 share a quadrant and split the 128 columns
+    const int q = warp & 3, chalf = warp >> 2, row = 16 * q + (lane & 15);
+    const bool rl = lane < 16;
+    if (ok) {
+        for (int part = 0; part < 2; ++part) {
+            float d[32];
+            const int col0 = 64 * chalf + 32 * part;
+            tmem_ld32(tmem_addr(tm, 32 * q, col0), d);  // dv_new
+            tmem_ld_wait();
+            if (rl) {
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4)
+                    *reinterpret_cast<float4*>(bw + kBwDVn + row * kDv + col0 + 4 * q4) =
+                        make_float4(d[4 * q4], d[4 * q4 + 1], d[4 * q4 + 2], d[4 * q4 + 3]);
+#pragma unroll
+                for (int q8 = 0; q8 < 4; ++q8)  // rows 64.. of the (3) A tile
+                    store_split8(sm + T_A, sm + T_A + 32768, sw128_offset(64 + row, col0 + 8 * q8, 128), d + 8 * q8);
+            }
+            tmem_ld32(tmem_addr(tm, 32 * q, 128 + col0), d);  // w S
+            tmem_ld_wait();
+            if (rl) {
+                float vn[32];
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4) {
+                    const float4 u = *reinterpret_cast<const float4*>(fw + kWsU + row * kDv + col0 + 4 * q4);
+                    vn[4 * q4] = u.x - d[4 * q4];
+                    vn[4 * q4 + 1] = u.y - d[4 * q4 + 1];
+                    vn[4 * q4 + 2] = u.z - d[4 * q4 + 2];
+                    vn[4 * q4 + 3] = u.w - d[4 * q4 + 3];
+                    *reinterpret_cast<float4*>(bw + kBwVn + row * kDv + col0 + 4 * q4) =
+                        make_float4(vn[4 * q4], vn[4 * q4 + 1], vn[4 * q4 + 2], vn[4 * q4 + 3]);
+                }
+#pragma unroll
+                for (int q8 = 0; q8 < 4; ++q8)  // the (4) A tile: hi in place of do's B tile, lo after the w tiles
+                    store_split8(sm + T_DOB, sm + T_A + 65536, sw128_offset(row, col0 + 8 * q8, 64), vn + 8 * q8);
+            }
+        }
+    }
+    for (int idx = tid; idx < kChunk * kDv / 8; idx += kBtThreads) {  // rows 0..63 of the (3) A tile: do, lo = 0
+        const int r = idx >> 4, c8 = (idx & 15) * 8;
+        const int64_t t = t0 + r;
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (t < p.T)
+            u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.dout.p) + (int64_t)b * p.dout.sb +
+                                                t * p.dout.st + (int64_t)h * p.dout.sh + c8);
+        const uint32_t off = sw128_offset(r, c8, 128);
+        *reinterpret_cast<uint4*>(sm + T_A + off) = u;
+        *reinterpret_cast<uint4*>(sm + T_A + 32768 + off) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (ok && tid == 0) {
+        const uint32_t id_kk128 = make_idesc_f16(128, 128, false, false, true);
+        const uint32_t id_kk64 = make_idesc_f16(64, 128, false, false, true);
+        // (3) [do; dv_new] S^T -> [256,384): A K-major [128][128] (atom columns of 16 KiB), B = S K-major
+        bool acc = false;
+        for (int ps = 0; ps < 3; ++ps)
+            for (int ks = 0; ks < 8; ++ks, acc = true)
+                mma_f16(tm + 256, make_sdesc(sb + T_A + pa[ps] * 32768 + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSwizzle128B),
+                        make_sdesc(sb + T_S + pb[ps] * 32768 + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSwizzle128B),
+                        id_kk128, acc);
+        // (4) v_new dS'^T -> [384,512): A K-major [64][128] (atom columns of 8 KiB), B = dS' K-major
+        const uint32_t vh = sb + T_DOB, vl = sb + T_A + 65536;
+        acc = false;
+        for (int ps = 0; ps < 3; ++ps)
+            for (int ks = 0; ks < 8; ++ks, acc = true)
+                mma_f16(tm + 384, make_sdesc((pa[ps] ? vl : vh) + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024, kSwizzle128B),
+                        make_sdesc(sb + T_DS + pb[ps] * 32768 + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSwizzle128B),
+                        id_kk64, acc);
+        mma_commit(&ms.bar);
+    }
+    if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);
+    ok = !__syncthreads_or(!ok);
+    tc_fence_after();
+    if (ok) {
+        // (3): row r = 32 q + lane (M=128), columns split by warp / 4
+        const int r = 32 * q + lane;
+        for (int part = 0; part < 2; ++part) {
+            float d[32];
+            const int col0 = 64 * chalf + 32 * part;
+            tmem_ld32(tmem_addr(tm, 32 * q, 256 + col0), d);
+            tmem_ld_wait();
+            float* dst = r < 64 ? bw + kBwDQg + r * kDk + col0 : bw + kBwDW + (r - 64) * kDk + col0;
+            const float sgn = r < 64 ? 1.f : -1.f;
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4)
+                *reinterpret_cast<float4*>(dst + 4 * q4) =
+                    make_float4(sgn * d[4 * q4], sgn * d[4 * q4 + 1], sgn * d[4 * q4 + 2], sgn * d[4 * q4 + 3]);
+            tmem_ld32(tmem_addr(tm, 32 * q, 384 + col0), d);  // (4), M=64
+            tmem_ld_wait();
+            if (rl) {
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4)
+                    *reinterpret_cast<float4*>(bw + kBwDKd + row * kDk + col0 + 4 * q4) =
+                        make_float4(d[4 * q4], d[4 * q4 + 1], d[4 * q4 + 2], d[4 * q4 + 3]);
+            }
+        }
+    }
+    dgam = warp_sum(dgam);
+    if (lane == 0) ms.red[warp] = dgam;
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.f;
+        for (int w = 0; w < kBtThreads / 32; ++w) t += ms.red[w];
+        bw[kBwSmall] = t;
+        if (!ok) report(p.err, kErrTimeoutPrep);
+    }
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tm, kBtTmemCols);
+    }
+}
+
 // Packed sequences: chunk_base[n] = sum_{m<n} ceil(T_m / 64) and chunk_seq[j] = the sequence of global
 // chunk j, from the device's cu_seqlens, so the host never reads the offsets.  One CTA: each thread
 // counts the chunks of a contiguous run of sequences, a block scan turns the counts into bases, and
@@ -1219,6 +1480,16 @@ cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)((p.cu_seqlens ? p.N : p.B) * p.H), (p.scan_mode == 1 ? 2 : 1) * (kDv / kTcDvTile));
     gdn_scan_tc<<<grid, kScanThreads, S_SMEM, stream>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    note_launch();
+    return cudaSuccess;
+}
+
+cudaError_t launch_bwd_states_tc(const BwdParams& p, cudaStream_t stream) {
+    static_assert(T_SMEM <= 227 * 1024, "shared memory budget");
+    cudaError_t e = cudaFuncSetAttribute(gdn_bwd_states_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)T_SMEM);
+    if (e != cudaSuccess) return e;
+    gdn_bwd_states_tc<<<(unsigned)((int64_t)p.B * p.H * p.NC), kBtThreads, T_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     return cudaSuccess;

@@ -115,6 +115,9 @@ cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStr
 // Reverse scan on the tensor cores over the forward's records (p.tc_records): dS_c = M_c^T dS_{c+1} +
 // Q'_c^T do_c; records dS_{c+1} per chunk and writes dh0.
 cudaError_t launch_bwd_scan_tc(const BwdParams& p, cudaStream_t stream);
+// The backward's products with S_c and dS_{c+1} on the tensor cores (p.tc_records mode): dv_new, v_new,
+// dQg, dw, dKd and <S_c, dS_{c+1}> into every chunk's backward record.
+cudaError_t launch_bwd_states_tc(const BwdParams& p, cudaStream_t stream);
 // The CUDA-core prep alone (u, w, Qg, Kd, Aqk, e^gc_last per chunk into p.ws).
 cudaError_t launch_chunk_simt_prep(const ChunkParams& p, cudaStream_t stream);
 
