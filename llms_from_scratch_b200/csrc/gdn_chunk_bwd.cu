@@ -28,6 +28,10 @@ constexpr int kThreads = 256;
 constexpr int kPad = 132;   // fp32 row stride of 128-wide shared tiles
 constexpr int kPad64 = 68;  // fp32 row stride of 64-wide shared tiles
 constexpr int kScanDv = 16; // gradient-state columns per reverse-scan CTA
+constexpr int kWide = 512;  // threads of the WY and gradient kernels (16 warps: their shared memory allows one CTA
+                            // per SM, so the warps come from the CTA)
+constexpr int kRg = kWide / 16;     // row groups of the 64-row tiles: thread (ty, tx) owns rows ty + kRg r
+constexpr int kRt = kChunk / kRg;   // rows per thread in those tiles
 
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
@@ -428,7 +432,7 @@ struct WySmem {
     float gc[kChunk], beta[kChunk], egc[kChunk], ekd[kChunk];
 };
 
-__global__ void __launch_bounds__(kThreads) gdn_bwd_wy(BwdParams p) {
+__global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     WySmem& s = *reinterpret_cast<WySmem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -437,7 +441,7 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_wy(BwdParams p) {
     const int64_t t0 = (int64_t)c * kChunk;
     const float* fw = p.fws + ci * kWsChunkFloats;
     float* bw = p.bws + ci * kBwChunkFloats;
-    for (int i = warp; i < kChunk; i += kThreads / 32) {
+    for (int i = warp; i < kChunk; i += kWide / 32) {
         float x[4], r;
         qk_row(p.k, b, t0 + i, p.T, h, lane, p.l2norm, x, r);
 #pragma unroll
@@ -447,34 +451,33 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_wy(BwdParams p) {
 
     const int ty = tid >> 4, tx = tid & 15;
     {  // L_ij = -(beta_i k_i.k_j) e^(gc_i - gc_j), i > j, stored transposed
-        float kk[4][4];
+        float kk[kRt][4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < kRt; ++r)
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) kk[r][cc] = 0.f;
         for (int d = 0; d < kDk; d += 4) {
-            float4 ki[4], kj[4];
+            float4 ki[kRt], kj[4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                ki[r] = ld4(&s.K[ty + 16 * r][d]);
-                kj[r] = ld4(&s.K[tx + 16 * r][d]);
-            }
+            for (int r = 0; r < kRt; ++r) ki[r] = ld4(&s.K[ty + kRg * r][d]);
 #pragma unroll
-            for (int r = 0; r < 4; ++r)
+            for (int cc = 0; cc < 4; ++cc) kj[cc] = ld4(&s.K[tx + 16 * cc][d]);
+#pragma unroll
+            for (int r = 0; r < kRt; ++r)
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc)
                     kk[r][cc] += ki[r].x * kj[cc].x + ki[r].y * kj[cc].y + ki[r].z * kj[cc].z + ki[r].w * kj[cc].w;
         }
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < kRt; ++r)
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
-                const int i = ty + 16 * r, j = tx + 16 * cc;
+                const int i = ty + kRg * r, j = tx + 16 * cc;
                 s.Lt[j][i] = (i > j) ? -(s.beta[i] * kk[r][cc]) * expf(s.gc[i] - s.gc[j]) : 0.f;
             }
     }
     __syncthreads();
-    {  // back substitution: x_i = rhs_i + sum_{m > i} L_mi x_m, i = 63 .. 0
+    if (tid < kDv + kDk) {  // back substitution: x_i = rhs_i + sum_{m > i} L_mi x_m, i = 63 .. 0
         const int col = tid;
         const float* src = bw + (col < kDv ? kBwDVn + col : kBwDW + (col - kDv));
         float x[kChunk];
@@ -495,7 +498,7 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_wy(BwdParams p) {
 #pragma unroll
         for (int i = 0; i < kChunk; ++i) dst[i * kPad] = x[i];
     }
-    for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
+    for (int idx = tid; idx < kChunk * kDk / 4; idx += kWide) {
         const int i = idx >> 5, d4 = (idx & 31) * 4;
         cp_async16_rec(&s.U[i][d4], fw + kWsU + i * kDv + d4);
         cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
@@ -506,8 +509,8 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_wy(BwdParams p) {
     {  // dv = beta d(beta v); d beta, d gc and the k^ term of d(beta e^gc k^)
         const int cols[2] = {4 * tx, 64 + 4 * tx};
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int i = ty + 16 * r;
+        for (int r = 0; r < kRt; ++r) {
+            const int i = ty + kRg * r;
             const int64_t t = t0 + i;
             const float bi = s.beta[i], be = s.beta[i] * s.egc[i];
             float sv = 0.f, sk = 0.f;
@@ -542,68 +545,70 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_wy(BwdParams p) {
         }
     }
     {  // dL = strict(d(beta v) u^T + d(beta e^gc k^) w^T)
-        float a[4][4];
+        float a[kRt][4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < kRt; ++r)
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.f;
         for (int d = 0; d < kDk; d += 4) {
-            float4 xv[4], xk[4], uu[4], ww[4];
+            float4 xv[kRt], xk[kRt], uu[4], ww[4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                xv[r] = ld4(&s.Xv[ty + 16 * r][d]);
-                xk[r] = ld4(&s.Xk[ty + 16 * r][d]);
-                uu[r] = ld4(&s.U[tx + 16 * r][d]);
-                ww[r] = ld4(&s.W[tx + 16 * r][d]);
+            for (int r = 0; r < kRt; ++r) {
+                xv[r] = ld4(&s.Xv[ty + kRg * r][d]);
+                xk[r] = ld4(&s.Xk[ty + kRg * r][d]);
             }
 #pragma unroll
-            for (int r = 0; r < 4; ++r)
+            for (int cc = 0; cc < 4; ++cc) {
+                uu[cc] = ld4(&s.U[tx + 16 * cc][d]);
+                ww[cc] = ld4(&s.W[tx + 16 * cc][d]);
+            }
+#pragma unroll
+            for (int r = 0; r < kRt; ++r)
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc)
                     a[r][cc] += xv[r].x * uu[cc].x + xv[r].y * uu[cc].y + xv[r].z * uu[cc].z + xv[r].w * uu[cc].w +
                                 xk[r].x * ww[cc].x + xk[r].y * ww[cc].y + xk[r].z * ww[cc].z + xk[r].w * ww[cc].w;
         }
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < kRt; ++r)
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
-                const int i = ty + 16 * r, j = tx + 16 * cc;
+                const int i = ty + kRg * r, j = tx + 16 * cc;
                 bw[kBwDL + i * kChunk + j] = (i > j) ? a[r][cc] : 0.f;
             }
     }
     __syncthreads();  // u and w are read: v_new and do replace them
-    for (int idx = tid; idx < kChunk * kDv / 4; idx += kThreads) {
+    for (int idx = tid; idx < kChunk * kDv / 4; idx += kWide) {
         const int i = idx >> 5, d4 = (idx & 31) * 4;
         cp_async16_rec(&s.U[i][d4], bw + kBwVn + i * kDv + d4);
     }
     cp_async_commit_rec();
-    for (int i = warp; i < kChunk; i += kThreads / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.W[i][0]);
+    for (int i = warp; i < kChunk; i += kWide / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.W[i][0]);
     cp_async_wait_rec();
     __syncthreads();
     {  // dAqk = incl(do v_new^T)
-        float a[4][4];
+        float a[kRt][4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < kRt; ++r)
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.f;
         for (int d = 0; d < kDv; d += 4) {
-            float4 oo[4], vv[4];
+            float4 oo[kRt], vv[4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                oo[r] = ld4(&s.W[ty + 16 * r][d]);
-                vv[r] = ld4(&s.U[tx + 16 * r][d]);
-            }
+            for (int r = 0; r < kRt; ++r) oo[r] = ld4(&s.W[ty + kRg * r][d]);
 #pragma unroll
-            for (int r = 0; r < 4; ++r)
+            for (int cc = 0; cc < 4; ++cc) vv[cc] = ld4(&s.U[tx + 16 * cc][d]);
+#pragma unroll
+            for (int r = 0; r < kRt; ++r)
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc)
                     a[r][cc] += oo[r].x * vv[cc].x + oo[r].y * vv[cc].y + oo[r].z * vv[cc].z + oo[r].w * vv[cc].w;
         }
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < kRt; ++r)
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
-                const int i = ty + 16 * r, j = tx + 16 * cc;
+                const int i = ty + kRg * r, j = tx + 16 * cc;
                 bw[kBwDA + i * kChunk + j] = (i >= j) ? a[r][cc] : 0.f;
             }
     }
@@ -623,11 +628,11 @@ struct GradSmem {
     float G[kChunk][kPad64];  // dL -> dG
     float gc[kChunk], beta[kChunk], egc[kChunk], ekd[kChunk], rq[kChunk], rk[kChunk];
     float dgc[kChunk], dbeta[kChunk];
-    float colpart[16][kChunk];  // column sums of R per 16-row group, summed in a fixed order
-    float dglpart[16];          // dgc_last terms per 16-row group
+    float colpart[kRg][kChunk];  // column sums of R per row group, summed in a fixed order
+    float dglpart[kRg];          // dgc_last terms per row group
 };
 
-__global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
+__global__ void __launch_bounds__(kWide) gdn_bwd_grads(BwdParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     GradSmem& s = *reinterpret_cast<GradSmem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -636,7 +641,7 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
     const int64_t t0 = (int64_t)c * kChunk;
     const float* bw = p.bws + ci * kBwChunkFloats;
     const float scale = rsqrtf((float)kDk);
-    for (int i = warp; i < kChunk; i += kThreads / 32) {
+    for (int i = warp; i < kChunk; i += kWide / 32) {
         float x[4], r;
         qk_row(p.q, b, t0 + i, p.T, h, lane, p.l2norm, x, r);
 #pragma unroll
@@ -647,7 +652,7 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
         for (int e = 0; e < 4; ++e) s.K[i][lane + 32 * e] = x[e];
         if (lane == 0) s.rk[i] = r;
     }
-    for (int idx = tid; idx < kChunk * kChunk / 4; idx += kThreads) {
+    for (int idx = tid; idx < kChunk * kChunk / 4; idx += kWide) {
         const int i = idx >> 4, j4 = (idx & 15) * 4;
         cp_async16_rec(&s.P[i][j4], bw + kBwDA + i * kChunk + j4);
         cp_async16_rec(&s.G[i][j4], bw + kBwDL + i * kChunk + j4);
@@ -662,21 +667,22 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
 
     const int ty = tid >> 4, tx = tid & 15;
     {  // the 64 x 64 terms
-        float kk[4][4], qk[4][4];
+        float kk[kRt][4], qk[kRt][4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < kRt; ++r)
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) kk[r][cc] = qk[r][cc] = 0.f;
         for (int d = 0; d < kDk; d += 4) {
-            float4 ki[4], qi[4], kj[4];
+            float4 ki[kRt], qi[kRt], kj[4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                ki[r] = ld4(&s.K[ty + 16 * r][d]);
-                qi[r] = ld4(&s.Q[ty + 16 * r][d]);
-                kj[r] = ld4(&s.K[tx + 16 * r][d]);
+            for (int r = 0; r < kRt; ++r) {
+                ki[r] = ld4(&s.K[ty + kRg * r][d]);
+                qi[r] = ld4(&s.Q[ty + kRg * r][d]);
             }
 #pragma unroll
-            for (int r = 0; r < 4; ++r)
+            for (int cc = 0; cc < 4; ++cc) kj[cc] = ld4(&s.K[tx + 16 * cc][d]);
+#pragma unroll
+            for (int r = 0; r < kRt; ++r)
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
                     kk[r][cc] += ki[r].x * kj[cc].x + ki[r].y * kj[cc].y + ki[r].z * kj[cc].z + ki[r].w * kj[cc].w;
@@ -684,12 +690,14 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
                 }
         }
         __syncthreads();  // every thread has read the operands; P and G are rewritten in place below
-        float rowR[4] = {0.f, 0.f, 0.f, 0.f}, rowB[4] = {0.f, 0.f, 0.f, 0.f}, colR[4] = {0.f, 0.f, 0.f, 0.f};
+        float rowR[kRt], rowB[kRt], colR[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+        for (int r = 0; r < kRt; ++r) rowR[r] = rowB[r] = 0.f;
+#pragma unroll
+        for (int r = 0; r < kRt; ++r)
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
-                const int i = ty + 16 * r, j = tx + 16 * cc;
+                const int i = ty + kRg * r, j = tx + 16 * cc;
                 const float E = (i >= j) ? expf(s.gc[i] - s.gc[j]) : 0.f;
                 const float LB = (i > j) ? -kk[r][cc] * E : 0.f;  // -G E; L = beta_i LB
                 const float A = (i >= j) ? qk[r][cc] * E : 0.f;
@@ -702,21 +710,21 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
                 s.G[i][j] = (i > j) ? -s.beta[i] * E * dL : 0.f;
             }
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
+        for (int r = 0; r < kRt; ++r) {
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) {
                 rowR[r] += __shfl_xor_sync(0xffffffffu, rowR[r], o);
                 rowB[r] += __shfl_xor_sync(0xffffffffu, rowB[r], o);
             }
             if (tx == 0) {
-                atomicAdd(&s.dgc[ty + 16 * r], rowR[r]);
-                atomicAdd(&s.dbeta[ty + 16 * r], rowB[r]);
+                atomicAdd(&s.dgc[ty + kRg * r], rowR[r]);
+                atomicAdd(&s.dbeta[ty + kRg * r], rowB[r]);
             }
         }
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) s.colpart[ty][tx + 16 * cc] = colR[cc];
     }
-    for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
+    for (int idx = tid; idx < kChunk * kDk / 4; idx += kWide) {
         const int i = idx >> 5, d4 = (idx & 31) * 4;
         cp_async16_rec(&s.X[i][d4], bw + kBwDQg + i * kDk + d4);
     }
@@ -725,14 +733,14 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
     __syncthreads();
     if (tid < kChunk) {  // every add to one address comes from one thread, in program order: deterministic
         float cs = 0.f;
-        for (int y = 0; y < 16; ++y) cs += s.colpart[y][tid];
+        for (int y = 0; y < kRg; ++y) cs += s.colpart[y][tid];
         s.dgc[tid] -= cs;
     }
     __syncthreads();  // dgc is updated again below, by other threads
     const int cols[2] = {4 * tx, 64 + 4 * tx};
-    float dq[4][8], dk[4][8];
+    float dq[kRt][8], dk[kRt][8];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < kRt; ++r)
 #pragma unroll
         for (int e = 0; e < 8; ++e) dq[r][e] = dk[r][e] = 0.f;
     for (int j = 0; j < kChunk; ++j) {
@@ -741,8 +749,8 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
         const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
         const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int i = ty + 16 * r;
+        for (int r = 0; r < kRt; ++r) {
+            const int i = ty + kRg * r;
             const float pij = s.P[i][j], pji = s.P[j][i], gs = s.G[i][j] + s.G[j][i];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
@@ -753,8 +761,8 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
     }
     {  // + e^gc dQg; dgc += Qg . dQg
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int i = ty + 16 * r;
+        for (int r = 0; r < kRt; ++r) {
+            const int i = ty + kRg * r;
             const float eg = s.egc[i];
             float sq = 0.f;
 #pragma unroll
@@ -772,7 +780,7 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
         }
     }
     __syncthreads();  // dQg is read: dKd replaces it
-    for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
+    for (int idx = tid; idx < kChunk * kDk / 4; idx += kWide) {
         const int i = idx >> 5, d4 = (idx & 31) * 4;
         cp_async16_rec(&s.X[i][d4], bw + kBwDKd + i * kDk + d4);
     }
@@ -782,8 +790,8 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
     {  // + e^(gc_last - gc) dKd + the beta e^gc term; dgc -= Kd . dKd, dgc_last += sum Kd . dKd
         float dgl = 0.f;
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int i = ty + 16 * r;
+        for (int r = 0; r < kRt; ++r) {
+            const int i = ty + kRg * r;
             const float ek = s.ekd[i];
             float sk = 0.f;
 #pragma unroll
@@ -806,14 +814,14 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_grads(BwdParams p) {
     __syncthreads();
     if (tid == 0) {
         float dgl = 0.f;
-        for (int y = 0; y < 16; ++y) dgl += s.dglpart[y];
+        for (int y = 0; y < kRg; ++y) dgl += s.dglpart[y];
         s.dgc[kChunk - 1] += dgl + s.egc[kChunk - 1] * bw[kBwSmall];
     }
     __syncthreads();
     // outputs: dq, dk through the l2norm (dx = r (dx^ - x^ (x^ . dx^)), x^ = x r), dg, dbeta
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int i = ty + 16 * r;
+    for (int r = 0; r < kRt; ++r) {
+        const int i = ty + kRg * r;
         const int64_t t = t0 + i;
         const bool in = t < p.T;
 #pragma unroll
@@ -924,11 +932,11 @@ cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStr
         note_launch();
     }
     if ((e = phase_event(4, stream)) != cudaSuccess) return e;
-    gdn_bwd_wy<<<nchunks, kThreads, sizeof(WySmem), stream>>>(p);
+    gdn_bwd_wy<<<nchunks, kWide, sizeof(WySmem), stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     if ((e = phase_event(5, stream)) != cudaSuccess) return e;
-    gdn_bwd_grads<<<nchunks, kThreads, sizeof(GradSmem), stream>>>(p);
+    gdn_bwd_grads<<<nchunks, kWide, sizeof(GradSmem), stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     return phase_event(6, stream);
