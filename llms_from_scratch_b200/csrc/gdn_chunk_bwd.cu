@@ -43,19 +43,18 @@ __device__ __forceinline__ void row_to_smem(const View4& v, int b, int64_t t, in
     for (int e = 0; e < 4; ++e) dst[lane + 32 * e] = t < T ? load_elem(v.p, base + lane + 32 * e, v.dtype) : 0.f;
 }
 
-// Row t of q or k as the forward uses it (l2-normalised in the input dtype as gdn_prep_simt does), and
-// r = (sum x^2 + 1e-6)^-1/2 of the raw row in fp32 for the l2norm's derivative.
-__device__ __forceinline__ void qk_row(const View4& v, int b, int64_t t, int64_t T, int h, int lane, int l2norm,
-                                       float (&x)[4], float& r) {
+// Row t of q or k (4 elements a lane, zero past T); loads only, so a warp can have several rows in flight.
+__device__ __forceinline__ void qk_load(const View4& v, int b, int64_t t, int64_t T, int h, int lane, float (&x)[4]) {
+    const int64_t base = (int64_t)b * v.sb + (t < T ? t : 0) * v.st + (int64_t)h * v.sh;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x[e] = t < T ? load_elem(v.p, base + lane + 32 * e, v.dtype) : 0.f;
+}
+
+// A loaded row as the forward uses it (l2-normalised in the input dtype as gdn_prep_simt does), and
+// r = (sum x^2 + 1e-6)^-1/2 of the raw row in fp32 for the l2norm's derivative.  Warp-uniform in t.
+__device__ __forceinline__ void qk_norm(const View4& v, int64_t t, int64_t T, int l2norm, float (&x)[4], float& r) {
     r = 1.f;
-    if (t >= T) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) x[e] = 0.f;
-        return;
-    }
-    const int64_t base = (int64_t)b * v.sb + t * v.st + (int64_t)h * v.sh;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) x[e] = load_elem(v.p, base + lane + 32 * e, v.dtype);
+    if (t >= T) return;
     if (l2norm) {
         float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
 #pragma unroll
@@ -441,11 +440,18 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
     const int64_t t0 = (int64_t)c * kChunk;
     const float* fw = p.fws + ci * kWsChunkFloats;
     float* bw = p.bws + ci * kBwChunkFloats;
-    for (int i = warp; i < kChunk; i += kWide / 32) {
-        float x[4], r;
-        qk_row(p.k, b, t0 + i, p.T, h, lane, p.l2norm, x, r);
+    {  // k rows: a warp's 4 rows loaded together, then normalised
+        constexpr int kR = kChunk / (kWide / 32);
+        float x[kR][4], r;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) s.K[i][lane + 32 * e] = x[e];
+        for (int rr = 0; rr < kR; ++rr) qk_load(p.k, b, t0 + warp + (kWide / 32) * rr, p.T, h, lane, x[rr]);
+#pragma unroll
+        for (int rr = 0; rr < kR; ++rr) {
+            const int i = warp + (kWide / 32) * rr;
+            qk_norm(p.k, t0 + i, p.T, p.l2norm, x[rr], r);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) s.K[i][lane + 32 * e] = x[rr][e];
+        }
     }
     chunk_gates(p, b, h, t0, s.gc, s.beta, s.egc, s.ekd);  // ends with a barrier
 
@@ -641,16 +647,26 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_grads(BwdParams p) {
     const int64_t t0 = (int64_t)c * kChunk;
     const float* bw = p.bws + ci * kBwChunkFloats;
     const float scale = rsqrtf((float)kDk);
-    for (int i = warp; i < kChunk; i += kWide / 32) {
-        float x[4], r;
-        qk_row(p.q, b, t0 + i, p.T, h, lane, p.l2norm, x, r);
+    {  // q and k rows: a warp's 4 rows of each loaded together, then normalised
+        constexpr int kR = kChunk / (kWide / 32);
+        float xq[kR][4], xk[kR][4], r;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) s.Q[i][lane + 32 * e] = x[e] * scale;
-        if (lane == 0) s.rq[i] = r;
-        qk_row(p.k, b, t0 + i, p.T, h, lane, p.l2norm, x, r);
+        for (int rr = 0; rr < kR; ++rr) {
+            qk_load(p.q, b, t0 + warp + (kWide / 32) * rr, p.T, h, lane, xq[rr]);
+            qk_load(p.k, b, t0 + warp + (kWide / 32) * rr, p.T, h, lane, xk[rr]);
+        }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) s.K[i][lane + 32 * e] = x[e];
-        if (lane == 0) s.rk[i] = r;
+        for (int rr = 0; rr < kR; ++rr) {
+            const int i = warp + (kWide / 32) * rr;
+            qk_norm(p.q, t0 + i, p.T, p.l2norm, xq[rr], r);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) s.Q[i][lane + 32 * e] = xq[rr][e] * scale;
+            if (lane == 0) s.rq[i] = r;
+            qk_norm(p.k, t0 + i, p.T, p.l2norm, xk[rr], r);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) s.K[i][lane + 32 * e] = xk[rr][e];
+            if (lane == 0) s.rk[i] = r;
+        }
     }
     for (int idx = tid; idx < kChunk * kChunk / 4; idx += kWide) {
         const int i = idx >> 4, j4 = (idx & 15) * 4;
