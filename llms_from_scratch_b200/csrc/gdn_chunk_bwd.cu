@@ -18,11 +18,16 @@
 // scan (recording S_c), then gdn_bwd_scan (one CTA per (b, h, 16 state columns), chunks
 // in reverse), then gdn_bwd_states, gdn_bwd_wy and gdn_bwd_grads (one CTA per chunk each,
 // all chunks in parallel).
+#include "gdn_bwd.cuh"
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 
 namespace gdn {
 namespace {
+
+using bwd::chunk_gates;
+using bwd::qk_load;
+using bwd::qk_norm;
 
 constexpr int kThreads = 256;
 constexpr int kPad = 132;   // fp32 row stride of 128-wide shared tiles
@@ -41,56 +46,6 @@ __device__ __forceinline__ void row_to_smem(const View4& v, int b, int64_t t, in
     const int64_t base = (int64_t)b * v.sb + t * v.st + (int64_t)h * v.sh;
 #pragma unroll
     for (int e = 0; e < 4; ++e) dst[lane + 32 * e] = t < T ? load_elem(v.p, base + lane + 32 * e, v.dtype) : 0.f;
-}
-
-// Row t of q or k (4 elements a lane, zero past T); loads only, so a warp can have several rows in flight.
-__device__ __forceinline__ void qk_load(const View4& v, int b, int64_t t, int64_t T, int h, int lane, float (&x)[4]) {
-    const int64_t base = (int64_t)b * v.sb + (t < T ? t : 0) * v.st + (int64_t)h * v.sh;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) x[e] = t < T ? load_elem(v.p, base + lane + 32 * e, v.dtype) : 0.f;
-}
-
-// A loaded row as the forward uses it (l2-normalised in the input dtype as gdn_prep_simt does), and
-// r = (sum x^2 + 1e-6)^-1/2 of the raw row in fp32 for the l2norm's derivative.  Warp-uniform in t.
-__device__ __forceinline__ void qk_norm(const View4& v, int64_t t, int64_t T, int l2norm, float (&x)[4], float& r) {
-    r = 1.f;
-    if (t >= T) return;
-    if (l2norm) {
-        float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        r = rsqrtf(ss + 1e-6f);
-        const float inv = l2norm_inv(x, v.dtype);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) x[e] = round_to(x[e] * inv, v.dtype);
-    }
-}
-
-// g, beta of the chunk -> gc (inclusive cumsum), beta, e^gc, e^(gc_last - gc); rows past T are zero.
-__device__ __forceinline__ void chunk_gates(const BwdParams& p, int b, int h, int64_t t0, float* gc, float* beta,
-                                            float* egc, float* ekd) {
-    const int tid = threadIdx.x;
-    if (tid < kChunk) {
-        const int64_t t = t0 + tid;
-        gc[tid] = t < p.T ? load_elem(p.g.p, (int64_t)b * p.g.sb + t * p.g.st + (int64_t)h * p.g.sh, p.g.dtype) : 0.f;
-        beta[tid] = t < p.T ? load_elem(p.beta.p, (int64_t)b * p.beta.sb + t * p.beta.st + (int64_t)h * p.beta.sh,
-                                        p.beta.dtype)
-                            : 0.f;
-    }
-    __syncthreads();
-    if (tid == 0) {  // in order, as the forward's prep sums it
-        float acc = 0.f;
-        for (int i = 0; i < kChunk; ++i) {
-            acc += gc[i];
-            gc[i] = acc;
-        }
-    }
-    __syncthreads();
-    if (tid < kChunk) {
-        egc[tid] = expf(gc[tid]);
-        ekd[tid] = expf(gc[kChunk - 1] - gc[tid]);
-    }
-    __syncthreads();
 }
 
 // ============================================================================ reverse scan
