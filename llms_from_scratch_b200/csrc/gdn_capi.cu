@@ -261,7 +261,8 @@ size_t gdn_chunk_varlen_workspace_bytes(int64_t T, int64_t N, int64_t H, int64_t
     (void)qkv_dtype;
     if (T < 0 || N <= 0 || H <= 0) return 0;
     const int64_t max_chunks = (T + gdn::kChunk - 1) / gdn::kChunk + N;
-    const size_t header = ((size_t)(N + 1 + max_chunks) * sizeof(int) + 255) & ~size_t(255);
+    // tables: chunk bases (N + 1), chunk -> sequence (max_chunks), the scan's sequence order (N)
+    const size_t header = ((size_t)(2 * N + 1 + max_chunks) * sizeof(int) + 255) & ~size_t(255);
     return header + (size_t)(max_chunks * H) * (size_t)gdn::kTcChunkBytes;
 }
 
@@ -295,7 +296,7 @@ int gdn_chunk_gated_delta_rule_varlen(const gdn_tensor* query, const gdn_tensor*
     int dev = 0;
     cudaGetDevice(&dev);
     const int64_t max_chunks = (T + gdn::kChunk - 1) / gdn::kChunk + num_seqs;
-    const size_t header = ((size_t)(num_seqs + 1 + max_chunks) * sizeof(int) + 255) & ~size_t(255);
+    const size_t header = ((size_t)(2 * num_seqs + 1 + max_chunks) * sizeof(int) + 255) & ~size_t(255);
     int* tables = reinterpret_cast<int*>(workspace);
     gdn::ChunkParams p{};
     p.q = view4(query);
@@ -320,6 +321,7 @@ int gdn_chunk_gated_delta_rule_varlen(const gdn_tensor* query, const gdn_tensor*
     p.cu_seqlens = cu_seqlens;
     p.chunk_base = tables;
     p.chunk_seq = tables + num_seqs + 1;
+    p.seq_order = tables + num_seqs + 1 + max_chunks;
     p.N = (int)num_seqs;
     p.max_chunks = (int)max_chunks;
     cudaError_t e = gdn::launch_varlen_tables(p, st);

@@ -740,9 +740,20 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     ScanMisc& ms = *reinterpret_cast<ScanMisc*>(sm + S_MISC);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int bh = blockIdx.x;  // (sequence, head): also the state's [Dk, Dv] block
-    const int h = bh % p.H;
-    const int dvt = blockIdx.y & 3;  // 32-column slice of the state (and of b / o0)
+    // (sequence, head) -- also the state's [Dk, Dv] block -- and the 32-column slice of the state (and of b /
+    // o0).  Packed sequences: a 1-D grid over (rank, head, slice), longest sequence first, so the long chains
+    // start before the short ones fill the remaining SMs.
+    int bh, h, dvt;
+    if (p.cu_seqlens) {
+        const int x = blockIdx.x;
+        h = (x >> 2) % p.H;
+        dvt = x & 3;
+        bh = p.seq_order[x / (4 * p.H)] * p.H + h;
+    } else {
+        bh = blockIdx.x;
+        h = bh % p.H;
+        dvt = blockIdx.y & 3;
+    }
     const bool summary = p.scan_mode == 1;
     const bool transition = summary && blockIdx.y < 4;  // state starts from I, b ignored
     const int dv0 = dvt * kTcDvTile;
@@ -1417,8 +1428,11 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
 // counts the chunks of a contiguous run of sequences, a block scan turns the counts into bases, and
 // each thread writes its run.  Offsets that do not start at 0, decrease, or end at T set
 // kErrBadSeqlens and leave zero chunks (every base 0), so the prep and scan do nothing.
+constexpr int kOrderMax = 2048;
+
 __global__ void __launch_bounds__(256) gdn_varlen_tables(ChunkParams p, int* chunk_base, int* chunk_seq) {
     __shared__ int part[256];
+    __shared__ int ncs[kOrderMax];
     __shared__ int bad;
     const int tid = threadIdx.x, N = p.N;
     if (tid == 0) bad = 0;
@@ -1453,6 +1467,21 @@ __global__ void __launch_bounds__(256) gdn_varlen_tables(ChunkParams p, int* chu
         chunk_base[N] = ok ? part[255] : 0;
         if (!ok) report(p.err, kErrBadSeqlens);
     }
+    // Sequences by chunk count, longest first (stable): rank = #{m : nc_m > nc_n, or equal with m < n}.  The
+    // O(N^2) ranking serves up to kOrderMax sequences; beyond that the natural order is kept.
+    int* order = const_cast<int*>(p.seq_order);
+    if (N <= kOrderMax) {
+        for (int n = tid; n < N; n += 256) ncs[n] = ok ? (p.cu_seqlens[n + 1] - p.cu_seqlens[n] + kChunk - 1) / kChunk : 0;
+        __syncthreads();
+        for (int n = tid; n < N; n += 256) {
+            const int v = ncs[n];
+            int rank = 0;
+            for (int m = 0; m < N; ++m) rank += (ncs[m] > v) | ((ncs[m] == v) & (m < n));
+            order[rank] = n;
+        }
+    } else {
+        for (int n = tid; n < N; n += 256) order[n] = n;
+    }
 }
 
 }  // namespace
@@ -1478,7 +1507,8 @@ cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream) {
 cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(gdn_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
     if (e != cudaSuccess) return e;
-    dim3 grid((unsigned)((p.cu_seqlens ? p.N : p.B) * p.H), (p.scan_mode == 1 ? 2 : 1) * (kDv / kTcDvTile));
+    const dim3 grid = p.cu_seqlens ? dim3((unsigned)(p.N * p.H * (kDv / kTcDvTile)), 1)
+                                   : dim3((unsigned)(p.B * p.H), (p.scan_mode == 1 ? 2 : 1) * (kDv / kTcDvTile));
     gdn_scan_tc<<<grid, kScanThreads, S_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();

@@ -54,6 +54,7 @@ struct ChunkParams {
     const int* cu_seqlens;
     const int* chunk_base;  // [N + 1]
     const int* chunk_seq;   // [max_chunks]
+    const int* seq_order;   // [N]: sequences by chunk count, longest first (the scan starts those first)
     int N;                  // sequences
     int max_chunks;         // ceil(T / 64) + N: bound of sum_n ceil(T_n / 64), the prep's grid
     // CUDA-core scan only: when set, the state at the start of every chunk is written to

@@ -195,11 +195,12 @@ def test_varlen_entry_rejects_bad_arguments_before_any_cuda_call(lib, case, stat
 def test_varlen_workspace_size(lib):
     f = lib.gdn_chunk_varlen_workspace_bytes
     rec = 147456  # one tensor-core chunk record: M (32 KB) + Q' (16 KB) + b (64 KB) + o0 (32 KB)
-    # tables (N + 1 bases, one sequence id per chunk) rounded to 256 B, then ceil(T/64) + N records per head
+    # tables (N + 1 bases, one sequence id per chunk, N sequence ranks) rounded to 256 B, then ceil(T/64) + N
+    # records per head
     assert f(1000, 3, 4, 128, 128, _lib.GDN_BF16) == 256 + (16 + 3) * 4 * rec
     assert f(64, 1, 1, 128, 128, _lib.GDN_BF16) == 256 + 2 * rec
     big = f(100000, 500, 16, 128, 128, _lib.GDN_BF16)
-    header = (4 * (501 + 1563 + 500) + 255) // 256 * 256
+    header = (4 * (501 + 1563 + 500 + 500) + 255) // 256 * 256
     assert big == header + (1563 + 500) * 16 * rec
 
 

@@ -86,6 +86,29 @@ def test_bwd_bf16_matches_oracle(B, T, H):
         assert err <= 1e-2 and rl2 <= 5e-3, f"{name}: relative max {err:.2e}, rel-L2 {rl2:.2e}"
 
 
+@pytest.mark.parametrize("l2norm,with_state", [(True, False), (False, True)])
+def test_bwd_bf16_without_state_or_l2norm_matches_oracle(l2norm, with_state):
+    """The tensor-core path with no initial state and no final-state gradient, and with pre-normalised q/k
+    (use_qk_l2norm_in_kernel=False)."""
+    from llms_from_scratch_b200 import chunk_gated_delta_rule_bwd
+    q, k, v, g, beta, h0, do, dhT = _inputs(1, 200, 2, seed=31 + int(l2norm), state=with_state)
+    if not l2norm:
+        q = torch.nn.functional.normalize(q.float(), dim=-1).to(torch.bfloat16)
+        k = torch.nn.functional.normalize(k.float(), dim=-1).to(torch.bfloat16)
+    dhT = dhT if with_state else None
+    grads = chunk_gated_delta_rule_bwd(q, k, v, g, beta, do, initial_state=h0, d_final_state=dhT,
+                                       use_qk_l2norm_in_kernel=l2norm)
+    assert (grads[5] is None) == (not with_state)
+    host = lambda x: None if x is None else x.float().cpu().numpy()  # noqa: E731
+    ref = oracle_bwd(*(host(x) for x in (q, k, v, g, beta, do)), initial_state=host(h0), d_final_state=host(dhT),
+                     use_qk_l2norm_in_kernel=l2norm, in_dtype="bf16")
+    for name, ours, r in zip(NAMES[:5], grads[:5], ref[:5]):
+        ours = ours.float().cpu().numpy()
+        err = rel_max(ours, r)
+        rl2 = float(np.linalg.norm(ours - r) / np.linalg.norm(r))
+        assert err <= 1e-2 and rl2 <= 5e-3, f"{name}: relative max {err:.2e}, rel-L2 {rl2:.2e}"
+
+
 def test_autograd_wrapper_equals_direct_call():
     from llms_from_scratch_b200 import chunk_gated_delta_rule, chunk_gated_delta_rule_bwd
     q, k, v, g, beta, h0, do, dhT = _inputs(1, 200, 2, seed=3, dtype=torch.float32)
