@@ -66,12 +66,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// bf16 hi/lo split: x ~= hi + lo with |x - hi - lo| <= 2^-16 |x|.
-__device__ __forceinline__ void split_bf16(float x, float& hi, float& lo) {
-    hi = __bfloat162float(__float2bfloat16_rn(x));
-    lo = x - hi;
-}
-
 // ============================================================================ prep
 
 constexpr int kPrepThreads = 512;          // 16 warps; two CTAs share an SM (32 warps to hide latency)
@@ -126,14 +120,23 @@ __device__ __forceinline__ void store_bf16x8(unsigned char* tile, uint32_t off, 
     *reinterpret_cast<uint4*>(tile + off) = u;
 }
 
-// hi/lo halves of 8 consecutive values into two swizzled bf16 tiles.
+// hi/lo halves of 8 consecutive values into two swizzled bf16 tiles: each pair is rounded to bf16 once (hi),
+// the exact remainders x - hi are rounded again (lo).
 __device__ __forceinline__ void store_split8(unsigned char* hi_tile, unsigned char* lo_tile, uint32_t off,
                                              const float* x) {
-    float h[8], l[8];
+    uint4 hu, lu;
+    uint32_t* hp = &hu.x;
+    uint32_t* lp = &lu.x;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) split_bf16(x[e], h[e], l[e]);
-    store_bf16x8(hi_tile, off, h);
-    store_bf16x8(lo_tile, off, l);
+    for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 hb = __floats2bfloat162_rn(x[2 * e], x[2 * e + 1]);
+        const float2 hf = __bfloat1622float2(hb);
+        const __nv_bfloat162 lb = __floats2bfloat162_rn(x[2 * e] - hf.x, x[2 * e + 1] - hf.y);
+        hp[e] = *reinterpret_cast<const uint32_t*>(&hb);
+        lp[e] = *reinterpret_cast<const uint32_t*>(&lb);
+    }
+    *reinterpret_cast<uint4*>(hi_tile + off) = hu;
+    *reinterpret_cast<uint4*>(lo_tile + off) = lu;
 }
 
 // fp32 row of 32 values in a [rows][32] block whose 16-byte chunks are swizzled by row % 8.
@@ -307,15 +310,15 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
             const float y = __shfl_up_sync(0xffffffffu, x, o);
             if (lane >= o) x += y;
         }
-        ms.gc[2 * lane] = x - g1;
+        const float gc0 = x - g1, gcl = __shfl_sync(0xffffffffu, x, 31);  // gc_last: lane 31's sum
+        ms.gc[2 * lane] = gc0;
         ms.gc[2 * lane + 1] = x;
+        ms.egc[2 * lane] = __expf(gc0);
+        ms.egc[2 * lane + 1] = __expf(x);
+        ms.ekd[2 * lane] = __expf(gcl - gc0);
+        ms.ekd[2 * lane + 1] = __expf(gcl - x);
     }
-    __syncthreads();
-    if (tid < kChunk) {
-        ms.egc[tid] = __expf(ms.gc[tid]);
-        ms.ekd[tid] = __expf(ms.gc[kChunk - 1] - ms.gc[tid]);
-    }
-    bool ok = mbar_wait(&ms.bar, 0, kWaitNs);
+    bool ok = mbar_wait(&ms.bar, 0, kWaitNs);  // the barrier below publishes gc, e^gc and e^(gc_last - gc)
     tc_fence_after();
 
     // ---- 3. L = -(beta_i G_k e^(gc_i-gc_j)) strictly lower (:152-153), Aqk = Dk^-1/2 G_q e^(gc_i-gc_j) causal (:172)
