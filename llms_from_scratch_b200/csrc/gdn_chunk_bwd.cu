@@ -17,7 +17,10 @@
 // Launches: the forward's CUDA-core prep (u, w, Qg, Kd, Aqk, e^gc_last per chunk) and
 // scan (recording S_c), then gdn_bwd_scan (one CTA per (b, h, 16 state columns), chunks
 // in reverse), then gdn_bwd_states, gdn_bwd_wy and gdn_bwd_grads (one CTA per chunk each,
-// all chunks in parallel).
+// all chunks in parallel).  With bf16 q/k/v and d_out the forward recompute, the reverse
+// scan and the state products run on the tensor cores instead (gdn_chunk_tc.cu): the
+// tensor-core prep writes the u, w, Kd and Aqk tiles beside its own records, its scan
+// records S_c, and gdn_bwd_wy / gdn_bwd_grads follow as here.
 #include "gdn_bwd.cuh"
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
@@ -186,87 +189,12 @@ __global__ void __launch_bounds__(kThreads) gdn_bwd_states(BwdParams p) {
     const int ty = tid >> 4, tx = tid & 15, c0 = 4 * tx, c1 = 64 + 4 * tx;
     const int ri = tid >> 2, cs = tid & 3;
     for (int i = warp; i < kChunk; i += kThreads / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.dO[i][0]);
-    if (p.tc_records) {
-        // The tensor-core reverse scan leaves dv_new to this kernel: dv_new = Kd dS_{c+1} + Aqk^T do, with
-        // Kd staged in the dv_new tile and Aqk in the S slab (as [64][64]) until dv_new replaces them.
-        float* sA = &s.S[0][0];
-        for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
-            const int i = idx >> 5, d4 = (idx & 31) * 4;
-            cp_async16_rec(&s.dVn[i][d4], fw + kWsKd + i * kDk + d4);
-        }
-        for (int idx = tid; idx < kChunk * kChunk / 4; idx += kThreads) cp_async16_rec(sA + 4 * idx, fw + kWsAqk + 4 * idx);
-        cp_async_commit_rec();
-        cp_async_wait_rec();
-        __syncthreads();
-        float dvn[4][8];
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) dvn[r][e] = 0.f;
-        for (int j = 0; j < kChunk; ++j) {  // Aqk^T do: Aqk is lower incl. the diagonal (j >= i)
-            const float4 o0 = ld4(&s.dO[j][c0]), o1 = ld4(&s.dO[j][c1]);
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const float a = sA[j * kChunk + ty + 16 * r];
-                dvn[r][0] += a * o0.x;
-                dvn[r][1] += a * o0.y;
-                dvn[r][2] += a * o0.z;
-                dvn[r][3] += a * o0.w;
-                dvn[r][4] += a * o1.x;
-                dvn[r][5] += a * o1.y;
-                dvn[r][6] += a * o1.z;
-                dvn[r][7] += a * o1.w;
-            }
-        }
-        for (int slab = 0; slab < 4; ++slab) {  // + Kd dS_{c+1}, 32 rows of dS at a time
-            __syncthreads();
-            for (int idx = tid; idx < 32 * kDv / 4; idx += kThreads) {
-                const int rr = idx >> 5, d4 = (idx & 31) * 4;
-                cp_async16_rec(&s.E[rr][d4], bw + kBwDSe + (int64_t)(32 * slab + rr) * kDv + d4);
-            }
-            cp_async_commit_rec();
-            cp_async_wait_rec();
-            __syncthreads();
-            for (int kk = 0; kk < 32; ++kk) {
-                const float4 e0 = ld4(&s.E[kk][c0]), e1 = ld4(&s.E[kk][c1]);
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const float kd = s.dVn[ty + 16 * r][32 * slab + kk];
-                    dvn[r][0] += kd * e0.x;
-                    dvn[r][1] += kd * e0.y;
-                    dvn[r][2] += kd * e0.z;
-                    dvn[r][3] += kd * e0.w;
-                    dvn[r][4] += kd * e1.x;
-                    dvn[r][5] += kd * e1.y;
-                    dvn[r][6] += kd * e1.z;
-                    dvn[r][7] += kd * e1.w;
-                }
-            }
-        }
-        __syncthreads();  // every reader of Kd is done
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int i = ty + 16 * r;
-            const float4 v0 = make_float4(dvn[r][0], dvn[r][1], dvn[r][2], dvn[r][3]);
-            const float4 v1 = make_float4(dvn[r][4], dvn[r][5], dvn[r][6], dvn[r][7]);
-            st4(&s.dVn[i][c0], v0);
-            st4(&s.dVn[i][c1], v1);
-            st4(bw + kBwDVn + i * kDv + c0, v0);
-            st4(bw + kBwDVn + i * kDv + c1, v1);
-        }
-        for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
-            const int i = idx >> 5, d4 = (idx & 31) * 4;
-            cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
-        }
-        cp_async_commit_rec();
-    } else {
-        for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
-            const int i = idx >> 5, d4 = (idx & 31) * 4;
-            cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
-            cp_async16_rec(&s.dVn[i][d4], bw + kBwDVn + i * kDv + d4);
-        }
-        cp_async_commit_rec();
+    for (int idx = tid; idx < kChunk * kDk / 4; idx += kThreads) {
+        const int i = idx >> 5, d4 = (idx & 31) * 4;
+        cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
+        cp_async16_rec(&s.dVn[i][d4], bw + kBwDVn + i * kDv + d4);
     }
+    cp_async_commit_rec();
 
     float acc[4][8];
 #pragma unroll
@@ -861,15 +789,13 @@ cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStr
     f.hT = nullptr;
     f.states = p.bws + kBwS;
     f.states_stride = kBwChunkFloats;
-    if (p.tc_records) {  // tensor-core prep + scan (records M, Q', b, o0), then the CUDA-core prep's tiles
+    if (p.tc_records) {  // tensor-core prep (records M, Q', b, o0; u, w, Kd, Aqk tiles into fws) + scan
         f.ws = reinterpret_cast<float*>(p.tc_records);
+        f.bwd_tiles = p.fws;
         if ((e = phase_event(0, stream)) != cudaSuccess) return e;
         if ((e = launch_chunk_tc_prep(f, stream)) != cudaSuccess) return e;
-        if ((e = launch_chunk_tc_scan(f, stream)) != cudaSuccess) return e;
         if ((e = phase_event(1, stream)) != cudaSuccess) return e;
-        f.ws = p.fws;
-        f.states = nullptr;
-        if ((e = launch_chunk_simt_prep(f, stream)) != cudaSuccess) return e;
+        if ((e = launch_chunk_tc_scan(f, stream)) != cudaSuccess) return e;
         if ((e = phase_event(2, stream)) != cudaSuccess) return e;
     } else {  // the CUDA-core prep and scan (phase events 0-2 inside)
         f.ws = p.fws;

@@ -316,15 +316,6 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_simt(ChunkParams p) {
 
 }  // namespace
 
-cudaError_t launch_chunk_simt_prep(const ChunkParams& p, cudaStream_t stream) {
-    cudaError_t e = cudaFuncSetAttribute(gdn_prep_simt, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PrepSmem));
-    if (e != cudaSuccess) return e;
-    gdn_prep_simt<<<(unsigned)((int64_t)p.B * p.H * p.NC), kThreads, sizeof(PrepSmem), stream>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    note_launch();
-    return cudaSuccess;
-}
-
 cudaError_t launch_chunk_simt(const ChunkParams& p, cudaStream_t stream) {
     static_assert(sizeof(PrepSmem) <= 227 * 1024, "prep smem");
     static_assert(sizeof(ScanSmem) <= 227 * 1024, "scan smem");

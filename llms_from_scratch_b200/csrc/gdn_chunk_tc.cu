@@ -31,9 +31,10 @@
 //   4. T = (I - L)^-1 in 16x16 blocks (diagonal blocks by substitution, then
 //      the off-diagonal blocks by distance)
 //   5. Aqk T on the tensor cores (M=64, N=64, K=64, hi/lo operands); then
-//      X = E_d T B_e, Y = E_d T B, W = Aqk T B, Z = Aqk T B_e  (64x64, fp32)
-//   6. [X; Z] k^ -> P_X | Zk, then [Y; W] v -> P_Y | o0  (M=128, N=128, K=64, hi+lo)
-//   7. Q' = q^ e^gc Dk^-1/2 - Zk, o0 -> workspace; P_X, P_Y -> hi+lo B tiles
+//      X = T B_e, Y = T B, W = Aqk T B, Z = Aqk T B_e  (64x64, fp32)
+//   6. [X; Z] k^ -> w | Zk, then [Y; W] v -> u | o0  (M=128, N=128, K=64, hi+lo)
+//   7. Q' = q^ e^gc Dk^-1/2 - Zk, o0 -> workspace; P_X = E_d w, P_Y = E_d u -> hi+lo
+//      B tiles (E_d = diag e^(gc_last - gc))
 //   8. M' = k^T P_X, b = k^T P_Y (M=128, N=128, K=64, hi+lo)
 //   9. M = e^gc_last I - M', b -> workspace
 // gdn_scan_tc: one CTA per (batch, head, 32-column slice of Dv); warps 4-5
@@ -142,6 +143,13 @@ __device__ __forceinline__ void store_split8(unsigned char* hi_tile, unsigned ch
 // fp32 row of 32 values in a [rows][32] block whose 16-byte chunks are swizzled by row % 8.
 __device__ __forceinline__ uint32_t f32blk_offset(int row, int chunk4) {
     return (uint32_t)row * 128u + (uint32_t)((chunk4 ^ (row & 7)) * 16);
+}
+
+// 16 consecutive fp32 values to global memory (dst 16-byte aligned).
+__device__ __forceinline__ void store_f32x16(float* dst, const float* v) {
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4)
+        *reinterpret_cast<float4*>(dst + 4 * q4) = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
 }
 
 __device__ __forceinline__ void load_bf16x4_smem(const unsigned char* src, float (&x)[4]) {
@@ -345,6 +353,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
 #pragma unroll
             for (int q8 = 0; q8 < 2; ++q8)
                 store_split8(sm + P_AQK, sm + P_AQK + 8192, sw128_offset(i, 16 * part + 8 * q8, 64), a + 8 * q8);
+            if (p.bwd_tiles) store_f32x16(p.bwd_tiles + chunk * kWsChunkFloats + kWsAqk + i * kChunk + 16 * part, a);
         }
     } else {
         ok = false;
@@ -507,11 +516,10 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     }
     tc_fence_before();
     __syncthreads();  // the tiles of step 5 are read: the work region is free for the A tiles
-    // ---- 6. the four 64x64 coefficient matrices X = E_d T B_e, Y = E_d T B, W = (Aqk T) B, Z = (Aqk T) B_e,
-    //      in two M=128, N=128, K=64 rounds (hi+lo): [X;Z] k^ -> cols [0,128) (P_X | Zk), then
-    //      [Y;W] v -> cols [128,256) (P_Y | o0), the A tiles of the second round written over the first's.
+    // ---- 6. the four 64x64 coefficient matrices X = T B_e, Y = T B, W = (Aqk T) B, Z = (Aqk T) B_e,
+    //      in two M=128, N=128, K=64 rounds (hi+lo): [X;Z] k^ -> cols [0,128) (w | Zk), then
+    //      [Y;W] v -> cols [128,256) (u | o0), the A tiles of the second round written over the first's.
     const uint32_t id6 = make_idesc_f16(128, 128, false, true, true);
-    const float rowc = top ? ms.ekd[ri] : 1.f;
     uint32_t ph = 1;
     for (int round = 0; round < 2 && ok; ++round) {
         float x[16];  // row ri (X or Y) or 64+ri (Z or W)
@@ -520,7 +528,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
             const int j = jc + e;
             const float bj = ms.beta[j];
             const float bb = round == 0 ? bj * ms.egc[j] : bj;
-            x[e] = rowc * cv[e] * bb;
+            x[e] = cv[e] * bb;
         }
         unsigned char* at_hi = sm + P_ATILE;
         unsigned char* at_lo = sm + P_ATILE + 16384;
@@ -541,9 +549,12 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     }
     tc_fence_after();
 
-    // ---- 7. rows 0-63: P_X, P_Y -> hi/lo B tiles; rows 64-127: Q' (in place of q^) and o0 -> workspace
+    // ---- 7. rows 0-63: P_X = E_d w, P_Y = E_d u -> hi/lo B tiles (and w, u, Kd in fp32 for the backward);
+    //      rows 64-127: Q' (in place of q^) and o0 -> workspace
+    float* const tiles = p.bwd_tiles ? p.bwd_tiles + chunk * kWsChunkFloats : nullptr;
     if (ok) {
         const int r = 32 * quad + lane, i = r & 63;
+        const float ed = ms.ekd[i];
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {  // this thread's 32 columns, 16 at a time
             float v[16];
@@ -551,6 +562,20 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
             tmem_ld16(tmem_addr(tm, 32 * quad, d0), v);
             tmem_ld_wait();
             if (r < 64) {  // P_X (MN-major B tile: rows = tokens)
+                if (tiles) {
+                    store_f32x16(tiles + kWsW + i * kDk + d0, v);
+                    float kd[16];  // Kd = k^ e^(gc_last - gc), from the k^ rows of KQ
+#pragma unroll
+                    for (int q8 = 0; q8 < 2; ++q8) {
+                        const uint4 ku = *reinterpret_cast<const uint4*>(sm + P_KQ + sw128_offset(i, d0 + 8 * q8, 128));
+                        const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(&ku);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) kd[8 * q8 + e] = __bfloat162float(kb[e]) * ed;
+                    }
+                    store_f32x16(tiles + kWsKd + i * kDk + d0, kd);
+                }
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] *= ed;
 #pragma unroll
                 for (int q8 = 0; q8 < 2; ++q8)
                     store_split8(sm + P_PX, sm + P_PX + 16384, sw128_offset(i, d0 + 8 * q8, 64), v + 8 * q8);
@@ -575,6 +600,9 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
             tmem_ld16(tmem_addr(tm, 32 * quad, 128 + d0), v);
             tmem_ld_wait();
             if (r < 64) {  // P_Y
+                if (tiles) store_f32x16(tiles + kWsU + i * kDv + d0, v);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] *= ed;
 #pragma unroll
                 for (int q8 = 0; q8 < 2; ++q8)
                     store_split8(sm + P_PYH, sm + P_PYL, sw128_offset(i, d0 + 8 * q8, 64), v + 8 * q8);

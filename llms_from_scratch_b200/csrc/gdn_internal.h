@@ -62,6 +62,10 @@ struct ChunkParams {
     // recompute); out may then be null.
     float* states;
     int64_t states_stride;
+    // Tensor-core prep only (fixed length): when set, every chunk's u, w, Kd and Aqk are also
+    // written in fp32 to bwd_tiles + ((b*H + h)*NC + c) * kWsChunkFloats at kWsU / kWsW /
+    // kWsKd / kWsAqk, the tiles the backward's chunk kernels read.
+    float* bwd_tiles;
 };
 
 // ---------------------------------------------------------------- backward
@@ -119,8 +123,6 @@ cudaError_t launch_bwd_scan_tc(const BwdParams& p, cudaStream_t stream);
 // The backward's products with S_c and dS_{c+1} on the tensor cores (p.tc_records mode): dv_new, v_new,
 // dQg, dw, dKd and <S_c, dS_{c+1}> into every chunk's backward record.
 cudaError_t launch_bwd_states_tc(const BwdParams& p, cudaStream_t stream);
-// The CUDA-core prep alone (u, w, Qg, Kd, Aqk, e^gc_last per chunk into p.ws).
-cudaError_t launch_chunk_simt_prep(const ChunkParams& p, cudaStream_t stream);
 
 struct RecurrentParams {
     View4 q, k, v;
