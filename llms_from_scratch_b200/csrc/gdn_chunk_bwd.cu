@@ -323,6 +323,17 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
     const int64_t t0 = (int64_t)c * kChunk;
     const float* fw = p.fws + ci * kWsChunkFloats;
     float* bw = p.bws + ci * kBwChunkFloats;
+    // Every global input of the kernel is requested at entry: u, w (for dL) and v_new (for dAqk) by
+    // asynchronous copies, d_out rows into Xk; Xv and Xk hold v_new and d_out until dAqk is formed,
+    // then the back substitution's results.
+    for (int idx = tid; idx < kChunk * kDk / 4; idx += kWide) {
+        const int i = idx >> 5, d4 = (idx & 31) * 4;
+        cp_async16_rec(&s.U[i][d4], fw + kWsU + i * kDv + d4);
+        cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
+        cp_async16_rec(&s.Xv[i][d4], bw + kBwVn + i * kDv + d4);
+    }
+    cp_async_commit_rec();
+    for (int i = warp; i < kChunk; i += kWide / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.Xk[i][0]);
     {  // k rows: a warp's 4 rows loaded together, then normalised
         constexpr int kR = kChunk / (kWide / 32);
         float x[kR][4], r;
@@ -365,7 +376,35 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
                 s.Lt[j][i] = (i > j) ? -(s.beta[i] * kk[r][cc]) * expf(s.gc[i] - s.gc[j]) : 0.f;
             }
     }
-    __syncthreads();
+    cp_async_wait_rec();
+    __syncthreads();  // Lt, v_new (Xv) and d_out (Xk) are in shared memory
+    {  // dAqk = incl(do v_new^T)
+        float a[kRt][4];
+#pragma unroll
+        for (int r = 0; r < kRt; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.f;
+        for (int d = 0; d < kDv; d += 4) {
+            float4 oo[kRt], vv[4];
+#pragma unroll
+            for (int r = 0; r < kRt; ++r) oo[r] = ld4(&s.Xk[ty + kRg * r][d]);
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) vv[cc] = ld4(&s.Xv[tx + 16 * cc][d]);
+#pragma unroll
+            for (int r = 0; r < kRt; ++r)
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc)
+                    a[r][cc] += oo[r].x * vv[cc].x + oo[r].y * vv[cc].y + oo[r].z * vv[cc].z + oo[r].w * vv[cc].w;
+        }
+#pragma unroll
+        for (int r = 0; r < kRt; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                const int i = ty + kRg * r, j = tx + 16 * cc;
+                bw[kBwDA + i * kChunk + j] = (i >= j) ? a[r][cc] : 0.f;
+            }
+    }
+    __syncthreads();  // v_new and d_out are read: the substitution writes Xv and Xk
     if (tid < kDv + kDk) {  // back substitution: x_i = rhs_i + sum_{m > i} L_mi x_m, i = 63 .. 0
         const int col = tid;
         const float* src = bw + (col < kDv ? kBwDVn + col : kBwDW + (col - kDv));
@@ -374,26 +413,23 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
         for (int i = 0; i < kChunk; ++i) x[i] = src[i * kDv];
 #pragma unroll
         for (int i = kChunk - 2; i >= 0; --i) {
-            float acc = x[i];
+            // four independent partial sums: the dependent chain is a quarter as long
+            float a0 = x[i], a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
             for (int m4 = (i + 1) / 4; m4 < kChunk / 4; ++m4) {
                 // Lt[i][m] = L_mi = 0 for m <= i, so the head of the first group adds 0 * x
                 const float4 l = ld4(&s.Lt[i][4 * m4]);
-                acc += l.x * x[4 * m4] + l.y * x[4 * m4 + 1] + l.z * x[4 * m4 + 2] + l.w * x[4 * m4 + 3];
+                a0 += l.x * x[4 * m4];
+                a1 += l.y * x[4 * m4 + 1];
+                a2 += l.z * x[4 * m4 + 2];
+                a3 += l.w * x[4 * m4 + 3];
             }
-            x[i] = acc;
+            x[i] = (a0 + a1) + (a2 + a3);
         }
         float* dst = col < kDv ? &s.Xv[0][col] : &s.Xk[0][col - kDv];
 #pragma unroll
         for (int i = 0; i < kChunk; ++i) dst[i * kPad] = x[i];
     }
-    for (int idx = tid; idx < kChunk * kDk / 4; idx += kWide) {
-        const int i = idx >> 5, d4 = (idx & 31) * 4;
-        cp_async16_rec(&s.U[i][d4], fw + kWsU + i * kDv + d4);
-        cp_async16_rec(&s.W[i][d4], fw + kWsW + i * kDk + d4);
-    }
-    cp_async_commit_rec();
-    cp_async_wait_rec();
     __syncthreads();
     {  // dv = beta d(beta v); d beta, d gc and the k^ term of d(beta e^gc k^)
         const int cols[2] = {4 * tx, 64 + 4 * tx};
@@ -466,41 +502,6 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
                 bw[kBwDL + i * kChunk + j] = (i > j) ? a[r][cc] : 0.f;
             }
     }
-    __syncthreads();  // u and w are read: v_new and do replace them
-    for (int idx = tid; idx < kChunk * kDv / 4; idx += kWide) {
-        const int i = idx >> 5, d4 = (idx & 31) * 4;
-        cp_async16_rec(&s.U[i][d4], bw + kBwVn + i * kDv + d4);
-    }
-    cp_async_commit_rec();
-    for (int i = warp; i < kChunk; i += kWide / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.W[i][0]);
-    cp_async_wait_rec();
-    __syncthreads();
-    {  // dAqk = incl(do v_new^T)
-        float a[kRt][4];
-#pragma unroll
-        for (int r = 0; r < kRt; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) a[r][cc] = 0.f;
-        for (int d = 0; d < kDv; d += 4) {
-            float4 oo[kRt], vv[4];
-#pragma unroll
-            for (int r = 0; r < kRt; ++r) oo[r] = ld4(&s.W[ty + kRg * r][d]);
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) vv[cc] = ld4(&s.U[tx + 16 * cc][d]);
-#pragma unroll
-            for (int r = 0; r < kRt; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc)
-                    a[r][cc] += oo[r].x * vv[cc].x + oo[r].y * vv[cc].y + oo[r].z * vv[cc].z + oo[r].w * vv[cc].w;
-        }
-#pragma unroll
-        for (int r = 0; r < kRt; ++r)
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const int i = ty + kRg * r, j = tx + 16 * cc;
-                bw[kBwDA + i * kChunk + j] = (i >= j) ? a[r][cc] : 0.f;
-            }
-    }
 }
 
 // ============================================================================ gradients
@@ -512,7 +513,9 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
 struct GradSmem {
     float Q[kChunk][kPad];    // q^ Dk^-1/2
     float K[kChunk][kPad];    // k^
-    float X[kChunk][kPad];    // dQg, then dKd
+    float X[kChunk][kPad];    // dQg
+    float Xd[kChunk][kPad];   // dKd
+    float Kp[kChunk][kPad];   // dk^ through beta e^gc k^
     float P[kChunk][kPad64];  // dAqk -> dP
     float G[kChunk][kPad64];  // dL -> dG
     float gc[kChunk], beta[kChunk], egc[kChunk], ekd[kChunk], rq[kChunk], rk[kChunk];
@@ -530,6 +533,19 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_grads(BwdParams p) {
     const int64_t t0 = (int64_t)c * kChunk;
     const float* bw = p.bws + ci * kBwChunkFloats;
     const float scale = rsqrtf((float)kDk);
+    // every record tile of the chunk is requested at entry (asynchronous copies) and waited for once
+    for (int idx = tid; idx < kChunk * kChunk / 4; idx += kWide) {
+        const int i = idx >> 4, j4 = (idx & 15) * 4;
+        cp_async16_rec(&s.P[i][j4], bw + kBwDA + i * kChunk + j4);
+        cp_async16_rec(&s.G[i][j4], bw + kBwDL + i * kChunk + j4);
+    }
+    for (int idx = tid; idx < kChunk * kDk / 4; idx += kWide) {
+        const int i = idx >> 5, d4 = (idx & 31) * 4;
+        cp_async16_rec(&s.X[i][d4], bw + kBwDQg + i * kDk + d4);
+        cp_async16_rec(&s.Xd[i][d4], bw + kBwDKd + i * kDk + d4);
+        cp_async16_rec(&s.Kp[i][d4], bw + kBwDKp + i * kDk + d4);
+    }
+    cp_async_commit_rec();
     {  // q and k rows: a warp's 4 rows of each loaded together, then normalised
         constexpr int kR = kChunk / (kWide / 32);
         float xq[kR][4], xk[kR][4], r;
@@ -551,17 +567,11 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_grads(BwdParams p) {
             if (lane == 0) s.rk[i] = r;
         }
     }
-    for (int idx = tid; idx < kChunk * kChunk / 4; idx += kWide) {
-        const int i = idx >> 4, j4 = (idx & 15) * 4;
-        cp_async16_rec(&s.P[i][j4], bw + kBwDA + i * kChunk + j4);
-        cp_async16_rec(&s.G[i][j4], bw + kBwDL + i * kChunk + j4);
-    }
-    cp_async_commit_rec();
     if (tid < kChunk) {
         s.dbeta[tid] = bw[kBwSmall + 64 + tid];
         s.dgc[tid] = bw[kBwSmall + 128 + tid];
     }
-    cp_async_wait_rec();  // dAqk and dL landed; chunk_gates' barriers publish them
+    cp_async_wait_rec();  // the record tiles landed; chunk_gates' barriers publish them
     chunk_gates(p, b, h, t0, s.gc, s.beta, s.egc, s.ekd);  // ends with a barrier
 
     const int ty = tid >> 4, tx = tid & 15;
@@ -623,12 +633,6 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_grads(BwdParams p) {
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) s.colpart[ty][tx + 16 * cc] = colR[cc];
     }
-    for (int idx = tid; idx < kChunk * kDk / 4; idx += kWide) {
-        const int i = idx >> 5, d4 = (idx & 31) * 4;
-        cp_async16_rec(&s.X[i][d4], bw + kBwDQg + i * kDk + d4);
-    }
-    cp_async_commit_rec();
-    cp_async_wait_rec();
     __syncthreads();
     if (tid < kChunk) {  // every add to one address comes from one thread, in program order: deterministic
         float cs = 0.f;
@@ -678,14 +682,6 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_grads(BwdParams p) {
             if (tx == 0) atomicAdd(&s.dgc[i], eg * sq);
         }
     }
-    __syncthreads();  // dQg is read: dKd replaces it
-    for (int idx = tid; idx < kChunk * kDk / 4; idx += kWide) {
-        const int i = idx >> 5, d4 = (idx & 31) * 4;
-        cp_async16_rec(&s.X[i][d4], bw + kBwDKd + i * kDk + d4);
-    }
-    cp_async_commit_rec();
-    cp_async_wait_rec();
-    __syncthreads();
     {  // + e^(gc_last - gc) dKd + the beta e^gc term; dgc -= Kd . dKd, dgc_last += sum Kd . dKd
         float dgl = 0.f;
 #pragma unroll
@@ -695,8 +691,8 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_grads(BwdParams p) {
             float sk = 0.f;
 #pragma unroll
             for (int hlf = 0; hlf < 2; ++hlf) {
-                const float4 x = ld4(&s.X[i][cols[hlf]]), kq = ld4(&s.K[i][cols[hlf]]);
-                const float4 kp = ld4(bw + kBwDKp + i * kDk + cols[hlf]);
+                const float4 x = ld4(&s.Xd[i][cols[hlf]]), kq = ld4(&s.K[i][cols[hlf]]);
+                const float4 kp = ld4(&s.Kp[i][cols[hlf]]);
                 dk[r][4 * hlf] += ek * x.x + kp.x;
                 dk[r][4 * hlf + 1] += ek * x.y + kp.y;
                 dk[r][4 * hlf + 2] += ek * x.z + kp.z;
