@@ -829,9 +829,13 @@ cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStr
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     if ((e = phase_event(5, stream)) != cudaSuccess) return e;
-    gdn_bwd_grads<<<nchunks, kWide, sizeof(GradSmem), stream>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    note_launch();
+    if (p.tc_records) {  // bf16 mode: the chain rule's products on the tensor cores
+        if ((e = launch_bwd_grads_tc(p, stream)) != cudaSuccess) return e;
+    } else {
+        gdn_bwd_grads<<<nchunks, kWide, sizeof(GradSmem), stream>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        note_launch();
+    }
     return phase_event(6, stream);
 }
 

@@ -47,6 +47,7 @@
 //   the next state has been handed over, while the next chunk's MMAs run.
 #include <cuda_bf16.h>
 
+#include "gdn_bwd.cuh"
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 #include "gdn_tc.cuh"
@@ -1454,6 +1455,394 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
     }
 }
 
+// ============================================================================ backward gradients
+// gdn_bwd_grads_tc: the chain rule of one chunk in bf16 mode, one CTA (16 warps) per chunk, with the products
+// of the CUDA-core gdn_bwd_grads on the tensor cores:
+//   1. [k^; q^] k^T (M=128, N=64, K=Dk, exact bf16 operands) -> lanes 0-63 G = k^ k^T, 64-127 q^ k^T
+//   2. the 64x64 terms: dP = dAqk E, dG = -beta_i E dL (strictly lower), R = Aqk . dAqk + L . dL
+//      (dgc_i += sum_j R_ij - sum_j R_ji), dbeta_i += sum_j (-G E)_ij dL_ij
+//   3. [dP; dG + dG^T] k^ + [0; Dk^-1/2 dP^T] q^ (M=128, N=128, K=64 tokens, hi/lo A operands): lanes 0-63
+//      the dQ rows without e^gc dQg, lanes 64-127 the dk^ rows without e^(gc_last-gc) dKd + dKp
+//   4. per row: the remaining terms, dgc's Qg . dQg and Kd . dKd terms, the l2norm's derivative, the outputs
+// dAqk, dL, dKp and the dbeta / dgc parts come from gdn_bwd_wy, dQg, dKd and <S_c, dS_{c+1}> from
+// gdn_bwd_states_tc.
+constexpr int kGtThreads = 512;
+constexpr uint32_t kGtTmemCols = 256;  // cols [0,64): step 1, [64,192): step 3
+constexpr int kGLd = 68;               // fp32 row stride of the 64x64 tiles
+constexpr uint32_t G_KQ = 0;           // bf16 [128 rows][128] swizzled: rows 0-63 k^, 64-127 q^ (atom columns 16 KiB apart)
+constexpr uint32_t G_A1 = 32768;       // [dP; dG + dG^T] hi | lo: K-major A tiles, 128 rows x 64 tokens (16 KiB each)
+constexpr uint32_t G_A2 = 65536;       // [0; Dk^-1/2 dP^T] hi | lo
+constexpr uint32_t G_P = 98304;        // fp32 dAqk, then dP
+constexpr uint32_t G_L = G_P + 64 * kGLd * 4;  // fp32 dL, then dG
+constexpr uint32_t G_R = G_L + 64 * kGLd * 4;  // fp32 R [64][65]
+constexpr uint32_t G_MISC = G_R + 64 * 65 * 4;
+struct GtMisc {
+    float gc[64], beta[64], egc[64], ekd[64], rq[64], rk[64];
+    float dgc[64], dbeta[64], colr[64], kdot[64];
+    float rowb[4][64];     // sum_j (-G E) dL over each 16-column part
+    float dot[4][128][2];  // per 32-column part and row: (q^ . dQg | k^ . dKd, x^ . g)
+    uint64_t bar;
+    uint32_t tmem;
+};
+constexpr uint32_t G_SMEM = G_MISC + (uint32_t)sizeof(GtMisc) + 1024;  // + alignment slack
+static_assert(G_MISC % 8 == 0, "barrier alignment");
+
+// As mma_split_a, adding to the accumulator from the first pass on.
+__device__ __forceinline__ void mma_split_a_acc(uint32_t d_tmem, uint32_t a_hi, uint32_t a_lo, uint32_t b_tile,
+                                                uint32_t b_lbo, uint32_t idesc) {
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+            mma_f16(d_tmem, make_sdesc((s2 ? a_lo : a_hi) + ks * 32, 16, 1024, kSwizzle128B),
+                    make_sdesc(b_tile + ks * 2048, b_lbo, 1024, kSwizzle128B), idesc, true);
+}
+
+// Four consecutive bf16 of row t (columns 4 lane ..), zero past T; rows are 8-byte aligned in bf16 mode.
+__device__ __forceinline__ void load_row4_bf16(const View4& v, int b, int64_t t, int64_t T, int h, int lane,
+                                               float (&x)[4]) {
+    if (t < T) {
+        const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(v.p) + (int64_t)b * v.sb +
+                                                        t * v.st + (int64_t)h * v.sh + 4 * lane);
+        const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        x[0] = lo.x;
+        x[1] = lo.y;
+        x[2] = hi.x;
+        x[3] = hi.y;
+    } else {
+        x[0] = x[1] = x[2] = x[3] = 0.f;
+    }
+}
+
+__global__ void __launch_bounds__(kGtThreads, 1) gdn_bwd_grads_tc(BwdParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    GtMisc& ms = *reinterpret_cast<GtMisc*>(sm + G_MISC);
+    float(*sP)[kGLd] = reinterpret_cast<float(*)[kGLd]>(sm + G_P);
+    float(*sL)[kGLd] = reinterpret_cast<float(*)[kGLd]>(sm + G_L);
+    float(*sR)[65] = reinterpret_cast<float(*)[65]>(sm + G_R);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int quad = warp & 3, part = warp >> 2;  // TMEM lane quadrant, column part
+    const int64_t ci = blockIdx.x;
+    const int c = (int)(ci % p.NC), bh = (int)(ci / p.NC), b = bh / p.H, h = bh % p.H;
+    const int64_t t0 = (int64_t)c * kChunk;
+    const float* bw = p.bws + ci * kBwChunkFloats;
+    const float scale = rsqrtf((float)kDk);
+
+    // dAqk and dL by asynchronous copies; the dbeta / dgc parts; TMEM and the barrier
+    for (int idx = tid; idx < kChunk * kChunk / 4; idx += kGtThreads) {
+        const int i = idx >> 4, j4 = (idx & 15) * 4;
+        cp_async16_rec(&sP[i][j4], bw + kBwDA + i * kChunk + j4);
+        cp_async16_rec(&sL[i][j4], bw + kBwDL + i * kChunk + j4);
+    }
+    cp_async_commit_rec();
+    // the dbeta / dgc parts, g and beta: loaded into registers now, stored after the q/k rows are requested
+    float sdb = 0.f, sdg = 0.f, gv0 = 0.f, bv0 = 0.f;
+    if (tid < kChunk) {
+        sdb = bw[kBwSmall + 64 + tid];
+        sdg = bw[kBwSmall + 128 + tid];
+        const int64_t t = t0 + tid;
+        if (t < p.T) {
+            gv0 = load_elem(p.g.p, (int64_t)b * p.g.sb + t * p.g.st + (int64_t)h * p.g.sh, p.g.dtype);
+            bv0 = load_elem(p.beta.p, (int64_t)b * p.beta.sb + t * p.beta.st + (int64_t)h * p.beta.sh, p.beta.dtype);
+        }
+    }
+    if (warp == 0) {
+        tmem_alloc(&ms.tmem, kGtTmemCols);
+        tmem_relinquish();
+    }
+    if (tid == 32) {
+        mbar_init(&ms.bar, 1);
+        fence_mbar_init();
+    }
+    if (tid == 64) {  // step 4's records (dQg; dKd and dKp, adjacent) into L2 while steps 1-3 run
+        bulk_prefetch_l2(bw + kBwDQg, kChunk * kDk * 4);
+        bulk_prefetch_l2(bw + kBwDKd, 2 * kChunk * kDk * 4);
+    }
+    {  // q^, k^ rows (a warp's 4 rows of each, 4 columns a lane), normalised as the forward does -> the bf16 tile
+        constexpr int kR = kChunk / (kGtThreads / 32);
+        float xq[kR][4], xk[kR][4];
+#pragma unroll
+        for (int rr = 0; rr < kR; ++rr) {
+            const int64_t t = t0 + warp + (kGtThreads / 32) * rr;
+            load_row4_bf16(p.q, b, t, p.T, h, lane, xq[rr]);
+            load_row4_bf16(p.k, b, t, p.T, h, lane, xk[rr]);
+        }
+#pragma unroll
+        for (int rr = 0; rr < kR; ++rr) {
+            const int i = warp + (kGtThreads / 32) * rr;
+            float r;
+            bwd::qk_norm(p.q, t0 + i, p.T, p.l2norm, xq[rr], r);
+            if (lane == 0) ms.rq[i] = r;
+            store_bf16x4(sm + G_KQ, sw128_offset(64 + i, 4 * lane, 128), xq[rr]);
+            bwd::qk_norm(p.k, t0 + i, p.T, p.l2norm, xk[rr], r);
+            if (lane == 0) ms.rk[i] = r;
+            store_bf16x4(sm + G_KQ, sw128_offset(i, 4 * lane, 128), xk[rr]);
+        }
+    }
+    if (tid < kChunk) {
+        ms.dbeta[tid] = sdb;
+        ms.dgc[tid] = sdg;
+        ms.gc[tid] = gv0;
+        ms.beta[tid] = bv0;
+    }
+    cp_async_wait_rec();
+    __syncthreads();
+    if (warp == 1) {  // inclusive scan of g over the chunk, two values a lane, as the tensor-core prep forms it
+        const float g0 = ms.gc[2 * lane], g1 = ms.gc[2 * lane + 1];
+        float x = g0 + g1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        const float gc0 = x - g1, gcl = __shfl_sync(0xffffffffu, x, 31);
+        ms.gc[2 * lane] = gc0;
+        ms.gc[2 * lane + 1] = x;
+        ms.egc[2 * lane] = expf(gc0);
+        ms.egc[2 * lane + 1] = expf(x);
+        ms.ekd[2 * lane] = expf(gcl - gc0);
+        ms.ekd[2 * lane + 1] = expf(gcl - x);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = ms.tmem;
+    const uint32_t sbase = smem_u32(sm);
+
+    // ---- 1. [k^; q^] k^T -> cols [0,64)
+    if (tid == 0) {
+        const uint32_t id = make_idesc_f16(128, 64, false, false, true);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t d = make_sdesc(sbase + G_KQ + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, kSwizzle128B);
+            mma_f16(tm, d, d, id, ks > 0);  // B reads only rows 0-63 (k^) of the same tile
+        }
+        mma_commit(&ms.bar);
+    }
+    bool ok = mbar_wait(&ms.bar, 0, kWaitNs);
+    tc_fence_after();
+    ok = !__syncthreads_or(!ok);
+
+    // ---- 2. the 64x64 terms: thread (quadrant, lane, part) holds row r of step 1, columns j0 .. j0+15
+    const int r = 32 * quad + lane, i = r & 63, j0 = 16 * part;
+    float ra[16];  // Aqk . dAqk of this thread's entries (rows 64-127)
+    if (ok) {
+        float gv[16];
+        tmem_ld16(tmem_addr(tm, 32 * quad, j0), gv);
+        tmem_ld_wait();
+        const float gci = ms.gc[i];
+        if (r < 64) {  // L = -(beta_i G) E strictly lower
+            const float bi = ms.beta[i];
+            float rb = 0.f;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const int j = j0 + e;
+                const float dl = sL[i][j];
+                float dg = 0.f, rl = 0.f;
+                if (j < i) {
+                    const float E = expf(gci - ms.gc[j]);
+                    const float lb = -gv[e] * E;
+                    rl = bi * lb * dl;
+                    rb += lb * dl;
+                    dg = -bi * E * dl;
+                }
+                sL[i][j] = dg;
+                sR[i][j] = rl;
+            }
+            ms.rowb[part][i] = rb;
+        } else {  // Aqk = Dk^-1/2 (q^ k^T) E incl. the diagonal
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const int j = j0 + e;
+                const float da = sP[i][j];
+                float dp = 0.f, rv = 0.f;
+                if (j <= i) {
+                    const float E = expf(gci - ms.gc[j]);
+                    rv = (scale * gv[e]) * E * da;
+                    dp = da * E;
+                }
+                sP[i][j] = dp;
+                ra[e] = rv;
+            }
+        }
+    }
+    __syncthreads();  // dP, dG and R_L are in shared memory
+    if (ok) {
+        if (r >= 64) {  // R += Aqk . dAqk; dP row i -> A1 row i; Dk^-1/2 (column i of dP) -> A2 row 64 + i
+            float a[16], t[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                sR[i][j0 + e] += ra[e];
+                a[e] = sP[i][j0 + e];
+                t[e] = scale * sP[j0 + e][i];
+            }
+#pragma unroll
+            for (int q8 = 0; q8 < 2; ++q8) {
+                store_split8(sm + G_A1, sm + G_A1 + 16384, sw128_offset(i, j0 + 8 * q8, 128), a + 8 * q8);
+                store_split8(sm + G_A2, sm + G_A2 + 16384, sw128_offset(64 + i, j0 + 8 * q8, 128), t + 8 * q8);
+            }
+        } else {  // (dG + dG^T) row i -> A1 row 64 + i; A2 row i is zero
+            float a[16], z[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                a[e] = sL[i][j0 + e] + sL[j0 + e][i];
+                z[e] = 0.f;
+            }
+#pragma unroll
+            for (int q8 = 0; q8 < 2; ++q8) {
+                store_split8(sm + G_A1, sm + G_A1 + 16384, sw128_offset(64 + i, j0 + 8 * q8, 128), a + 8 * q8);
+                store_split8(sm + G_A2, sm + G_A2 + 16384, sw128_offset(i, j0 + 8 * q8, 128), z + 8 * q8);
+            }
+        }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    // ---- 3. [dP; dG + dG^T] k^ + [0; Dk^-1/2 dP^T] q^ -> cols [64,192); the sums of R meanwhile
+    if (ok && tid == 0) {
+        const uint32_t id = make_idesc_f16(128, 128, false, true, true);
+        mma_split_a(tm + 64, sbase + G_A1, sbase + G_A1 + 16384, sbase + G_KQ, 16384, id);
+        mma_split_a_acc(tm + 64, sbase + G_A2, sbase + G_A2 + 16384, sbase + G_KQ + 8192, 16384, id);
+        mma_commit(&ms.bar);
+    }
+    if (tid < kChunk) {  // row sums of R and of (-G E) dL, in a fixed order
+        float s = 0.f;
+        for (int j = 0; j < kChunk; ++j) s += sR[tid][j];
+        ms.dgc[tid] += s;
+        ms.dbeta[tid] += ((ms.rowb[0][tid] + ms.rowb[1][tid]) + ms.rowb[2][tid]) + ms.rowb[3][tid];
+    } else if (tid < 2 * kChunk) {  // column sums of R
+        const int j = tid - kChunk;
+        float s = 0.f;
+        for (int ii = 0; ii < kChunk; ++ii) s += sR[ii][j];
+        ms.colr[j] = s;
+    }
+    if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);
+    tc_fence_after();
+    ok = !__syncthreads_or(!ok);
+
+    // ---- 4. row r of step 3 (r < 64: dq row i, else dk row i), columns cb .. cb+31
+    const int cb = 32 * part;
+    const bool qrow = r < 64;
+    const int64_t t = t0 + i;
+    const bool in = t < p.T;
+    const float rr = qrow ? ms.rq[i] : ms.rk[i];
+    float gq[32], xh[32];
+    float d1 = 0.f, d2 = 0.f;
+    if (ok) {
+        const View4& X = qrow ? p.q : p.k;
+        const __nv_bfloat16* xrow = reinterpret_cast<const __nv_bfloat16*>(X.p) + (int64_t)b * X.sb +
+                                    (in ? t : t0) * X.st + (int64_t)h * X.sh + cb;
+        uint4 raw[4];
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) raw[q8] = in ? reinterpret_cast<const uint4*>(xrow)[q8] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            const int c0 = cb + 16 * hf;
+            float4 x1[4], x2[4];  // dQg | dKd, and dKp
+            const float* src1 = bw + (qrow ? kBwDQg : kBwDKd) + i * kDk + c0;
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+                x1[q4] = *reinterpret_cast<const float4*>(src1 + 4 * q4);
+                x2[q4] = qrow ? make_float4(0.f, 0.f, 0.f, 0.f)
+                              : *reinterpret_cast<const float4*>(bw + kBwDKp + i * kDk + c0 + 4 * q4);
+            }
+            float v[16];
+            tmem_ld16(tmem_addr(tm, 32 * quad, 64 + c0), v);
+            tmem_ld_wait();
+            const float ex = qrow ? ms.egc[i] : ms.ekd[i];
+#pragma unroll
+            for (int q8 = 0; q8 < 2; ++q8) {
+                const uint4 hu = *reinterpret_cast<const uint4*>(sm + G_KQ + sw128_offset(qrow ? 64 + i : i, c0 + 8 * q8, 128));
+                const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&hu);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int k = 8 * q8 + e;
+                    const float4 a1 = x1[k >> 2], a2 = x2[k >> 2];
+                    const float y1 = (k & 3) == 0 ? a1.x : (k & 3) == 1 ? a1.y : (k & 3) == 2 ? a1.z : a1.w;
+                    const float y2 = (k & 3) == 0 ? a2.x : (k & 3) == 1 ? a2.y : (k & 3) == 2 ? a2.z : a2.w;
+                    const float g = v[k] + ex * y1 + y2;
+                    gq[16 * hf + k] = qrow ? scale * g : g;
+                    d1 += __bfloat162float(hb[e]) * y1;
+                }
+            }
+        }
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+            const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&raw[q8]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                xh[8 * q8 + e] = __bfloat162float(xb[e]) * rr;
+                d2 += xh[8 * q8 + e] * gq[8 * q8 + e];
+            }
+        }
+        ms.dot[part][r][0] = d1;
+        ms.dot[part][r][1] = d2;
+    }
+    __syncthreads();
+    if (ok && in) {  // dx = r (dx^ - x^ (x^ . dx^)) with the l2norm, dx^ otherwise
+        const float dot = ((ms.dot[0][r][1] + ms.dot[1][r][1]) + ms.dot[2][r][1]) + ms.dot[3][r][1];
+        const Out4& O = qrow ? p.dq : p.dk;
+        const int64_t ob = (int64_t)b * O.sb + t * O.st + (int64_t)h * O.sh + cb;
+        float o[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = p.l2norm ? rr * (gq[e] - xh[e] * dot) : gq[e];
+        __nv_bfloat16* ob16 = reinterpret_cast<__nv_bfloat16*>(O.p) + ob;
+        if (O.dtype == GDN_BF16 && (reinterpret_cast<uintptr_t>(ob16) & 15) == 0) {  // four 16-byte stores
+#pragma unroll
+            for (int q8 = 0; q8 < 4; ++q8)
+                reinterpret_cast<uint4*>(ob16)[q8] =
+                    make_uint4(pack_bf16x2(o[8 * q8], o[8 * q8 + 1]), pack_bf16x2(o[8 * q8 + 2], o[8 * q8 + 3]),
+                               pack_bf16x2(o[8 * q8 + 4], o[8 * q8 + 5]), pack_bf16x2(o[8 * q8 + 6], o[8 * q8 + 7]));
+        } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) store_elem(O.p, ob + e, O.dtype, o[e]);
+        }
+    }
+    if (tid < kChunk) {  // dgc_i: - sum_j R_ji + e^gc Dk^-1/2 (q^ . dQg) - e^(gc_last-gc) (k^ . dKd)
+        const float dq1 = ((ms.dot[0][tid][0] + ms.dot[1][tid][0]) + ms.dot[2][tid][0]) + ms.dot[3][tid][0];
+        const float dk1 = ((ms.dot[0][64 + tid][0] + ms.dot[1][64 + tid][0]) + ms.dot[2][64 + tid][0]) +
+                          ms.dot[3][64 + tid][0];
+        ms.kdot[tid] = ms.ekd[tid] * dk1;
+        ms.dgc[tid] += -ms.colr[tid] + ms.egc[tid] * scale * dq1 - ms.kdot[tid];
+    }
+    __syncthreads();
+    if (tid == 0) {  // dgc_last += sum_i Kd . dKd + e^gc_last <S_c, dS_{c+1}>
+        float dgl = 0.f;
+        for (int ii = 0; ii < kChunk; ++ii) dgl += ms.kdot[ii];
+        ms.dgc[kChunk - 1] += dgl + ms.egc[kChunk - 1] * bw[kBwSmall];
+        if (!ok) report(p.err, kErrTimeoutPrep);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {  // dg_t = sum_{i >= t} dgc_i: suffix scan over the chunk, two rows per lane
+        const float a0 = ms.dgc[2 * lane], a1 = ms.dgc[2 * lane + 1];
+        float x = a0 + a1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_down_sync(0xffffffffu, x, o);
+            if (lane + o < 32) x += y;
+        }
+        const float dg[2] = {x, x - a0};
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int ii = 2 * lane + e;
+            const int64_t tt = t0 + ii;
+            if (ok && tt < p.T) {
+                store_elem(p.dg.p, (int64_t)b * p.dg.sb + tt * p.dg.st + (int64_t)h * p.dg.sh, p.dg.dtype, dg[e]);
+                store_elem(p.dbeta.p, (int64_t)b * p.dbeta.sb + tt * p.dbeta.st + (int64_t)h * p.dbeta.sh,
+                           p.dbeta.dtype, ms.dbeta[ii]);
+            }
+        }
+        tc_fence_after();
+        tmem_dealloc(tm, kGtTmemCols);
+    }
+}
+
 // Packed sequences: chunk_base[n] = sum_{m<n} ceil(T_m / 64) and chunk_seq[j] = the sequence of global
 // chunk j, from the device's cu_seqlens, so the host never reads the offsets.  One CTA: each thread
 // counts the chunks of a contiguous run of sequences, a block scan turns the counts into bases, and
@@ -1551,6 +1940,16 @@ cudaError_t launch_bwd_states_tc(const BwdParams& p, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(gdn_bwd_states_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)T_SMEM);
     if (e != cudaSuccess) return e;
     gdn_bwd_states_tc<<<(unsigned)((int64_t)p.B * p.H * p.NC), kBtThreads, T_SMEM, stream>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    note_launch();
+    return cudaSuccess;
+}
+
+cudaError_t launch_bwd_grads_tc(const BwdParams& p, cudaStream_t stream) {
+    static_assert(G_SMEM <= 227 * 1024, "shared memory budget");
+    cudaError_t e = cudaFuncSetAttribute(gdn_bwd_grads_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G_SMEM);
+    if (e != cudaSuccess) return e;
+    gdn_bwd_grads_tc<<<(unsigned)((int64_t)p.B * p.H * p.NC), kGtThreads, G_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     return cudaSuccess;

@@ -123,6 +123,9 @@ cudaError_t launch_bwd_scan_tc(const BwdParams& p, cudaStream_t stream);
 // The backward's products with S_c and dS_{c+1} on the tensor cores (p.tc_records mode): dv_new, v_new,
 // dQg, dw, dKd and <S_c, dS_{c+1}> into every chunk's backward record.
 cudaError_t launch_bwd_states_tc(const BwdParams& p, cudaStream_t stream);
+// The chain rule of every chunk on the tensor cores (p.tc_records mode): dq, dk, dg, dbeta from the records of
+// gdn_bwd_wy and gdn_bwd_states_tc.
+cudaError_t launch_bwd_grads_tc(const BwdParams& p, cudaStream_t stream);
 
 struct RecurrentParams {
     View4 q, k, v;
