@@ -1,6 +1,8 @@
 // Device helpers shared by the backward's kernels (CUDA-core and tensor-core files).
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
 
@@ -30,9 +32,27 @@ __device__ __forceinline__ void qk_norm(const View4& v, int64_t t, int64_t T, in
     }
 }
 
+// Four consecutive bf16 of row t (columns 4 lane ..), zero past T; bf16 rows 8-byte aligned.
+__device__ __forceinline__ void row4_bf16(const View4& v, int b, int64_t t, int64_t T, int h, int lane, float (&x)[4]) {
+    if (t < T) {
+        const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(v.p) + (int64_t)b * v.sb +
+                                                        t * v.st + (int64_t)h * v.sh + 4 * lane);
+        const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        x[0] = lo.x;
+        x[1] = lo.y;
+        x[2] = hi.x;
+        x[3] = hi.y;
+    } else {
+        x[0] = x[1] = x[2] = x[3] = 0.f;
+    }
+}
+
 // g, beta of the chunk -> gc (inclusive cumsum), beta, e^gc, e^(gc_last - gc); rows past T are zero.
+// warp_scan (CTA-uniform): the cumsum by one warp, two values a lane, as the tensor-core prep forms it (the
+// bf16 mode's forward); otherwise in order by one thread, as the CUDA-core prep forms it.
 __device__ __forceinline__ void chunk_gates(const BwdParams& p, int b, int h, int64_t t0, float* gc, float* beta,
-                                            float* egc, float* ekd) {
+                                            float* egc, float* ekd, bool warp_scan = false) {
     const int tid = threadIdx.x;
     if (tid < kChunk) {
         const int64_t t = t0 + tid;
@@ -42,6 +62,27 @@ __device__ __forceinline__ void chunk_gates(const BwdParams& p, int b, int h, in
                             : 0.f;
     }
     __syncthreads();
+    if (warp_scan) {
+        if (tid >= 32 && tid < 64) {
+            const int lane = tid - 32;
+            const float g0 = gc[2 * lane], g1 = gc[2 * lane + 1];
+            float x = g0 + g1;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            const float gc0 = x - g1, gcl = __shfl_sync(0xffffffffu, x, 31);
+            gc[2 * lane] = gc0;
+            gc[2 * lane + 1] = x;
+            egc[2 * lane] = expf(gc0);
+            egc[2 * lane + 1] = expf(x);
+            ekd[2 * lane] = expf(gcl - gc0);
+            ekd[2 * lane + 1] = expf(gcl - x);
+        }
+        __syncthreads();
+        return;
+    }
     if (tid == 0) {  // in order, as the forward's prep sums it
         float acc = 0.f;
         for (int i = 0; i < kChunk; ++i) {

@@ -41,6 +41,10 @@ constexpr int kWide = 512;  // threads of the WY and gradient kernels (16 warps:
 constexpr int kRg = kWide / 16;     // row groups of the 64-row tiles: thread (ty, tx) owns rows ty + kRg r
 constexpr int kRt = kChunk / kRg;   // rows per thread in those tiles
 
+// Hint: bring [p, p + bytes) into L2 (16-byte aligned, a multiple of 16 bytes).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 
@@ -333,23 +337,49 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
         cp_async16_rec(&s.Xv[i][d4], bw + kBwVn + i * kDv + d4);
     }
     cp_async_commit_rec();
+    const bool bf16 = p.tc_records != nullptr;  // bf16 q/k/v/d_out with 16-byte aligned rows
+    if (tid == 0) {  // the back substitution's right-hand sides (dv_new, dw) into L2 meanwhile
+        prefetch_l2(bw + kBwDVn, kChunk * kDv * 4);
+        prefetch_l2(bw + kBwDW, kChunk * kDk * 4);
+    }
+    const int ty = tid >> 4, tx = tid & 15;
+    const int cols[2] = {4 * tx, 64 + 4 * tx};
+    uint2 vraw[kRt][2];  // bf16 mode: this thread's v entries for the dv phase, requested now
+    if (bf16) {
+#pragma unroll
+        for (int r = 0; r < kRt; ++r) {
+            const int64_t t = t0 + ty + kRg * r;
+#pragma unroll
+            for (int hlf = 0; hlf < 2; ++hlf)
+                vraw[r][hlf] = t < p.T ? *reinterpret_cast<const uint2*>(
+                                             reinterpret_cast<const __nv_bfloat16*>(p.v.p) + (int64_t)b * p.v.sb +
+                                             t * p.v.st + (int64_t)h * p.v.sh + cols[hlf])
+                                       : make_uint2(0u, 0u);
+        }
+    }
     for (int i = warp; i < kChunk; i += kWide / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.Xk[i][0]);
     {  // k rows: a warp's 4 rows loaded together, then normalised
         constexpr int kR = kChunk / (kWide / 32);
         float x[kR][4], r;
 #pragma unroll
-        for (int rr = 0; rr < kR; ++rr) qk_load(p.k, b, t0 + warp + (kWide / 32) * rr, p.T, h, lane, x[rr]);
+        for (int rr = 0; rr < kR; ++rr) {
+            if (bf16) bwd::row4_bf16(p.k, b, t0 + warp + (kWide / 32) * rr, p.T, h, lane, x[rr]);
+            else qk_load(p.k, b, t0 + warp + (kWide / 32) * rr, p.T, h, lane, x[rr]);
+        }
 #pragma unroll
         for (int rr = 0; rr < kR; ++rr) {
             const int i = warp + (kWide / 32) * rr;
             qk_norm(p.k, t0 + i, p.T, p.l2norm, x[rr], r);
+            if (bf16) {
+                st4(&s.K[i][4 * lane], make_float4(x[rr][0], x[rr][1], x[rr][2], x[rr][3]));
+            } else {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) s.K[i][lane + 32 * e] = x[rr][e];
+                for (int e = 0; e < 4; ++e) s.K[i][lane + 32 * e] = x[rr][e];
+            }
         }
     }
-    chunk_gates(p, b, h, t0, s.gc, s.beta, s.egc, s.ekd);  // ends with a barrier
+    chunk_gates(p, b, h, t0, s.gc, s.beta, s.egc, s.ekd, bf16);  // ends with a barrier
 
-    const int ty = tid >> 4, tx = tid & 15;
     {  // L_ij = -(beta_i k_i.k_j) e^(gc_i - gc_j), i > j, stored transposed
         float kk[kRt][4];
 #pragma unroll
@@ -432,7 +462,6 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
     }
     __syncthreads();
     {  // dv = beta d(beta v); d beta, d gc and the k^ term of d(beta e^gc k^)
-        const int cols[2] = {4 * tx, 64 + 4 * tx};
 #pragma unroll
         for (int r = 0; r < kRt; ++r) {
             const int i = ty + kRg * r;
@@ -444,16 +473,30 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
                 const int cc = cols[hlf];
                 const float4 xv = ld4(&s.Xv[i][cc]), xk = ld4(&s.Xk[i][cc]), kv = ld4(&s.K[i][cc]);
                 const float xva[4] = {xv.x, xv.y, xv.z, xv.w};
-                const int64_t vb = (int64_t)b * p.v.sb + t * p.v.st + (int64_t)h * p.v.sh + cc;
+                if (bf16) {
+                    const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vraw[r][hlf].x));
+                    const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vraw[r][hlf].y));
+                    sv += v01.x * xva[0] + v01.y * xva[1] + v23.x * xva[2] + v23.y * xva[3];
+                } else {
+                    const int64_t vb = (int64_t)b * p.v.sb + t * p.v.st + (int64_t)h * p.v.sh + cc;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float vv = t < p.T ? load_elem(p.v.p, vb + e, p.v.dtype) : 0.f;
-                    sv += vv * xva[e];
+                    for (int e = 0; e < 4; ++e) {
+                        const float vv = t < p.T ? load_elem(p.v.p, vb + e, p.v.dtype) : 0.f;
+                        sv += vv * xva[e];
+                    }
                 }
                 if (t < p.T) {
                     const int64_t ob = (int64_t)b * p.dv.sb + t * p.dv.st + (int64_t)h * p.dv.sh + cc;
+                    __nv_bfloat16* o16 = reinterpret_cast<__nv_bfloat16*>(p.dv.p) + ob;
+                    if (p.dv.dtype == GDN_BF16 && (reinterpret_cast<uintptr_t>(o16) & 7) == 0) {  // one 8-byte store
+                        const __nv_bfloat162 o01 = __floats2bfloat162_rn(bi * xva[0], bi * xva[1]);
+                        const __nv_bfloat162 o23 = __floats2bfloat162_rn(bi * xva[2], bi * xva[3]);
+                        *reinterpret_cast<uint2*>(o16) = make_uint2(*reinterpret_cast<const uint32_t*>(&o01),
+                                                                    *reinterpret_cast<const uint32_t*>(&o23));
+                    } else {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) store_elem(p.dv.p, ob + e, p.dv.dtype, bi * xva[e]);
+                        for (int e = 0; e < 4; ++e) store_elem(p.dv.p, ob + e, p.dv.dtype, bi * xva[e]);
+                    }
                 }
                 sk += kv.x * xk.x + kv.y * xk.y + kv.z * xk.z + kv.w * xk.w;
                 st4(bw + kBwDKp + i * kDk + cc, make_float4(be * xk.x, be * xk.y, be * xk.z, be * xk.w));

@@ -1498,23 +1498,6 @@ __device__ __forceinline__ void mma_split_a_acc(uint32_t d_tmem, uint32_t a_hi, 
                     make_sdesc(b_tile + ks * 2048, b_lbo, 1024, kSwizzle128B), idesc, true);
 }
 
-// Four consecutive bf16 of row t (columns 4 lane ..), zero past T; rows are 8-byte aligned in bf16 mode.
-__device__ __forceinline__ void load_row4_bf16(const View4& v, int b, int64_t t, int64_t T, int h, int lane,
-                                               float (&x)[4]) {
-    if (t < T) {
-        const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(v.p) + (int64_t)b * v.sb +
-                                                        t * v.st + (int64_t)h * v.sh + 4 * lane);
-        const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-        const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-        x[0] = lo.x;
-        x[1] = lo.y;
-        x[2] = hi.x;
-        x[3] = hi.y;
-    } else {
-        x[0] = x[1] = x[2] = x[3] = 0.f;
-    }
-}
-
 __global__ void __launch_bounds__(kGtThreads, 1) gdn_bwd_grads_tc(BwdParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1566,8 +1549,8 @@ __global__ void __launch_bounds__(kGtThreads, 1) gdn_bwd_grads_tc(BwdParams p) {
 #pragma unroll
         for (int rr = 0; rr < kR; ++rr) {
             const int64_t t = t0 + warp + (kGtThreads / 32) * rr;
-            load_row4_bf16(p.q, b, t, p.T, h, lane, xq[rr]);
-            load_row4_bf16(p.k, b, t, p.T, h, lane, xk[rr]);
+            bwd::row4_bf16(p.q, b, t, p.T, h, lane, xq[rr]);
+            bwd::row4_bf16(p.k, b, t, p.T, h, lane, xk[rr]);
         }
 #pragma unroll
         for (int rr = 0; rr < kR; ++rr) {
