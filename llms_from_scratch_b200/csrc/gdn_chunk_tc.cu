@@ -1149,11 +1149,6 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
         }
         for (int it = 0; it < NC; ++it) {
             const int s = it & 1, c = NC - 1 - it;
-            // dS_{c+1} (fp32) for the chunk kernels
-            float* dst = p.bws + ((int64_t)bh * NC + c) * kBwChunkFloats + kBwDSe + (int64_t)dk * kDv + dv0;
-#pragma unroll
-            for (int q4 = 0; q4 < 16; ++q4)
-                *reinterpret_cast<float4*>(dst + 4 * q4) = make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
             if (ok) {  // tile s was last read by the MMAs of iteration it - 2, complete before iteration it - 1's
 #pragma unroll
                 for (int q8 = 0; q8 < 8; ++q8) store_bf16x8(sm + B_STILE + s * 16384, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
@@ -1161,20 +1156,21 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
             }
             tc_fence_before();
             named_bar_arrive(kBsBar, kBsBarCount);
+            {  // dS_{c+1} (fp32) for the chunk kernels, while the MMAs run
+                float* dst = p.bws + ((int64_t)bh * NC + c) * kBwChunkFloats + kBwDSe + (int64_t)dk * kDv + dv0;
+#pragma unroll
+                for (int q4 = 0; q4 < 16; ++q4)
+                    *reinterpret_cast<float4*>(dst + 4 * q4) =
+                        make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
+            }
             if (ok && bs_aborted(ms)) ok = false;
             if (ok && !mbar_wait(&ms.mma, it & 1, kWaitNs)) ok = false;
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
             if (ok) {
                 tc_fence_after();
-                float d[32];
-                tmem_ld32(tmem_addr(tm, 32 * warp, 0), d);
+                tmem_ld32(tmem_addr(tm, 32 * warp, 0), *reinterpret_cast<float(*)[32]>(S));
+                tmem_ld32(tmem_addr(tm, 32 * warp, 32), *reinterpret_cast<float(*)[32]>(S + 32));
                 tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 32; ++e) S[e] = d[e];
-                tmem_ld32(tmem_addr(tm, 32 * warp, 32), d);
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 32; ++e) S[32 + e] = d[e];
                 tc_fence_before();
             }
             if (!ok) ms.abort = 1;
