@@ -153,6 +153,24 @@ __device__ __forceinline__ void store_f32x16(float* dst, const float* v) {
         *reinterpret_cast<float4*>(dst + 4 * q4) = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
 }
 
+// Rows held one per lane (lane l: row l of a 32-row block, kN fp32 values in v) stored to global rows
+// g + l * ld through the warp's staging tile [32][kN + 4]: each store instruction then writes whole
+// 128-byte lines instead of 32 lines a 16-byte piece each.
+template <int kN>
+__device__ __forceinline__ void store_rows_coalesced(float* stage, const float* v, float* g, int64_t ld, int lane) {
+    constexpr int kS = kN + 4, kC = kN / 4;  // padded row stride; 16-byte pieces per row
+#pragma unroll
+    for (int q4 = 0; q4 < kC; ++q4)
+        *reinterpret_cast<float4*>(stage + lane * kS + 4 * q4) = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < kC; ++j) {
+        const int idx = 32 * j + lane, row = idx / kC, piece = idx % kC;
+        *reinterpret_cast<float4*>(g + row * ld + 4 * piece) = *reinterpret_cast<const float4*>(stage + row * kS + 4 * piece);
+    }
+    __syncwarp();  // the tile may be rewritten by the next call
+}
+
 __device__ __forceinline__ void load_bf16x4_smem(const unsigned char* src, float (&x)[4]) {
     const uint2 u = *reinterpret_cast<const uint2*>(src);
     const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
@@ -718,7 +736,8 @@ constexpr uint32_t S_STAGE = 73728;        // M image 32K | Q image 16K | b slic
 constexpr uint32_t S_OFF_Q = 32768, S_OFF_B = 49152, S_OFF_O0 = 65536;
 constexpr uint32_t S_STILE = 2 * S_STAGE;  // state operand, two tiles by chunk parity: bf16 [128 dk][64] swizzled
                                            // (32 columns used); chunk c's MMAs read tile c % 2
-constexpr uint32_t S_MISC = S_STILE + 2 * 16384;
+constexpr uint32_t S_XPOSE = S_STILE + 2 * 16384;  // per state warp: fp32 [32 rows][36] staging of the S_c records
+constexpr uint32_t S_MISC = S_XPOSE + 4 * 32 * 36 * 4;
 constexpr uint32_t S_SMEM = S_MISC + 256 + 1024;
 
 struct ScanMisc {
@@ -929,13 +948,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
         for (int c = 0; c < NC; ++c) {
             const int s = c & 1;
             const unsigned char* st = sm + s * S_STAGE;
-            if (p.states) {  // S_c (fp32) for the backward: row dk, this CTA's 32 columns
-                float* dst = p.states + (rec0 + (int64_t)c * rec_step) * p.states_stride + (int64_t)dk * kDv + dv0;
-#pragma unroll
-                for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
-                    *reinterpret_cast<float4*>(dst + 4 * q4) =
-                        make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
-            }
+            if (p.states)  // S_c (fp32) for the backward: the warp's 32 rows, this CTA's 32 columns
+                store_rows_coalesced<kTcDvTile>(
+                    reinterpret_cast<float*>(sm + S_XPOSE) + warp * 32 * (kTcDvTile + 4), S,
+                    p.states + (rec0 + (int64_t)c * rec_step) * p.states_stride + (int64_t)(32 * warp) * kDv + dv0,
+                    kDv, lane);
             // ---- S_{c+1} = M_c S_c + b_c (the sequential path)
             if (ok && scan_aborted(ms)) ok = false;
             if (ok && (!mbar_wait(&ms.mma_s, c & 1, kWaitNs) || !mbar_wait(&ms.full_bo[s], (c >> 1) & 1, kWaitNs)))
@@ -1016,7 +1033,8 @@ constexpr uint32_t B_STAGE = 49152;         // M image 32 KiB | Q' image 16 KiB
 constexpr uint32_t B_OFF_Q = 32768;
 constexpr uint32_t B_DO = 2 * B_STAGE;      // do tiles: bf16 [64 t][64 dv] swizzled, 8 KiB each, by parity
 constexpr uint32_t B_STILE = B_DO + 2 * 8192;  // dS operand tiles: bf16 [128 dk][64 dv] swizzled, by parity
-constexpr uint32_t B_MISC = B_STILE + 2 * 16384;
+constexpr uint32_t B_XPOSE = B_STILE + 2 * 16384;  // per state warp: fp32 [32 rows][68] staging of the dS records
+constexpr uint32_t B_MISC = B_XPOSE + 4 * 32 * 68 * 4;
 constexpr uint32_t B_SMEM = B_MISC + 256 + 1024;
 
 struct BsMisc {
@@ -1156,13 +1174,11 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
             }
             tc_fence_before();
             named_bar_arrive(kBsBar, kBsBarCount);
-            {  // dS_{c+1} (fp32) for the chunk kernels, while the MMAs run
-                float* dst = p.bws + ((int64_t)bh * NC + c) * kBwChunkFloats + kBwDSe + (int64_t)dk * kDv + dv0;
-#pragma unroll
-                for (int q4 = 0; q4 < 16; ++q4)
-                    *reinterpret_cast<float4*>(dst + 4 * q4) =
-                        make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
-            }
+            // dS_{c+1} (fp32) for the chunk kernels, while the MMAs run: the warp's 32 rows, 64 columns
+            store_rows_coalesced<64>(reinterpret_cast<float*>(sm + B_XPOSE) + warp * 32 * 68, S,
+                                     p.bws + ((int64_t)bh * NC + c) * kBwChunkFloats + kBwDSe +
+                                         (int64_t)(32 * warp) * kDv + dv0,
+                                     kDv, lane);
             if (ok && bs_aborted(ms)) ok = false;
             if (ok && !mbar_wait(&ms.mma, it & 1, kWaitNs)) ok = false;
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
