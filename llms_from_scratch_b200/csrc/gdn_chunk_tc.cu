@@ -156,15 +156,19 @@ __device__ __forceinline__ void store_f32x16(float* dst, const float* v) {
 // Rows held one per lane (lane l: row l of a 32-row block, kN fp32 values in v) stored to global rows
 // g + l * ld through the warp's staging tile [32][kN + 4]: each store instruction then writes whole
 // 128-byte lines instead of 32 lines a 16-byte piece each.
-template <int kN>
+// kRows < 32: only lanes 0 .. kRows-1 hold rows (an M=64 accumulator's lanes).
+template <int kN, int kRows = 32>
 __device__ __forceinline__ void store_rows_coalesced(float* stage, const float* v, float* g, int64_t ld, int lane) {
     constexpr int kS = kN + 4, kC = kN / 4;  // padded row stride; 16-byte pieces per row
+    if (lane < kRows) {
 #pragma unroll
-    for (int q4 = 0; q4 < kC; ++q4)
-        *reinterpret_cast<float4*>(stage + lane * kS + 4 * q4) = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+        for (int q4 = 0; q4 < kC; ++q4)
+            *reinterpret_cast<float4*>(stage + lane * kS + 4 * q4) =
+                make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+    }
     __syncwarp();
 #pragma unroll
-    for (int j = 0; j < kC; ++j) {
+    for (int j = 0; j < kRows * kC / 32; ++j) {
         const int idx = 32 * j + lane, row = idx / kC, piece = idx % kC;
         *reinterpret_cast<float4*>(g + row * ld + 4 * piece) = *reinterpret_cast<const float4*>(stage + row * kS + 4 * piece);
     }
@@ -1358,13 +1362,9 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
         for (int part = 0; part < 2; ++part) {
             float d[32];
             const int col0 = 64 * chalf + 32 * part;
-            tmem_ld32(tmem_addr(tm, 32 * q, col0), d);  // dv_new
+            tmem_ld32(tmem_addr(tm, 32 * q, col0), d);  // dv_new (its record is written at the end)
             tmem_ld_wait();
             if (rl) {
-#pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4)
-                    *reinterpret_cast<float4*>(bw + kBwDVn + row * kDv + col0 + 4 * q4) =
-                        make_float4(d[4 * q4], d[4 * q4 + 1], d[4 * q4 + 2], d[4 * q4 + 3]);
 #pragma unroll
                 for (int q8 = 0; q8 < 4; ++q8)  // rows 64.. of the (3) A tile
                     store_split8(sm + T_A, sm + T_A + 32768, sw128_offset(64 + row, col0 + 8 * q8, 128), d + 8 * q8);
@@ -1380,8 +1380,6 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
                     vn[4 * q4 + 1] = u.y - d[4 * q4 + 1];
                     vn[4 * q4 + 2] = u.z - d[4 * q4 + 2];
                     vn[4 * q4 + 3] = u.w - d[4 * q4 + 3];
-                    *reinterpret_cast<float4*>(bw + kBwVn + row * kDv + col0 + 4 * q4) =
-                        make_float4(vn[4 * q4], vn[4 * q4 + 1], vn[4 * q4 + 2], vn[4 * q4 + 3]);
                 }
 #pragma unroll
                 for (int q8 = 0; q8 < 4; ++q8)  // the (4) A tile: hi in place of do's B tile, lo after the w tiles
@@ -1428,27 +1426,37 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
     ok = !__syncthreads_or(!ok);
     tc_fence_after();
     if (ok) {
-        // (3): row r = 32 q + lane (M=128), columns split by warp / 4
-        const int r = 32 * q + lane;
+        // The records, each warp's 32 (M=128) or 16 (M=64) rows x 32 columns at a time through its staging tile in
+        // the S operand region (read by the MMAs just completed): (3) row 32 q + lane, (1) (2) (4) row 16 q + lane.
+        float* stage = reinterpret_cast<float*>(sm + T_S) + warp * 32 * 36;
+        const float sgn = q < 2 ? 1.f : -1.f;  // (3): rows 0-63 dQg, 64-127 -dw
         for (int part = 0; part < 2; ++part) {
             float d[32];
             const int col0 = 64 * chalf + 32 * part;
-            tmem_ld32(tmem_addr(tm, 32 * q, 256 + col0), d);
+            tmem_ld32(tmem_addr(tm, 32 * q, 256 + col0), d);  // (3)
             tmem_ld_wait();
-            float* dst = r < 64 ? bw + kBwDQg + r * kDk + col0 : bw + kBwDW + (r - 64) * kDk + col0;
-            const float sgn = r < 64 ? 1.f : -1.f;
 #pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4)
-                *reinterpret_cast<float4*>(dst + 4 * q4) =
-                    make_float4(sgn * d[4 * q4], sgn * d[4 * q4 + 1], sgn * d[4 * q4 + 2], sgn * d[4 * q4 + 3]);
-            tmem_ld32(tmem_addr(tm, 32 * q, 384 + col0), d);  // (4), M=64
+            for (int e = 0; e < 32; ++e) d[e] *= sgn;
+            store_rows_coalesced<32>(stage, d, bw + (q < 2 ? kBwDQg : kBwDW) + (32 * (q & 1)) * kDk + col0, kDk, lane);
+            tmem_ld32(tmem_addr(tm, 32 * q, 384 + col0), d);  // (4) dKd, M=64
+            tmem_ld_wait();
+            store_rows_coalesced<32, 16>(stage, d, bw + kBwDKd + (16 * q) * kDk + col0, kDk, lane);
+            tmem_ld32(tmem_addr(tm, 32 * q, col0), d);  // (1) dv_new, M=64
+            tmem_ld_wait();
+            store_rows_coalesced<32, 16>(stage, d, bw + kBwDVn + (16 * q) * kDv + col0, kDv, lane);
+            tmem_ld32(tmem_addr(tm, 32 * q, 128 + col0), d);  // (2) w S, M=64: v_new = u - w S
             tmem_ld_wait();
             if (rl) {
 #pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4)
-                    *reinterpret_cast<float4*>(bw + kBwDKd + row * kDk + col0 + 4 * q4) =
-                        make_float4(d[4 * q4], d[4 * q4 + 1], d[4 * q4 + 2], d[4 * q4 + 3]);
+                for (int q4 = 0; q4 < 8; ++q4) {
+                    const float4 u = *reinterpret_cast<const float4*>(fw + kWsU + row * kDv + col0 + 4 * q4);
+                    d[4 * q4] = u.x - d[4 * q4];
+                    d[4 * q4 + 1] = u.y - d[4 * q4 + 1];
+                    d[4 * q4 + 2] = u.z - d[4 * q4 + 2];
+                    d[4 * q4 + 3] = u.w - d[4 * q4 + 3];
+                }
             }
+            store_rows_coalesced<32, 16>(stage, d, bw + kBwVn + (16 * q) * kDv + col0, kDv, lane);
         }
     }
     dgam = warp_sum(dgam);
