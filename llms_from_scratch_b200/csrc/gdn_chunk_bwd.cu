@@ -868,9 +868,13 @@ cudaError_t launch_chunk_bwd(const ChunkParams& fwd, const BwdParams& p, cudaStr
         note_launch();
     }
     if ((e = phase_event(4, stream)) != cudaSuccess) return e;
-    gdn_bwd_wy<<<nchunks, kWide, sizeof(WySmem), stream>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    note_launch();
+    if (p.tc_records) {  // bf16 mode: the WY products on the tensor cores
+        if ((e = launch_bwd_wy_tc(p, stream)) != cudaSuccess) return e;
+    } else {
+        gdn_bwd_wy<<<nchunks, kWide, sizeof(WySmem), stream>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        note_launch();
+    }
     if ((e = phase_event(5, stream)) != cudaSuccess) return e;
     if (p.tc_records) {  // bf16 mode: the chain rule's products on the tensor cores
         if ((e = launch_bwd_grads_tc(p, stream)) != cudaSuccess) return e;

@@ -1475,6 +1475,294 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
     }
 }
 
+// ============================================================================ backward WY terms
+// gdn_bwd_wy_tc: the WY part of the chunk's backward in bf16 mode, one CTA (16 warps) per chunk; the
+// CUDA-core gdn_bwd_wy with its three products on the tensor cores (M=64 accumulators: row 16 q + l in
+// lane 32 q + l, l < 16):
+//   1. G = k^ k^T (exact bf16 operands) and dAqk = incl(do v_new^T) (v_new as hi/lo)   -> cols [0,64), [64,128)
+//   2. L^T from G; dAqk -> its record
+//   3. X = [d(beta v) | d(beta e^gc k^)] = (I - L)^-T [dv_new | dw] by back substitution (warps 0-7, one
+//      column each), written as hi/lo A tiles; warps 8-15 meanwhile stage [u | w] as hi/lo B tiles
+//   4. row-wise: dv = beta d(beta v), dKp = beta e^gc d(beta e^gc k^), the dbeta and dgc parts
+//   5. dL = strict(X [u | w]^T) (K=256, three hi/lo passes)                               -> cols [128,192)
+constexpr int kWtThreads = 512;
+constexpr uint32_t kWtTmemCols = 256;
+constexpr uint32_t W_K = 0;          // k^ bf16 [64][128], K-major (atom columns 8 KiB apart)
+constexpr uint32_t W_DO = 16384;     // do bf16 [64][128], K-major; with W_VN the output staging after step 1
+constexpr uint32_t W_VN = 32768;     // v_new hi | lo bf16 [64][128] (16 KiB each)
+constexpr uint32_t W_LT = 65536;     // fp32 L^T [64][68]
+constexpr uint32_t W_XA = 82944;     // X hi | lo bf16 [64][256] (32 KiB each), K-major (atom columns 8 KiB apart)
+constexpr uint32_t W_UW = 148480;    // [u | w] hi | lo, same layout
+constexpr uint32_t W_MISC = 214016;
+struct WtMisc {
+    float gc[64], beta[64], egc[64], ekd[64];
+    uint64_t bar;
+    uint32_t tmem;
+};
+constexpr uint32_t W_SMEM = W_MISC + (uint32_t)sizeof(WtMisc) + 1024;
+static_assert(W_XA % 1024 == 0 && W_UW % 1024 == 0 && W_LT + 64 * 68 * 4 <= W_XA, "tile alignment");
+static_assert(16 * 32 * 20 * 4 <= W_LT - W_DO, "output staging");
+
+__global__ void __launch_bounds__(kWtThreads, 1) gdn_bwd_wy_tc(BwdParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    WtMisc& ms = *reinterpret_cast<WtMisc*>(sm + W_MISC);
+    float(*Lt)[68] = reinterpret_cast<float(*)[68]>(sm + W_LT);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t ci = blockIdx.x;
+    const int c = (int)(ci % p.NC), bh = (int)(ci / p.NC), b = bh / p.H, h = bh % p.H;
+    const int64_t t0 = (int64_t)c * kChunk;
+    const float* fw = p.fws + ci * kWsChunkFloats;
+    float* bw = p.bws + ci * kBwChunkFloats;
+    const __nv_bfloat16* dout = reinterpret_cast<const __nv_bfloat16*>(p.dout.p);
+    const __nv_bfloat16* vin = reinterpret_cast<const __nv_bfloat16*>(p.v.p);
+
+    if (tid == 0) {  // the substitution's right-hand sides into L2 meanwhile
+        bulk_prefetch_l2(bw + kBwDVn, kChunk * kDv * 4);
+        bulk_prefetch_l2(bw + kBwDW, kChunk * kDk * 4);
+    }
+    if (warp == 0) {
+        tmem_alloc(&ms.tmem, kWtTmemCols);
+        tmem_relinquish();
+    }
+    if (tid == 32) {
+        mbar_init(&ms.bar, 1);
+        fence_mbar_init();
+    }
+    // do rows (bf16) and v_new (fp32 -> hi/lo): two 8-column pieces each a thread
+    {
+        uint4 du[2];
+        float4 vv[2][2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int idx = tid + u * kWtThreads, r = idx >> 4, c8 = (idx & 15) * 8;
+            const int64_t t = t0 + r;
+            du[u] = t < p.T ? *reinterpret_cast<const uint4*>(dout + (int64_t)b * p.dout.sb + t * p.dout.st +
+                                                              (int64_t)h * p.dout.sh + c8)
+                            : make_uint4(0u, 0u, 0u, 0u);
+            vv[u][0] = *reinterpret_cast<const float4*>(bw + kBwVn + r * kDv + c8);
+            vv[u][1] = *reinterpret_cast<const float4*>(bw + kBwVn + r * kDv + c8 + 4);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int idx = tid + u * kWtThreads, r = idx >> 4, c8 = (idx & 15) * 8;
+            const uint32_t off = sw128_offset(r, c8, 64);
+            *reinterpret_cast<uint4*>(sm + W_DO + off) = du[u];
+            const float x[8] = {vv[u][0].x, vv[u][0].y, vv[u][0].z, vv[u][0].w,
+                                vv[u][1].x, vv[u][1].y, vv[u][1].z, vv[u][1].w};
+            store_split8(sm + W_VN, sm + W_VN + 16384, off, x);
+        }
+    }
+    // this thread's v entries for step 4 (rows ty + 32 r, columns 4 tx and 64 + 4 tx), requested now
+    const int ty = tid >> 4, tx = tid & 15;
+    const int cols[2] = {4 * tx, 64 + 4 * tx};
+    uint2 vraw[2][2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int64_t t = t0 + ty + 32 * r;
+#pragma unroll
+        for (int hlf = 0; hlf < 2; ++hlf)
+            vraw[r][hlf] = t < p.T ? *reinterpret_cast<const uint2*>(vin + (int64_t)b * p.v.sb + t * p.v.st +
+                                                                      (int64_t)h * p.v.sh + cols[hlf])
+                                   : make_uint2(0u, 0u);
+    }
+    {  // k^ rows (a warp's 4 rows, 4 columns a lane), normalised as the forward does
+        float x[4][4], r;
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) bwd::row4_bf16(p.k, b, t0 + warp + 16 * rr, p.T, h, lane, x[rr]);
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+            const int i = warp + 16 * rr;
+            bwd::qk_norm(p.k, t0 + i, p.T, p.l2norm, x[rr], r);
+            store_bf16x4(sm + W_K, sw128_offset(i, 4 * lane, 64), x[rr]);
+        }
+    }
+    bwd::chunk_gates(p, b, h, t0, ms.gc, ms.beta, ms.egc, ms.ekd, true);  // its barriers publish the tiles
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = ms.tmem, sb = smem_u32(sm);
+
+    // ---- 1. G = k^ k^T -> [0,64); dAqk = do v_new^T -> [64,128)
+    if (tid == 0) {
+        const uint32_t id = make_idesc_f16(64, 64, false, false, true);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t d = make_sdesc(sb + W_K + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024, kSwizzle128B);
+            mma_f16(tm, d, d, id, ks > 0);
+        }
+#pragma unroll
+        for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+                mma_f16(tm + 64, make_sdesc(sb + W_DO + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024, kSwizzle128B),
+                        make_sdesc(sb + W_VN + s2 * 16384 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024, kSwizzle128B),
+                        id, (s2 | ks) != 0);
+        mma_commit(&ms.bar);
+    }
+    bool ok = mbar_wait(&ms.bar, 0, kWaitNs);
+    tc_fence_after();
+    ok = !__syncthreads_or(!ok);
+
+    // ---- 2. L^T; the dAqk record (through the warp's staging tile over do / v_new, read by the MMAs)
+    const int q = warp & 3, cg = warp >> 2, row = 16 * q + (lane & 15), j0 = 16 * cg;
+    float* stage = reinterpret_cast<float*>(sm + W_DO) + warp * 32 * 20;
+    if (ok) {
+        float gv[16];
+        tmem_ld16(tmem_addr(tm, 32 * q, j0), gv);
+        tmem_ld_wait();
+        if (lane < 16) {
+            const float bi = ms.beta[row], gci = ms.gc[row];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const int j = j0 + e;
+                Lt[j][row] = (row > j) ? -(bi * gv[e]) * expf(gci - ms.gc[j]) : 0.f;
+            }
+        }
+        tmem_ld16(tmem_addr(tm, 32 * q, 64 + j0), gv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) gv[e] = (row >= j0 + e) ? gv[e] : 0.f;
+        store_rows_coalesced<16, 16>(stage, gv, bw + kBwDA + (16 * q) * kChunk + j0, kChunk, lane);
+    }
+    __syncthreads();  // L^T is complete
+
+    // ---- 3. back substitution (warps 0-7) | [u | w] hi/lo B tiles (warps 8-15)
+    if (tid < kDv + kDk) {  // x_i = rhs_i + sum_{m > i} L_mi x_m, i = 63 .. 0, for column tid
+        const int col = tid;
+        const float* src = bw + (col < kDv ? kBwDVn + col : kBwDW + (col - kDv));
+        float x[kChunk];
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) x[i] = src[i * kDv];
+#pragma unroll
+        for (int i = kChunk - 2; i >= 0; --i) {
+            float a0 = x[i], a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+            for (int m4 = (i + 1) / 4; m4 < kChunk / 4; ++m4) {
+                const float4 l = *reinterpret_cast<const float4*>(&Lt[i][4 * m4]);  // L_mi = 0 for m <= i
+                a0 += l.x * x[4 * m4];
+                a1 += l.y * x[4 * m4 + 1];
+                a2 += l.z * x[4 * m4 + 2];
+                a3 += l.w * x[4 * m4 + 3];
+            }
+            x[i] = (a0 + a1) + (a2 + a3);
+        }
+        __nv_bfloat16* xh = reinterpret_cast<__nv_bfloat16*>(sm + W_XA);
+        __nv_bfloat16* xl = reinterpret_cast<__nv_bfloat16*>(sm + W_XA + 32768);
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+            const uint32_t off = sw128_offset(i, col, 64) >> 1;
+            const __nv_bfloat16 hb = __float2bfloat16_rn(x[i]);
+            xh[off] = hb;
+            xl[off] = __float2bfloat16_rn(x[i] - __bfloat162float(hb));
+        }
+    } else {  // [u | w] rows j: 64 x 256 in 8-column pieces, 8 a thread
+        const int t2 = tid - (kDv + kDk);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int idx = t2 + 256 * u, r = idx >> 5, c8 = (idx & 31) * 8;
+            const float* srcu = fw + (c8 < kDv ? kWsU + r * kDv + c8 : kWsW + r * kDk + (c8 - kDv));
+            const float4 a = *reinterpret_cast<const float4*>(srcu), bq = *reinterpret_cast<const float4*>(srcu + 4);
+            const float x[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
+            store_split8(sm + W_UW, sm + W_UW + 32768, sw128_offset(r, c8, 64), x);
+        }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    // ---- 5 (issued first). dL = X [u | w]^T -> [128,192): passes (hi, hi), (hi, lo), (lo, hi)
+    if (ok && tid == 0) {
+        const uint32_t id = make_idesc_f16(64, 64, false, false, true);
+        const uint32_t pa[3] = {0u, 0u, 1u}, pb[3] = {0u, 1u, 0u};
+#pragma unroll
+        for (int ps = 0; ps < 3; ++ps)
+#pragma unroll
+            for (int ks = 0; ks < 16; ++ks)
+                mma_f16(tm + 128,
+                        make_sdesc(sb + W_XA + pa[ps] * 32768 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024, kSwizzle128B),
+                        make_sdesc(sb + W_UW + pb[ps] * 32768 + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024, kSwizzle128B),
+                        id, (ps | ks) != 0);
+        mma_commit(&ms.bar);
+    }
+
+    // ---- 4. row-wise terms (rows ty + 32 r, columns cols[hlf] .. + 3), X read back as hi + lo
+    if (ok) {
+        const __nv_bfloat16* xtile = reinterpret_cast<const __nv_bfloat16*>(sm + W_XA);
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int i = ty + 32 * r;
+            const int64_t t = t0 + i;
+            const float bi = ms.beta[i], be = ms.beta[i] * ms.egc[i];
+            float sv = 0.f, sk = 0.f;
+#pragma unroll
+            for (int hlf = 0; hlf < 2; ++hlf) {
+                const int cc = cols[hlf];
+                float xv[4], xk[4], kv[4];
+                {
+                    const uint32_t ov = sw128_offset(i, cc, 64), ok2 = sw128_offset(i, kDv + cc, 64);
+                    float hi[4], lo[4];
+                    load_bf16x4_smem(sm + W_XA + ov, hi);
+                    load_bf16x4_smem(sm + W_XA + 32768 + ov, lo);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) xv[e] = hi[e] + lo[e];
+                    load_bf16x4_smem(sm + W_XA + ok2, hi);
+                    load_bf16x4_smem(sm + W_XA + 32768 + ok2, lo);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) xk[e] = hi[e] + lo[e];
+                    load_bf16x4_smem(sm + W_K + sw128_offset(i, cc, 64), kv);
+                }
+                const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vraw[r][hlf].x));
+                const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vraw[r][hlf].y));
+                sv += v01.x * xv[0] + v01.y * xv[1] + v23.x * xv[2] + v23.y * xv[3];
+                if (t < p.T) {
+                    const int64_t ob = (int64_t)b * p.dv.sb + t * p.dv.st + (int64_t)h * p.dv.sh + cc;
+                    __nv_bfloat16* o16 = reinterpret_cast<__nv_bfloat16*>(p.dv.p) + ob;
+                    if (p.dv.dtype == GDN_BF16 && (reinterpret_cast<uintptr_t>(o16) & 7) == 0) {
+                        *reinterpret_cast<uint2*>(o16) = make_uint2(pack_bf16x2(bi * xv[0], bi * xv[1]),
+                                                                    pack_bf16x2(bi * xv[2], bi * xv[3]));
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) store_elem(p.dv.p, ob + e, p.dv.dtype, bi * xv[e]);
+                    }
+                }
+                sk += kv[0] * xk[0] + kv[1] * xk[1] + kv[2] * xk[2] + kv[3] * xk[3];
+                *reinterpret_cast<float4*>(bw + kBwDKp + i * kDk + cc) =
+                    make_float4(be * xk[0], be * xk[1], be * xk[2], be * xk[3]);
+            }
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) {
+                sv += __shfl_xor_sync(0xffffffffu, sv, o);
+                sk += __shfl_xor_sync(0xffffffffu, sk, o);
+            }
+            if (tx == 0) {
+                bw[kBwSmall + 64 + i] = sv + ms.egc[i] * sk;  // dbeta: v . d(beta v) + e^gc k^ . d(beta e^gc k^)
+                bw[kBwSmall + 128 + i] = be * sk;             // dgc:   (beta e^gc k^) . d(beta e^gc k^)
+            }
+        }
+    }
+    if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);
+    tc_fence_after();
+    ok = !__syncthreads_or(!ok);
+    if (ok) {  // the dL record (strictly lower)
+        float gv[16];
+        tmem_ld16(tmem_addr(tm, 32 * q, 128 + j0), gv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) gv[e] = (row > j0 + e) ? gv[e] : 0.f;
+        store_rows_coalesced<16, 16>(stage, gv, bw + kBwDL + (16 * q) * kChunk + j0, kChunk, lane);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && !ok) report(p.err, kErrTimeoutPrep);
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tm, kWtTmemCols);
+    }
+}
+
 // ============================================================================ backward gradients
 // gdn_bwd_grads_tc: the chain rule of one chunk in bf16 mode, one CTA (16 warps) per chunk, with the products
 // of the CUDA-core gdn_bwd_grads on the tensor cores:
@@ -1943,6 +2231,16 @@ cudaError_t launch_bwd_states_tc(const BwdParams& p, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(gdn_bwd_states_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)T_SMEM);
     if (e != cudaSuccess) return e;
     gdn_bwd_states_tc<<<(unsigned)((int64_t)p.B * p.H * p.NC), kBtThreads, T_SMEM, stream>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    note_launch();
+    return cudaSuccess;
+}
+
+cudaError_t launch_bwd_wy_tc(const BwdParams& p, cudaStream_t stream) {
+    static_assert(W_SMEM <= 227 * 1024, "shared memory budget");
+    cudaError_t e = cudaFuncSetAttribute(gdn_bwd_wy_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)W_SMEM);
+    if (e != cudaSuccess) return e;
+    gdn_bwd_wy_tc<<<(unsigned)((int64_t)p.B * p.H * p.NC), kWtThreads, W_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     return cudaSuccess;

@@ -126,6 +126,9 @@ cudaError_t launch_bwd_states_tc(const BwdParams& p, cudaStream_t stream);
 // The chain rule of every chunk on the tensor cores (p.tc_records mode): dq, dk, dg, dbeta from the records of
 // gdn_bwd_wy and gdn_bwd_states_tc.
 cudaError_t launch_bwd_grads_tc(const BwdParams& p, cudaStream_t stream);
+// The WY terms of every chunk with their products on the tensor cores (p.tc_records mode): dv, the dKp,
+// dL and dAqk records and the dbeta / dgc parts.
+cudaError_t launch_bwd_wy_tc(const BwdParams& p, cudaStream_t stream);
 
 struct RecurrentParams {
     View4 q, k, v;
