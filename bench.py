@@ -322,7 +322,7 @@ def time_backward(torch, lib, flush, device, T, H, reps=10):
         total.append(ev[0].elapsed_time(ev[6]))
     ms = _cold_median(torch, fn, flush, reps)  # the call without the phase events between its kernels
     return {"workload": f"chunk backward B=1 T={T} H={H}, bf16 q/k/v and d_out, fp32 g/beta/states, l2norm in "
-                        "kernel, d_final_state given; tensor-core scans and state products, CUDA-core chunk kernels",
+                        "kernel, d_final_state given; every kernel on the tensor cores (bf16 mode)",
             "ms": ms, "tok_s": T / (ms / 1e3), "ms_instrumented": statistics.median(total),
             "kernels_ms": {n: statistics.median(parts[n]) for n in names}}
 
