@@ -629,11 +629,13 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
 #pragma unroll
                 for (int q8 = 0; q8 < 2; ++q8)
                     store_split8(sm + P_PYH, sm + P_PYL, sw128_offset(i, d0 + 8 * q8, 64), v + 8 * q8);
-            } else {  // o0 = Aqk u, fp32 column tile d0/32, straight to the workspace
+            } else {  // o0 = Aqk u, fp32 column tile d0/32, straight to the workspace: the tile is stored
+                      // chunk-major ([8 chunks of 4 columns][64 rows][4]), so each store of a warp (32 rows, one
+                      // chunk) writes 512 contiguous bytes
                 unsigned char* blk = wrec + kTcO0 + (d0 >> 5) * (64 * 128);
 #pragma unroll
                 for (int q4 = 0; q4 < 4; ++q4)
-                    *reinterpret_cast<float4*>(blk + f32blk_offset(i, ((d0 & 31) >> 2) + q4)) =
+                    *reinterpret_cast<float4*>(blk + (((d0 & 31) >> 2) + q4) * 1024 + i * 16) =
                         make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
             }
         }
@@ -770,7 +772,7 @@ __device__ __forceinline__ void scan_store_output(const ChunkParams& p, const un
     float ov[32];
 #pragma unroll
     for (int q4 = 0; q4 < 8; ++q4) {
-        const float4 oo = *reinterpret_cast<const float4*>(st + S_OFF_O0 + f32blk_offset(tok, q4));
+        const float4 oo = *reinterpret_cast<const float4*>(st + S_OFF_O0 + q4 * 1024 + tok * 16);  // chunk-major tile
         ov[4 * q4] = o[4 * q4] + oo.x;
         ov[4 * q4 + 1] = o[4 * q4 + 1] + oo.y;
         ov[4 * q4 + 2] = o[4 * q4 + 2] + oo.z;

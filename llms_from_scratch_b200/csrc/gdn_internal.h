@@ -23,7 +23,7 @@ constexpr int64_t kWsChunkFloats = kWsGamma + 64;       // keeps every chunk 256
 constexpr int64_t kTcM = 0;             // M_c = e^gc_last I - kd^T w, bf16 K-major image [128][128]   32 KiB
 constexpr int64_t kTcQ = 32768;         // Q'_c = q e^gc Dk^-1/2 - Aqk w, bf16 K-major image [64][128] 16 KiB
 constexpr int64_t kTcB = 49152;         // b_c = kd^T u, fp32 [4 column tiles][128][32], rows swizzled   64 KiB
-constexpr int64_t kTcO0 = 114688;       // o0_c = Aqk u, fp32 [4 column tiles][64][32], rows swizzled    32 KiB
+constexpr int64_t kTcO0 = 114688;       // o0_c = Aqk u, fp32 [4 column tiles][8 chunks][64 rows][4]     32 KiB
 constexpr int64_t kTcChunkBytes = 147456;
 constexpr int kTcDvTile = 32;           // state columns per scan CTA
 
