@@ -146,11 +146,17 @@ __device__ __forceinline__ uint32_t f32blk_offset(int row, int chunk4) {
     return (uint32_t)row * 128u + (uint32_t)((chunk4 ^ (row & 7)) * 16);
 }
 
-// 16 consecutive fp32 values to global memory (dst 16-byte aligned).
-__device__ __forceinline__ void store_f32x16(float* dst, const float* v) {
+// The backward tiles (u, w, Kd [64][128]; Aqk [64][64]) as the tensor-core prep writes them: chunk-major,
+// element (row, col) at ((col / 4) * 64 + row) * 4 + col % 4, so the prep's stores from TMEM (a lane per
+// row, four columns per store) write 512 contiguous bytes per warp.
+__host__ __device__ constexpr int64_t cm_offset(int row, int col) { return ((int64_t)(col >> 2) * 64 + row) * 4 + (col & 3); }
+
+// Row `row`, columns col0 .. col0+15 of a chunk-major backward tile.
+__device__ __forceinline__ void store_cm16(float* tile, int row, int col0, const float* v) {
 #pragma unroll
     for (int q4 = 0; q4 < 4; ++q4)
-        *reinterpret_cast<float4*>(dst + 4 * q4) = make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
+        *reinterpret_cast<float4*>(tile + cm_offset(row, col0 + 4 * q4)) =
+            make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
 }
 
 // Rows held one per lane (lane l: row l of a 32-row block, kN fp32 values in v) stored to global rows
@@ -376,7 +382,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
 #pragma unroll
             for (int q8 = 0; q8 < 2; ++q8)
                 store_split8(sm + P_AQK, sm + P_AQK + 8192, sw128_offset(i, 16 * part + 8 * q8, 64), a + 8 * q8);
-            if (p.bwd_tiles) store_f32x16(p.bwd_tiles + chunk * kWsChunkFloats + kWsAqk + i * kChunk + 16 * part, a);
+            if (p.bwd_tiles) store_cm16(p.bwd_tiles + chunk * kWsChunkFloats + kWsAqk, i, 16 * part, a);
         }
     } else {
         ok = false;
@@ -586,7 +592,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
             tmem_ld_wait();
             if (r < 64) {  // P_X (MN-major B tile: rows = tokens)
                 if (tiles) {
-                    store_f32x16(tiles + kWsW + i * kDk + d0, v);
+                    store_cm16(tiles + kWsW, i, d0, v);
                     float kd[16];  // Kd = k^ e^(gc_last - gc), from the k^ rows of KQ
 #pragma unroll
                     for (int q8 = 0; q8 < 2; ++q8) {
@@ -595,7 +601,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
 #pragma unroll
                         for (int e = 0; e < 8; ++e) kd[8 * q8 + e] = __bfloat162float(kb[e]) * ed;
                     }
-                    store_f32x16(tiles + kWsKd + i * kDk + d0, kd);
+                    store_cm16(tiles + kWsKd, i, d0, kd);
                 }
 #pragma unroll
                 for (int e = 0; e < 16; ++e) v[e] *= ed;
@@ -623,7 +629,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
             tmem_ld16(tmem_addr(tm, 32 * quad, 128 + d0), v);
             tmem_ld_wait();
             if (r < 64) {  // P_Y
-                if (tiles) store_f32x16(tiles + kWsU + i * kDv + d0, v);
+                if (tiles) store_cm16(tiles + kWsU, i, d0, v);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) v[e] *= ed;
 #pragma unroll
@@ -1287,22 +1293,22 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
     {  // Kd and w: 4 groups each per thread; Aqk (rows j, columns t: the MN-major A^T): 2 groups
         float4 v[4][4], a[2][2];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int idx = tid + u * kBtThreads, r = idx >> 4, c8 = (idx & 15) * 8;
-            v[u][0] = *reinterpret_cast<const float4*>(fw + kWsKd + r * kDk + c8);
-            v[u][1] = *reinterpret_cast<const float4*>(fw + kWsKd + r * kDk + c8 + 4);
-            v[u][2] = *reinterpret_cast<const float4*>(fw + kWsW + r * kDk + c8);
-            v[u][3] = *reinterpret_cast<const float4*>(fw + kWsW + r * kDk + c8 + 4);
+        for (int u = 0; u < 4; ++u) {  // chunk-major tiles: consecutive threads take consecutive rows
+            const int idx = tid + u * kBtThreads, r = idx & 63, c8 = (idx >> 6) * 8;
+            v[u][0] = *reinterpret_cast<const float4*>(fw + kWsKd + cm_offset(r, c8));
+            v[u][1] = *reinterpret_cast<const float4*>(fw + kWsKd + cm_offset(r, c8 + 4));
+            v[u][2] = *reinterpret_cast<const float4*>(fw + kWsW + cm_offset(r, c8));
+            v[u][3] = *reinterpret_cast<const float4*>(fw + kWsW + cm_offset(r, c8 + 4));
         }
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-            const int idx = tid + u * kBtThreads, r = idx >> 3, c8 = (idx & 7) * 8;
-            a[u][0] = *reinterpret_cast<const float4*>(fw + kWsAqk + r * kChunk + c8);
-            a[u][1] = *reinterpret_cast<const float4*>(fw + kWsAqk + r * kChunk + c8 + 4);
+            const int idx = tid + u * kBtThreads, r = idx & 63, c8 = (idx >> 6) * 8;
+            a[u][0] = *reinterpret_cast<const float4*>(fw + kWsAqk + cm_offset(r, c8));
+            a[u][1] = *reinterpret_cast<const float4*>(fw + kWsAqk + cm_offset(r, c8 + 4));
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const int idx = tid + u * kBtThreads, r = idx >> 4, c8 = (idx & 15) * 8;
+            const int idx = tid + u * kBtThreads, r = idx & 63, c8 = (idx >> 6) * 8;
             const uint32_t off = sw128_offset(r, c8, 64);
             const float kx[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w, v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
             const float wx[8] = {v[u][2].x, v[u][2].y, v[u][2].z, v[u][2].w, v[u][3].x, v[u][3].y, v[u][3].z, v[u][3].w};
@@ -1311,7 +1317,7 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
         }
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-            const int idx = tid + u * kBtThreads, r = idx >> 3, c8 = (idx & 7) * 8;
+            const int idx = tid + u * kBtThreads, r = idx & 63, c8 = (idx >> 6) * 8;
             const float ax[8] = {a[u][0].x, a[u][0].y, a[u][0].z, a[u][0].w, a[u][1].x, a[u][1].y, a[u][1].z, a[u][1].w};
             store_split8(sm + T_A + 32768, sm + T_A + 40960, sw128_offset(r, c8, 64), ax);
         }
@@ -1377,7 +1383,7 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
                 float vn[32];
 #pragma unroll
                 for (int q4 = 0; q4 < 8; ++q4) {
-                    const float4 u = *reinterpret_cast<const float4*>(fw + kWsU + row * kDv + col0 + 4 * q4);
+                    const float4 u = *reinterpret_cast<const float4*>(fw + kWsU + cm_offset(row, col0 + 4 * q4));
                     vn[4 * q4] = u.x - d[4 * q4];
                     vn[4 * q4 + 1] = u.y - d[4 * q4 + 1];
                     vn[4 * q4 + 2] = u.z - d[4 * q4 + 2];
@@ -1451,7 +1457,7 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
             if (rl) {
 #pragma unroll
                 for (int q4 = 0; q4 < 8; ++q4) {
-                    const float4 u = *reinterpret_cast<const float4*>(fw + kWsU + row * kDv + col0 + 4 * q4);
+                    const float4 u = *reinterpret_cast<const float4*>(fw + kWsU + cm_offset(row, col0 + 4 * q4));
                     d[4 * q4] = u.x - d[4 * q4];
                     d[4 * q4 + 1] = u.y - d[4 * q4 + 1];
                     d[4 * q4 + 2] = u.z - d[4 * q4 + 2];
@@ -1663,9 +1669,10 @@ __global__ void __launch_bounds__(kWtThreads, 1) gdn_bwd_wy_tc(BwdParams p) {
         const int t2 = tid - (kDv + kDk);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-            const int idx = t2 + 256 * u, r = idx >> 5, c8 = (idx & 31) * 8;
-            const float* srcu = fw + (c8 < kDv ? kWsU + r * kDv + c8 : kWsW + r * kDk + (c8 - kDv));
-            const float4 a = *reinterpret_cast<const float4*>(srcu), bq = *reinterpret_cast<const float4*>(srcu + 4);
+            const int idx = t2 + 256 * u, r = idx & 63, c8 = (idx >> 6) * 8;  // chunk-major tiles: rows consecutive
+            const float* tile = fw + (c8 < kDv ? kWsU : kWsW);
+            const float4 a = *reinterpret_cast<const float4*>(tile + cm_offset(r, c8 & 127)),
+                         bq = *reinterpret_cast<const float4*>(tile + cm_offset(r, (c8 & 127) + 4));
             const float x[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
             store_split8(sm + W_UW, sm + W_UW + 32768, sw128_offset(r, c8, 64), x);
         }

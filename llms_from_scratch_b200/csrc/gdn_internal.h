@@ -64,7 +64,8 @@ struct ChunkParams {
     int64_t states_stride;
     // Tensor-core prep only (fixed length): when set, every chunk's u, w, Kd and Aqk are also
     // written in fp32 to bwd_tiles + ((b*H + h)*NC + c) * kWsChunkFloats at kWsU / kWsW /
-    // kWsKd / kWsAqk, the tiles the backward's chunk kernels read.
+    // kWsKd / kWsAqk, the tiles the backward's tensor-core kernels read, chunk-major within each
+    // tile (element (row, col) at ((col / 4) * 64 + row) * 4 + col % 4).
     float* bwd_tiles;
 };
 
