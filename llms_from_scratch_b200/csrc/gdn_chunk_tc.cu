@@ -1436,19 +1436,32 @@ __global__ void __launch_bounds__(kBtThreads, 1) gdn_bwd_states_tc(BwdParams p) 
     if (ok) {
         // The records, each warp's 32 (M=128) or 16 (M=64) rows x 32 columns at a time through its staging tile in
         // the S operand region (read by the MMAs just completed): (3) row 32 q + lane, (1) (2) (4) row 16 q + lane.
+        // dQg and dKd are read only by the chain-rule kernel (a lane per row): stored chunk-major straight from
+        // the accumulator rows; dw, dv_new and v_new row-major.
         float* stage = reinterpret_cast<float*>(sm + T_S) + warp * 32 * 36;
-        const float sgn = q < 2 ? 1.f : -1.f;  // (3): rows 0-63 dQg, 64-127 -dw
         for (int part = 0; part < 2; ++part) {
             float d[32];
             const int col0 = 64 * chalf + 32 * part;
-            tmem_ld32(tmem_addr(tm, 32 * q, 256 + col0), d);  // (3)
+            tmem_ld32(tmem_addr(tm, 32 * q, 256 + col0), d);  // (3): rows 0-63 dQg, 64-127 -dw
             tmem_ld_wait();
+            if (q < 2) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) d[e] *= sgn;
-            store_rows_coalesced<32>(stage, d, bw + (q < 2 ? kBwDQg : kBwDW) + (32 * (q & 1)) * kDk + col0, kDk, lane);
+                for (int q4 = 0; q4 < 8; ++q4)
+                    *reinterpret_cast<float4*>(bw + kBwDQg + cm_offset(32 * q + lane, col0 + 4 * q4)) =
+                        make_float4(d[4 * q4], d[4 * q4 + 1], d[4 * q4 + 2], d[4 * q4 + 3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) d[e] = -d[e];
+                store_rows_coalesced<32>(stage, d, bw + kBwDW + (32 * (q & 1)) * kDk + col0, kDk, lane);
+            }
             tmem_ld32(tmem_addr(tm, 32 * q, 384 + col0), d);  // (4) dKd, M=64
             tmem_ld_wait();
-            store_rows_coalesced<32, 16>(stage, d, bw + kBwDKd + (16 * q) * kDk + col0, kDk, lane);
+            if (rl) {
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4)
+                    *reinterpret_cast<float4*>(bw + kBwDKd + cm_offset(row, col0 + 4 * q4)) =
+                        make_float4(d[4 * q4], d[4 * q4 + 1], d[4 * q4 + 2], d[4 * q4 + 3]);
+            }
             tmem_ld32(tmem_addr(tm, 32 * q, col0), d);  // (1) dv_new, M=64
             tmem_ld_wait();
             store_rows_coalesced<32, 16>(stage, d, bw + kBwDVn + (16 * q) * kDv + col0, kDv, lane);
@@ -1738,8 +1751,6 @@ __global__ void __launch_bounds__(kWtThreads, 1) gdn_bwd_wy_tc(BwdParams p) {
                     }
                 }
                 sk += kv[0] * xk[0] + kv[1] * xk[1] + kv[2] * xk[2] + kv[3] * xk[3];
-                *reinterpret_cast<float4*>(bw + kBwDKp + i * kDk + cc) =
-                    make_float4(be * xk[0], be * xk[1], be * xk[2], be * xk[3]);
             }
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) {
@@ -1750,6 +1761,19 @@ __global__ void __launch_bounds__(kWtThreads, 1) gdn_bwd_wy_tc(BwdParams p) {
                 bw[kBwSmall + 64 + i] = sv + ms.egc[i] * sk;  // dbeta: v . d(beta v) + e^gc k^ . d(beta e^gc k^)
                 bw[kBwSmall + 128 + i] = be * sk;             // dgc:   (beta e^gc k^) . d(beta e^gc k^)
             }
+        }
+    }
+    if (ok) {  // dKp = beta e^gc d(beta e^gc k^), chunk-major (read by the chain-rule kernel a lane per row)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int idx = tid + u * kWtThreads, r = idx & 63, col = 4 * (idx >> 6);
+            const uint32_t off = sw128_offset(r, kDv + col, 64);
+            float hi[4], lo[4];
+            load_bf16x4_smem(sm + W_XA + off, hi);
+            load_bf16x4_smem(sm + W_XA + 32768 + off, lo);
+            const float be = ms.beta[r] * ms.egc[r];
+            *reinterpret_cast<float4*>(bw + kBwDKp + cm_offset(r, col)) =
+                make_float4(be * (hi[0] + lo[0]), be * (hi[1] + lo[1]), be * (hi[2] + lo[2]), be * (hi[3] + lo[3]));
         }
     }
     if (ok) ok = mbar_wait(&ms.bar, 1, kWaitNs);
@@ -2044,12 +2068,12 @@ __global__ void __launch_bounds__(kGtThreads, 1) gdn_bwd_grads_tc(BwdParams p) {
         for (int hf = 0; hf < 2; ++hf) {
             const int c0 = cb + 16 * hf;
             float4 x1[4], x2[4];  // dQg | dKd, and dKp
-            const float* src1 = bw + (qrow ? kBwDQg : kBwDKd) + i * kDk + c0;
+            const float* src1 = bw + (qrow ? kBwDQg : kBwDKd);  // chunk-major records: a warp reads 512-byte runs
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4) {
-                x1[q4] = *reinterpret_cast<const float4*>(src1 + 4 * q4);
+                x1[q4] = *reinterpret_cast<const float4*>(src1 + cm_offset(i, c0 + 4 * q4));
                 x2[q4] = qrow ? make_float4(0.f, 0.f, 0.f, 0.f)
-                              : *reinterpret_cast<const float4*>(bw + kBwDKp + i * kDk + c0 + 4 * q4);
+                              : *reinterpret_cast<const float4*>(bw + kBwDKp + cm_offset(i, c0 + 4 * q4));
             }
             float v[16];
             tmem_ld16(tmem_addr(tm, 32 * quad, 64 + c0), v);

@@ -83,6 +83,8 @@ constexpr int64_t kBwDL = kBwDKp + kChunk * kDk;   // dL (strictly lower)       
 constexpr int64_t kBwDA = kBwDL + kChunk * kChunk; // dAqk (lower incl. diagonal)             [64][64]
 constexpr int64_t kBwSmall = kBwDA + kChunk * kChunk;  // [0] <S_c, dS_{c+1}>, [64..] dbeta part, [128..] dgc part
 constexpr int64_t kBwChunkFloats = kBwSmall + 192;
+// With tensor-core records (bf16 mode) kBwDQg, kBwDKd and kBwDKp are chunk-major like the prep's backward
+// tiles (element (row, col) at ((col / 4) * 64 + row) * 4 + col % 4); every other region is row-major.
 
 struct Out4 {
     void* p;
