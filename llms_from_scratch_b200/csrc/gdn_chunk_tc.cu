@@ -1040,13 +1040,14 @@ constexpr int kBsThreads = 224;
 constexpr int kBsMmaWarp = 6;
 constexpr uint32_t kBsBar = 2;              // named barrier: the state warps (128) arrive, the MMA warp waits
 constexpr uint32_t kBsBarCount = 160;
-constexpr uint32_t kBsTmemCols = 64;        // the 128 x 64 fp32 accumulator
+constexpr int kBsCols = 32;                 // gradient-state columns per CTA (four CTAs per head)
+constexpr uint32_t kBsTmemCols = 32;        // the 128 x 32 fp32 accumulator
 constexpr uint32_t B_STAGE = 49152;         // M image 32 KiB | Q' image 16 KiB
 constexpr uint32_t B_OFF_Q = 32768;
-constexpr uint32_t B_DO = 2 * B_STAGE;      // do tiles: bf16 [64 t][64 dv] swizzled, 8 KiB each, by parity
-constexpr uint32_t B_STILE = B_DO + 2 * 8192;  // dS operand tiles: bf16 [128 dk][64 dv] swizzled, by parity
-constexpr uint32_t B_XPOSE = B_STILE + 2 * 16384;  // per state warp: fp32 [32 rows][68] staging of the dS records
-constexpr uint32_t B_MISC = B_XPOSE + 4 * 32 * 68 * 4;
+constexpr uint32_t B_DO = 2 * B_STAGE;      // do tiles: bf16 [64 t][64] swizzled (this CTA's 32 columns used), by parity
+constexpr uint32_t B_STILE = B_DO + 2 * 8192;  // dS operand tiles: bf16 [128 dk][64] swizzled (32 columns used), by parity
+constexpr uint32_t B_XPOSE = B_STILE + 2 * 16384;  // per state warp: fp32 [32 rows][36] staging of the dS records
+constexpr uint32_t B_MISC = B_XPOSE + 4 * 32 * (kBsCols + 4) * 4;
 constexpr uint32_t B_SMEM = B_MISC + 256 + 1024;
 
 struct BsMisc {
@@ -1064,7 +1065,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
     BsMisc& ms = *reinterpret_cast<BsMisc*>(sm + B_MISC);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
-    const int dv0 = blockIdx.y * 64;
+    const int dv0 = blockIdx.y * kBsCols;
     const int NC = p.NC;
     const unsigned char* recs = reinterpret_cast<const unsigned char*>(p.tc_records) + (int64_t)bh * NC * kTcChunkBytes;
     if (tid == 0) {
@@ -1092,7 +1093,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
 
     if (warp == kBsMmaWarp) {
         const uint32_t leader = elect_one();
-        const uint32_t id = make_idesc_f16(128, 64, true, true, true);
+        const uint32_t id = make_idesc_f16(128, kBsCols, true, true, true);
         for (int it = 0; it < NC; ++it) {
             const int s = it & 1;
             named_bar_sync(kBsBar, kBsBarCount);  // dS_{c+1} is in operand tile s
@@ -1141,7 +1142,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
             for (int it = (issued > 2 ? issued - 2 : 0); it < issued; ++it)
                 if (!mbar_wait(&ms.full_mq[it & 1], (it >> 1) & 1, kWaitNs)) ok = false;
         }
-    } else if (warp == 5) {  // do tiles: rows t of the chunk, this CTA's 64 columns, zero past T
+    } else if (warp == 5) {  // do tiles: rows t of the chunk, this CTA's 32 columns, zero past T
         for (int it = 0; it < NC; ++it) {
             const int s = it & 1, c = NC - 1 - it;
             bool go = !bs_aborted(ms);
@@ -1151,8 +1152,8 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
                 break;
             }
             unsigned char* tile = sm + B_DO + s * 8192;
-            for (int piece = lane; piece < kChunk * 8; piece += 32) {
-                const int row = piece >> 3, c8 = piece & 7;
+            for (int piece = lane; piece < kChunk * (kBsCols / 8); piece += 32) {
+                const int row = piece / (kBsCols / 8), c8 = piece % (kBsCols / 8);
                 const int64_t t = (int64_t)c * kChunk + row;
                 const bool in = t < p.T;
                 const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.dout.p) + (int64_t)b * p.dout.sb +
@@ -1165,12 +1166,12 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&ms.full_do[s]);
         }
-    } else {  // warps 0-3: thread = row dk of the gradient state, 64 columns
+    } else {  // warps 0-3: thread = row dk of the gradient state, this CTA's 32 columns
         const int dk = tid;
-        float S[64];
+        float S[kBsCols];
         const int64_t srow = ((int64_t)bh * kDk + dk) * kDv + dv0;
 #pragma unroll
-        for (int q4 = 0; q4 < 16; ++q4) {
+        for (int q4 = 0; q4 < kBsCols / 4; ++q4) {
             const float4 v = p.dhT ? *reinterpret_cast<const float4*>(p.dhT + srow + 4 * q4) : make_float4(0.f, 0.f, 0.f, 0.f);
             S[4 * q4] = v.x;
             S[4 * q4 + 1] = v.y;
@@ -1181,13 +1182,14 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
             const int s = it & 1, c = NC - 1 - it;
             if (ok) {  // tile s was last read by the MMAs of iteration it - 2, complete before iteration it - 1's
 #pragma unroll
-                for (int q8 = 0; q8 < 8; ++q8) store_bf16x8(sm + B_STILE + s * 16384, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
+                for (int q8 = 0; q8 < kBsCols / 8; ++q8)
+                    store_bf16x8(sm + B_STILE + s * 16384, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
                 fence_proxy_async_smem();
             }
             tc_fence_before();
             named_bar_arrive(kBsBar, kBsBarCount);
-            // dS_{c+1} (fp32) for the chunk kernels, while the MMAs run: the warp's 32 rows, 64 columns
-            store_rows_coalesced<64>(reinterpret_cast<float*>(sm + B_XPOSE) + warp * 32 * 68, S,
+            // dS_{c+1} (fp32) for the chunk kernels, while the MMAs run: the warp's 32 rows, this CTA's columns
+            store_rows_coalesced<kBsCols>(reinterpret_cast<float*>(sm + B_XPOSE) + warp * 32 * (kBsCols + 4), S,
                                      p.bws + ((int64_t)bh * NC + c) * kBwChunkFloats + kBwDSe +
                                          (int64_t)(32 * warp) * kDv + dv0,
                                      kDv, lane);
@@ -1196,8 +1198,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
             if (ok) {
                 tc_fence_after();
-                tmem_ld32(tmem_addr(tm, 32 * warp, 0), *reinterpret_cast<float(*)[32]>(S));
-                tmem_ld32(tmem_addr(tm, 32 * warp, 32), *reinterpret_cast<float(*)[32]>(S + 32));
+                tmem_ld32(tmem_addr(tm, 32 * warp, 0), S);
                 tmem_ld_wait();
                 tc_fence_before();
             }
@@ -1205,7 +1206,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
         }
         if (ok && p.dh0) {
 #pragma unroll
-            for (int q4 = 0; q4 < 16; ++q4)
+            for (int q4 = 0; q4 < kBsCols / 4; ++q4)
                 *reinterpret_cast<float4*>(p.dh0 + srow + 4 * q4) = make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
         }
     }
@@ -2293,7 +2294,7 @@ cudaError_t launch_bwd_scan_tc(const BwdParams& p, cudaStream_t stream) {
     static_assert(B_SMEM <= 227 * 1024, "shared memory budget");
     cudaError_t e = cudaFuncSetAttribute(gdn_bwd_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)B_SMEM);
     if (e != cudaSuccess) return e;
-    gdn_bwd_scan_tc<<<dim3((unsigned)(p.B * p.H), kDv / 64), kBsThreads, B_SMEM, stream>>>(p);
+    gdn_bwd_scan_tc<<<dim3((unsigned)(p.B * p.H), kDv / kBsCols), kBsThreads, B_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     return cudaSuccess;
