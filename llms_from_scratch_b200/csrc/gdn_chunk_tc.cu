@@ -141,10 +141,6 @@ __device__ __forceinline__ void store_split8(unsigned char* hi_tile, unsigned ch
     *reinterpret_cast<uint4*>(lo_tile + off) = lu;
 }
 
-// fp32 row of 32 values in a [rows][32] block whose 16-byte chunks are swizzled by row % 8.
-__device__ __forceinline__ uint32_t f32blk_offset(int row, int chunk4) {
-    return (uint32_t)row * 128u + (uint32_t)((chunk4 ^ (row & 7)) * 16);
-}
 
 // The backward tiles (u, w, Kd [64][128]; Aqk [64][64]) as the tensor-core prep writes them: chunk-major,
 // element (row, col) at ((col / 4) * 64 + row) * 4 + col % 4, so the prep's stores from TMEM (a lane per
@@ -707,7 +703,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
             unsigned char* blk = sm + btile[c0 >> 5];
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4)
-                *reinterpret_cast<float4*>(blk + f32blk_offset(dk, ((c0 & 31) >> 2) + q4)) =
+                *reinterpret_cast<float4*>(blk + ((((c0 & 31) >> 2) + q4) * 128 + dk) * 16) =  // chunk-major tile
                     make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
         }
     } else {
@@ -743,13 +739,17 @@ constexpr int kScanPrefetch = 4;           // chunks ahead that the producer pul
 constexpr int kScanMmaWarp = 6;
 constexpr uint32_t kScanBarS = 1;          // named barrier: epilogue (128) arrives with S_c stored, MMA warp waits
 constexpr uint32_t kScanBarCount = 160;
-constexpr uint32_t kScanTmemCols = 128;    // cols [0,32) state accumulator, [32,64) / [64,96) output accumulators
-constexpr uint32_t S_STAGE = 73728;        // M image 32K | Q image 16K | b slice 16K | o0 slice 8K
-constexpr uint32_t S_OFF_Q = 32768, S_OFF_B = 49152, S_OFF_O0 = 65536;
+constexpr int kScanSlices = kDv / kTcDvTile;  // state-column slices (CTAs) per head
+constexpr uint32_t kScanTmemCols = 64;     // cols [0,16) state accumulator, [16,32) / [32,48) output accumulators
+constexpr uint32_t S_STAGE = 61440;        // M image 32K | Q image 16K | b slice 8K | o0 slice 4K
+constexpr uint32_t S_OFF_Q = 32768, S_OFF_B = 49152, S_OFF_O0 = 57344;
+constexpr uint32_t kScanBBytes = 128 * kTcDvTile * 4, kScanO0Bytes = 64 * kTcDvTile * 4;  // a slice of b / of o0
+static_assert(S_STAGE % 1024 == 0 && S_OFF_O0 + kScanO0Bytes <= S_STAGE, "scan stage layout");
+static_assert(kScanTmemCols >= 3 * kTcDvTile, "scan TMEM columns");
 constexpr uint32_t S_STILE = 2 * S_STAGE;  // state operand, two tiles by chunk parity: bf16 [128 dk][64] swizzled
                                            // (32 columns used); chunk c's MMAs read tile c % 2
-constexpr uint32_t S_XPOSE = S_STILE + 2 * 16384;  // per state warp: fp32 [32 rows][36] staging of the S_c records
-constexpr uint32_t S_MISC = S_XPOSE + 4 * 32 * 36 * 4;
+constexpr uint32_t S_XPOSE = S_STILE + 2 * 16384;  // per state warp: fp32 [32 rows][kTcDvTile + 4] staging of S_c
+constexpr uint32_t S_MISC = S_XPOSE + 4 * 32 * (kTcDvTile + 4) * 4;
 constexpr uint32_t S_SMEM = S_MISC + 256 + 1024;
 
 struct ScanMisc {
@@ -767,18 +767,18 @@ __device__ __forceinline__ bool scan_aborted(const ScanMisc& ms) {
     return *reinterpret_cast<const volatile int*>(&ms.abort) != 0;
 }
 
-// o_c rows 16w..16w+15 of this CTA's 32 columns: o = Q'S (accumulator) + o0 (stage smem).
-__device__ __forceinline__ void scan_store_output(const ChunkParams& p, const unsigned char* st, const float (&o)[32],
+// o_c rows 16w..16w+15 of this CTA's columns: o = Q'S (accumulator) + o0 (stage smem).
+__device__ __forceinline__ void scan_store_output(const ChunkParams& p, const unsigned char* st, const float (&o)[kTcDvTile],
                                                   int64_t t0, int64_t t_lim, int warp, int lane, int b, int h,
                                                   int dv0) {
     if (lane >= 16) return;
     const int tok = 16 * warp + lane;
     const int64_t t = t0 + tok;
     if (t >= t_lim) return;
-    float ov[32];
+    float ov[kTcDvTile];
 #pragma unroll
-    for (int q4 = 0; q4 < 8; ++q4) {
-        const float4 oo = *reinterpret_cast<const float4*>(st + S_OFF_O0 + q4 * 1024 + tok * 16);  // chunk-major tile
+    for (int q4 = 0; q4 < kTcDvTile / 4; ++q4) {
+        const float4 oo = *reinterpret_cast<const float4*>(st + S_OFF_O0 + q4 * 1024 + tok * 16);  // chunk-major slice
         ov[4 * q4] = o[4 * q4] + oo.x;
         ov[4 * q4 + 1] = o[4 * q4 + 1] + oo.y;
         ov[4 * q4 + 2] = o[4 * q4 + 2] + oo.z;
@@ -787,7 +787,7 @@ __device__ __forceinline__ void scan_store_output(const ChunkParams& p, const un
     unsigned char* dst = reinterpret_cast<unsigned char*>(p.out) +
                          2 * ((int64_t)b * p.out_sb + t * p.out_st + (int64_t)h * p.out_sh + dv0);
 #pragma unroll
-    for (int q8 = 0; q8 < 4; ++q8) store_bf16x8(dst, 16 * q8, ov + 8 * q8);
+    for (int q8 = 0; q8 < kTcDvTile / 8; ++q8) store_bf16x8(dst, 16 * q8, ov + 8 * q8);
 }
 
 // The chunk-to-chunk chain S_{c+1} = M_c S_c + b_c runs through three parties each
@@ -809,16 +809,16 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     int bh, h, dvt;
     if (p.cu_seqlens) {
         const int x = blockIdx.x;
-        h = (x >> 2) % p.H;
-        dvt = x & 3;
-        bh = p.seq_order[x / (4 * p.H)] * p.H + h;
+        h = (x / kScanSlices) % p.H;
+        dvt = x % kScanSlices;
+        bh = p.seq_order[x / (kScanSlices * p.H)] * p.H + h;
     } else {
         bh = blockIdx.x;
         h = bh % p.H;
-        dvt = blockIdx.y & 3;
+        dvt = blockIdx.y % kScanSlices;
     }
     const bool summary = p.scan_mode == 1;
-    const bool transition = summary && blockIdx.y < 4;  // state starts from I, b ignored
+    const bool transition = summary && blockIdx.y < kScanSlices;  // state starts from I, b ignored
     const int dv0 = dvt * kTcDvTile;
     // chunk c of this sequence: record rec0 + c * rec_step, tokens tbase + 64 c .. (below t_lim)
     int b = bh / p.H, NC = p.NC;
@@ -900,15 +900,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             const bool mq = warp == 4;
             uint64_t* full = mq ? ms.full_mq : ms.full_bo;
             uint64_t* empty = mq ? ms.empty_mq : ms.empty_bo;
-            const uint32_t bytes = mq ? 32768 + 16384 : 16384 + 8192;
+            const uint32_t bytes = mq ? 32768 + 16384 : kScanBBytes + kScanO0Bytes;
             int issued = 0;
             for (int c = 0; c < NC; ++c) {
                 const int s = c & 1;
                 if (mq && c + kScanPrefetch < NC) {
                     const unsigned char* pre = record(c + kScanPrefetch);
                     bulk_prefetch_l2(pre + kTcM, 32768 + 16384);
-                    bulk_prefetch_l2(pre + kTcB + dvt * 16384, 16384);
-                    bulk_prefetch_l2(pre + kTcO0 + dvt * 8192, 8192);
+                    bulk_prefetch_l2(pre + kTcB + dvt * kScanBBytes, kScanBBytes);
+                    bulk_prefetch_l2(pre + kTcO0 + dvt * kScanO0Bytes, kScanO0Bytes);
                 }
                 if (scan_aborted(ms)) break;
                 if (c >= 2 && !mbar_wait(&empty[s], ((c >> 1) - 1) & 1, kWaitNs)) {
@@ -922,8 +922,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                     bulk_g2s(st, rec + kTcM, 32768, &full[s]);
                     bulk_g2s(st + S_OFF_Q, rec + kTcQ, 16384, &full[s]);
                 } else {
-                    bulk_g2s(st + S_OFF_B, rec + kTcB + dvt * 16384, 16384, &full[s]);
-                    bulk_g2s(st + S_OFF_O0, rec + kTcO0 + dvt * 8192, 8192, &full[s]);
+                    bulk_g2s(st + S_OFF_B, rec + kTcB + dvt * kScanBBytes, kScanBBytes, &full[s]);
+                    bulk_g2s(st + S_OFF_O0, rec + kTcO0 + dvt * kScanO0Bytes, kScanO0Bytes, &full[s]);
                 }
                 ++issued;
             }
@@ -972,12 +972,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: the warp loads or skips together
             if (ok) {
                 tc_fence_after();
-                float d[32];
-                tmem_ld32(tmem_addr(tm, 32 * warp, 0), d);
+                float d[kTcDvTile];
+                tmem_ld16(tmem_addr(tm, 32 * warp, 0), d);
                 tmem_ld_wait();
 #pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4) {
-                    float4 bb = *reinterpret_cast<const float4*>(st + S_OFF_B + f32blk_offset(dk, q4));
+                for (int q4 = 0; q4 < kTcDvTile / 4; ++q4) {  // b slice chunk-major: row dk, 16 bytes apart
+                    float4 bb = *reinterpret_cast<const float4*>(st + S_OFF_B + (q4 * 128 + dk) * 16);
                     if (transition) bb = make_float4(0.f, 0.f, 0.f, 0.f);
                     S[4 * q4] = d[4 * q4] + bb.x;
                     S[4 * q4 + 1] = d[4 * q4 + 1] + bb.y;
@@ -1000,8 +1000,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             ok = __all_sync(0xffffffffu, ok);
             if (ok) {
                 tc_fence_after();
-                float o[32];
-                tmem_ld32(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + s)), o);
+                float o[kTcDvTile];
+                tmem_ld16(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + s)), o);
                 tmem_ld_wait();
                 if (!summary && p.out)
                     scan_store_output(p, st, o, tbase + (int64_t)c * kChunk, t_lim, warp, lane, b, h, dv0);
@@ -2252,8 +2252,8 @@ cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream) {
 cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(gdn_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
     if (e != cudaSuccess) return e;
-    const dim3 grid = p.cu_seqlens ? dim3((unsigned)(p.N * p.H * (kDv / kTcDvTile)), 1)
-                                   : dim3((unsigned)(p.B * p.H), (p.scan_mode == 1 ? 2 : 1) * (kDv / kTcDvTile));
+    const dim3 grid = p.cu_seqlens ? dim3((unsigned)(p.N * p.H * kScanSlices), 1)
+                                   : dim3((unsigned)(p.B * p.H), (p.scan_mode == 1 ? 2 : 1) * kScanSlices);
     gdn_scan_tc<<<grid, kScanThreads, S_SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
