@@ -1040,13 +1040,13 @@ constexpr int kBsThreads = 224;
 constexpr int kBsMmaWarp = 6;
 constexpr uint32_t kBsBar = 2;              // named barrier: the state warps (128) arrive, the MMA warp waits
 constexpr uint32_t kBsBarCount = 160;
-constexpr int kBsCols = 32;                 // gradient-state columns per CTA (four CTAs per head)
-constexpr uint32_t kBsTmemCols = 32;        // the 128 x 32 fp32 accumulator
+constexpr int kBsCols = 16;                 // gradient-state columns per CTA (eight CTAs per head)
+constexpr uint32_t kBsTmemCols = 32;        // the 128 x 16 fp32 accumulator (the smallest allocation)
 constexpr uint32_t B_STAGE = 49152;         // M image 32 KiB | Q' image 16 KiB
 constexpr uint32_t B_OFF_Q = 32768;
-constexpr uint32_t B_DO = 2 * B_STAGE;      // do tiles: bf16 [64 t][64] swizzled (this CTA's 32 columns used), by parity
-constexpr uint32_t B_STILE = B_DO + 2 * 8192;  // dS operand tiles: bf16 [128 dk][64] swizzled (32 columns used), by parity
-constexpr uint32_t B_XPOSE = B_STILE + 2 * 16384;  // per state warp: fp32 [32 rows][36] staging of the dS records
+constexpr uint32_t B_DO = 2 * B_STAGE;      // do tiles: bf16 [64 t][64] swizzled (this CTA's columns used), by parity
+constexpr uint32_t B_STILE = B_DO + 2 * 8192;  // dS operand tiles: bf16 [128 dk][64] swizzled (this CTA's columns used)
+constexpr uint32_t B_XPOSE = B_STILE + 2 * 16384;  // per state warp: fp32 [32 rows][kBsCols + 4] staging of the dS records
 constexpr uint32_t B_MISC = B_XPOSE + 4 * 32 * (kBsCols + 4) * 4;
 constexpr uint32_t B_SMEM = B_MISC + 256 + 1024;
 
@@ -1142,7 +1142,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
             for (int it = (issued > 2 ? issued - 2 : 0); it < issued; ++it)
                 if (!mbar_wait(&ms.full_mq[it & 1], (it >> 1) & 1, kWaitNs)) ok = false;
         }
-    } else if (warp == 5) {  // do tiles: rows t of the chunk, this CTA's 32 columns, zero past T
+    } else if (warp == 5) {  // do tiles: rows t of the chunk, this CTA's columns, zero past T
         for (int it = 0; it < NC; ++it) {
             const int s = it & 1, c = NC - 1 - it;
             bool go = !bs_aborted(ms);
@@ -1166,7 +1166,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
             __syncwarp();
             if (lane == 0) mbar_arrive(&ms.full_do[s]);
         }
-    } else {  // warps 0-3: thread = row dk of the gradient state, this CTA's 32 columns
+    } else {  // warps 0-3: thread = row dk of the gradient state, this CTA's columns
         const int dk = tid;
         float S[kBsCols];
         const int64_t srow = ((int64_t)bh * kDk + dk) * kDv + dv0;
@@ -1198,7 +1198,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
             if (ok) {
                 tc_fence_after();
-                tmem_ld32(tmem_addr(tm, 32 * warp, 0), S);
+                tmem_ld16(tmem_addr(tm, 32 * warp, 0), S);
                 tmem_ld_wait();
                 tc_fence_before();
             }
