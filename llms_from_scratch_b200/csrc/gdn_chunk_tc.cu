@@ -739,18 +739,22 @@ constexpr int kScanPrefetch = 4;           // chunks ahead that the producer pul
 constexpr int kScanMmaWarp = 6;
 constexpr uint32_t kScanBarS = 1;          // named barrier: epilogue (128) arrives with S_c stored, MMA warp waits
 constexpr uint32_t kScanBarCount = 160;
-constexpr int kScanSlices = kDv / kTcDvTile;  // state-column slices (CTAs) per head
-constexpr uint32_t kScanTmemCols = 64;     // cols [0,16) state accumulator, [16,32) / [32,48) output accumulators
-constexpr uint32_t S_STAGE = 61440;        // M image 32K | Q image 16K | b slice 8K | o0 slice 4K
-constexpr uint32_t S_OFF_Q = 32768, S_OFF_B = 49152, S_OFF_O0 = 57344;
-constexpr uint32_t kScanBBytes = 128 * kTcDvTile * 4, kScanO0Bytes = 64 * kTcDvTile * 4;  // a slice of b / of o0
-static_assert(S_STAGE % 1024 == 0 && S_OFF_O0 + kScanO0Bytes <= S_STAGE, "scan stage layout");
-static_assert(kScanTmemCols >= 3 * kTcDvTile, "scan TMEM columns");
-constexpr uint32_t S_STILE = 2 * S_STAGE;  // state operand, two tiles by chunk parity: bf16 [128 dk][64] swizzled
-                                           // (32 columns used); chunk c's MMAs read tile c % 2
-constexpr uint32_t S_XPOSE = S_STILE + 2 * 16384;  // per state warp: fp32 [32 rows][kTcDvTile + 4] staging of S_c
-constexpr uint32_t S_MISC = S_XPOSE + 4 * 32 * (kTcDvTile + 4) * 4;
-constexpr uint32_t S_SMEM = S_MISC + 256 + 1024;
+// Shared-memory layout of a scan CTA that owns kW state columns (16 when the B*H*8 CTAs fit in one wave of
+// SMs, else 32): per stage the M image 32K | Q image 16K | the b slice | the o0 slice (both contiguous in the
+// chunk-major records), two stages, then the state operand tiles, the record staging and the barriers.
+template <int kW>
+struct ScanLayout {
+    static constexpr int kSlices = kDv / kW;                                   // CTAs per head
+    static constexpr uint32_t kTmemCols = kW == 16 ? 64 : 128;                 // state | two output accumulators
+    static constexpr uint32_t kBBytes = 128 * kW * 4, kO0Bytes = 64 * kW * 4;  // a slice of b / of o0
+    static constexpr uint32_t kOffQ = 32768, kOffB = 49152, kOffO0 = kOffB + kBBytes;
+    static constexpr uint32_t kStage = (kOffO0 + kO0Bytes + 1023) / 1024 * 1024;
+    static constexpr uint32_t kSTile = 2 * kStage;  // state operand, two tiles by chunk parity: bf16 [128 dk][64] swizzled
+    static constexpr uint32_t kXpose = kSTile + 2 * 16384;  // per state warp: fp32 [32 rows][kW + 4] staging of S_c
+    static constexpr uint32_t kMisc = kXpose + 4 * 32 * (kW + 4) * 4;
+    static constexpr uint32_t kSmem = kMisc + 256 + 1024;
+    static_assert(kTmemCols >= 3 * kW && kSmem <= 227 * 1024, "scan layout");
+};
 
 struct ScanMisc {
     uint64_t full_mq[2];   // M/Q images landed (tx)
@@ -768,17 +772,18 @@ __device__ __forceinline__ bool scan_aborted(const ScanMisc& ms) {
 }
 
 // o_c rows 16w..16w+15 of this CTA's columns: o = Q'S (accumulator) + o0 (stage smem).
-__device__ __forceinline__ void scan_store_output(const ChunkParams& p, const unsigned char* st, const float (&o)[kTcDvTile],
+template <int kW>
+__device__ __forceinline__ void scan_store_output(const ChunkParams& p, const unsigned char* st, const float (&o)[kW],
                                                   int64_t t0, int64_t t_lim, int warp, int lane, int b, int h,
                                                   int dv0) {
     if (lane >= 16) return;
     const int tok = 16 * warp + lane;
     const int64_t t = t0 + tok;
     if (t >= t_lim) return;
-    float ov[kTcDvTile];
+    float ov[kW];
 #pragma unroll
-    for (int q4 = 0; q4 < kTcDvTile / 4; ++q4) {
-        const float4 oo = *reinterpret_cast<const float4*>(st + S_OFF_O0 + q4 * 1024 + tok * 16);  // chunk-major slice
+    for (int q4 = 0; q4 < kW / 4; ++q4) {
+        const float4 oo = *reinterpret_cast<const float4*>(st + ScanLayout<kW>::kOffO0 + q4 * 1024 + tok * 16);  // chunk-major slice
         ov[4 * q4] = o[4 * q4] + oo.x;
         ov[4 * q4 + 1] = o[4 * q4 + 1] + oo.y;
         ov[4 * q4 + 2] = o[4 * q4 + 2] + oo.z;
@@ -787,7 +792,7 @@ __device__ __forceinline__ void scan_store_output(const ChunkParams& p, const un
     unsigned char* dst = reinterpret_cast<unsigned char*>(p.out) +
                          2 * ((int64_t)b * p.out_sb + t * p.out_st + (int64_t)h * p.out_sh + dv0);
 #pragma unroll
-    for (int q8 = 0; q8 < kTcDvTile / 8; ++q8) store_bf16x8(dst, 16 * q8, ov + 8 * q8);
+    for (int q8 = 0; q8 < kW / 8; ++q8) store_bf16x8(dst, 16 * q8, ov + 8 * q8);
 }
 
 // The chunk-to-chunk chain S_{c+1} = M_c S_c + b_c runs through three parties each
@@ -798,10 +803,12 @@ __device__ __forceinline__ void scan_store_output(const ChunkParams& p, const un
 // outputs, which overlap the next chunk's MMAs.  Every party takes every barrier
 // step of every chunk, also after a failed wait (then it skips the work), so the
 // named barrier can never be left short of arrivals.
+template <int kW>
 __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
+    using L = ScanLayout<kW>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    ScanMisc& ms = *reinterpret_cast<ScanMisc*>(sm + S_MISC);
+    ScanMisc& ms = *reinterpret_cast<ScanMisc*>(sm + L::kMisc);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // (sequence, head) -- also the state's [Dk, Dv] block -- and the 32-column slice of the state (and of b /
     // o0).  Packed sequences: a 1-D grid over (rank, head, slice), longest sequence first, so the long chains
@@ -809,17 +816,17 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     int bh, h, dvt;
     if (p.cu_seqlens) {
         const int x = blockIdx.x;
-        h = (x / kScanSlices) % p.H;
-        dvt = x % kScanSlices;
-        bh = p.seq_order[x / (kScanSlices * p.H)] * p.H + h;
+        h = (x / L::kSlices) % p.H;
+        dvt = x % L::kSlices;
+        bh = p.seq_order[x / (L::kSlices * p.H)] * p.H + h;
     } else {
         bh = blockIdx.x;
         h = bh % p.H;
-        dvt = blockIdx.y % kScanSlices;
+        dvt = blockIdx.y % L::kSlices;
     }
     const bool summary = p.scan_mode == 1;
-    const bool transition = summary && blockIdx.y < kScanSlices;  // state starts from I, b ignored
-    const int dv0 = dvt * kTcDvTile;
+    const bool transition = summary && blockIdx.y < L::kSlices;  // state starts from I, b ignored
+    const int dv0 = dvt * kW;
     // chunk c of this sequence: record rec0 + c * rec_step, tokens tbase + 64 c .. (below t_lim)
     int b = bh / p.H, NC = p.NC;
     int64_t rec0 = (int64_t)bh * p.NC, rec_step = 1, tbase = 0, t_lim = p.T;
@@ -849,7 +856,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
         fence_mbar_init();
     }
     if (warp == 0) {
-        tmem_alloc(&ms.tmem, kScanTmemCols);
+        tmem_alloc(&ms.tmem, L::kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -862,11 +869,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     if (warp == kScanMmaWarp) {
         // ---------------- MMA issue: the whole warp runs the loop, one elected lane issues
         const uint32_t leader = elect_one();
-        const uint32_t idS = make_idesc_f16(128, kTcDvTile, false, true, true);
-        const uint32_t idO = make_idesc_f16(64, kTcDvTile, false, true, true);
+        const uint32_t idS = make_idesc_f16(128, kW, false, true, true);
+        const uint32_t idO = make_idesc_f16(64, kW, false, true, true);
         const uint64_t dM = make_sdesc(sbase, 16, 1024, kSwizzle128B);
-        const uint64_t dQ = make_sdesc(sbase + S_OFF_Q, 16, 1024, kSwizzle128B);
-        const uint64_t dS = make_sdesc(sbase + S_STILE, 16384, 1024, kSwizzle128B);
+        const uint64_t dQ = make_sdesc(sbase + L::kOffQ, 16, 1024, kSwizzle128B);
+        const uint64_t dS = make_sdesc(sbase + L::kSTile, 16384, 1024, kSwizzle128B);
         for (int c = 0; c < NC; ++c) {
             const int s = c & 1;
             named_bar_sync(kScanBarS, kScanBarCount);  // S_c is in operand tile s
@@ -878,7 +885,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                 continue;
             }
             tc_fence_after();
-            const uint64_t so = (uint64_t)((s * S_STAGE) >> 4);
+            const uint64_t so = (uint64_t)((s * L::kStage) >> 4);
             // state first: it is the only product on the sequential path
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
@@ -887,7 +894,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             mma_commit_if(leader, &ms.mma_s);
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
-                mma_f16_if(leader, tm + kTcDvTile * (1 + s),
+                mma_f16_if(leader, tm + kW * (1 + s),
                            dQ + so + (uint64_t)((((ks >> 2) * 8192) + (ks & 3) * 32) >> 4),
                            dS + (uint64_t)((s * 16384 + ks * 2048) >> 4), idO, ks > 0);
             mma_commit_if(leader, &ms.mma_o[s]);
@@ -900,15 +907,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             const bool mq = warp == 4;
             uint64_t* full = mq ? ms.full_mq : ms.full_bo;
             uint64_t* empty = mq ? ms.empty_mq : ms.empty_bo;
-            const uint32_t bytes = mq ? 32768 + 16384 : kScanBBytes + kScanO0Bytes;
+            const uint32_t bytes = mq ? 32768 + 16384 : L::kBBytes + L::kO0Bytes;
             int issued = 0;
             for (int c = 0; c < NC; ++c) {
                 const int s = c & 1;
                 if (mq && c + kScanPrefetch < NC) {
                     const unsigned char* pre = record(c + kScanPrefetch);
                     bulk_prefetch_l2(pre + kTcM, 32768 + 16384);
-                    bulk_prefetch_l2(pre + kTcB + dvt * kScanBBytes, kScanBBytes);
-                    bulk_prefetch_l2(pre + kTcO0 + dvt * kScanO0Bytes, kScanO0Bytes);
+                    bulk_prefetch_l2(pre + kTcB + dvt * L::kBBytes, L::kBBytes);
+                    bulk_prefetch_l2(pre + kTcO0 + dvt * L::kO0Bytes, L::kO0Bytes);
                 }
                 if (scan_aborted(ms)) break;
                 if (c >= 2 && !mbar_wait(&empty[s], ((c >> 1) - 1) & 1, kWaitNs)) {
@@ -916,14 +923,14 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                     break;
                 }
                 const unsigned char* rec = record(c);
-                unsigned char* st = sm + s * S_STAGE;
+                unsigned char* st = sm + s * L::kStage;
                 mbar_arrive_expect_tx(&full[s], bytes);
                 if (mq) {
                     bulk_g2s(st, rec + kTcM, 32768, &full[s]);
-                    bulk_g2s(st + S_OFF_Q, rec + kTcQ, 16384, &full[s]);
+                    bulk_g2s(st + L::kOffQ, rec + kTcQ, 16384, &full[s]);
                 } else {
-                    bulk_g2s(st + S_OFF_B, rec + kTcB + dvt * kScanBBytes, kScanBBytes, &full[s]);
-                    bulk_g2s(st + S_OFF_O0, rec + kTcO0 + dvt * kScanO0Bytes, kScanO0Bytes, &full[s]);
+                    bulk_g2s(st + L::kOffB, rec + kTcB + dvt * L::kBBytes, L::kBBytes, &full[s]);
+                    bulk_g2s(st + L::kOffO0, rec + kTcO0 + dvt * L::kO0Bytes, L::kO0Bytes, &full[s]);
                 }
                 ++issued;
             }
@@ -934,10 +941,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     } else {
         // ---------------- thread = state row dk (TMEM lane); warp w also owns output rows 16w..16w+15
         const int dk = tid;
-        float S[kTcDvTile];
+        float S[kW];
         const int64_t srow = ((int64_t)bh * kDk + dk) * kDv + dv0;
 #pragma unroll
-        for (int q4 = 0; q4 < kTcDvTile / 4; ++q4) {
+        for (int q4 = 0; q4 < kW / 4; ++q4) {
             float4 v = (p.h0 && !summary) ? *reinterpret_cast<const float4*>(p.h0 + srow + 4 * q4)
                                           : make_float4(0.f, 0.f, 0.f, 0.f);
             if (transition) {  // identity columns dv0 .. dv0+31
@@ -951,18 +958,18 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             S[4 * q4 + 2] = v.z;
             S[4 * q4 + 3] = v.w;
         }
-        unsigned char* stile = sm + S_STILE;
+        unsigned char* stile = sm + L::kSTile;
 #pragma unroll
-        for (int q8 = 0; q8 < kTcDvTile / 8; ++q8) store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
+        for (int q8 = 0; q8 < kW / 8; ++q8) store_bf16x8(stile, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
         fence_proxy_async_smem();
         if (NC > 0) named_bar_arrive(kScanBarS, kScanBarCount);  // S_0 for chunk 0 (a sequence may be empty)
 
         for (int c = 0; c < NC; ++c) {
             const int s = c & 1;
-            const unsigned char* st = sm + s * S_STAGE;
+            const unsigned char* st = sm + s * L::kStage;
             if (p.states)  // S_c (fp32) for the backward: the warp's 32 rows, this CTA's 32 columns
-                store_rows_coalesced<kTcDvTile>(
-                    reinterpret_cast<float*>(sm + S_XPOSE) + warp * 32 * (kTcDvTile + 4), S,
+                store_rows_coalesced<kW>(
+                    reinterpret_cast<float*>(sm + L::kXpose) + warp * 32 * (kW + 4), S,
                     p.states + (rec0 + (int64_t)c * rec_step) * p.states_stride + (int64_t)(32 * warp) * kDv + dv0,
                     kDv, lane);
             // ---- S_{c+1} = M_c S_c + b_c (the sequential path)
@@ -972,12 +979,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: the warp loads or skips together
             if (ok) {
                 tc_fence_after();
-                float d[kTcDvTile];
-                tmem_ld16(tmem_addr(tm, 32 * warp, 0), d);
+                float d[kW];
+                if constexpr (kW == 16) tmem_ld16(tmem_addr(tm, 32 * warp, 0), d);
+                else tmem_ld32(tmem_addr(tm, 32 * warp, 0), d);
                 tmem_ld_wait();
 #pragma unroll
-                for (int q4 = 0; q4 < kTcDvTile / 4; ++q4) {  // b slice chunk-major: row dk, 16 bytes apart
-                    float4 bb = *reinterpret_cast<const float4*>(st + S_OFF_B + (q4 * 128 + dk) * 16);
+                for (int q4 = 0; q4 < kW / 4; ++q4) {  // b slice chunk-major: row dk, 16 bytes apart
+                    float4 bb = *reinterpret_cast<const float4*>(st + L::kOffB + (q4 * 128 + dk) * 16);
                     if (transition) bb = make_float4(0.f, 0.f, 0.f, 0.f);
                     S[4 * q4] = d[4 * q4] + bb.x;
                     S[4 * q4 + 1] = d[4 * q4 + 1] + bb.y;
@@ -988,7 +996,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             if (c + 1 < NC) {
                 if (ok) {  // tile (c+1) % 2 was last read by chunk c-1's MMAs, complete before chunk c's state product
 #pragma unroll
-                    for (int q8 = 0; q8 < kTcDvTile / 8; ++q8)
+                    for (int q8 = 0; q8 < kW / 8; ++q8)
                         store_bf16x8(stile + (s ^ 1) * 16384, sw128_offset(dk, 8 * q8, 128), S + 8 * q8);
                     fence_proxy_async_smem();
                 }
@@ -1000,11 +1008,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
             ok = __all_sync(0xffffffffu, ok);
             if (ok) {
                 tc_fence_after();
-                float o[kTcDvTile];
-                tmem_ld16(tmem_addr(tm, 32 * warp, kTcDvTile * (1 + s)), o);
+                float o[kW];
+                if constexpr (kW == 16) tmem_ld16(tmem_addr(tm, 32 * warp, kW * (1 + s)), o);
+                else tmem_ld32(tmem_addr(tm, 32 * warp, kW * (1 + s)), o);
                 tmem_ld_wait();
                 if (!summary && p.out)
-                    scan_store_output(p, st, o, tbase + (int64_t)c * kChunk, t_lim, warp, lane, b, h, dv0);
+                    scan_store_output<kW>(p, st, o, tbase + (int64_t)c * kChunk, t_lim, warp, lane, b, h, dv0);
                 tc_fence_before();
             }
             if (!ok) ms.abort = 1;
@@ -1013,7 +1022,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
         float* dst = summary ? (transition ? p.hT : p.hT2) : p.hT;
         if (ok && dst) {
 #pragma unroll
-            for (int q4 = 0; q4 < kTcDvTile / 4; ++q4)
+            for (int q4 = 0; q4 < kW / 4; ++q4)
                 *reinterpret_cast<float4*>(dst + srow + 4 * q4) =
                     make_float4(S[4 * q4], S[4 * q4 + 1], S[4 * q4 + 2], S[4 * q4 + 3]);
         }
@@ -1024,7 +1033,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tm, kScanTmemCols);
+    if (warp == 0) tmem_dealloc(tm, L::kTmemCols);
 }
 
 // ============================================================================ reverse scan (backward)
@@ -2239,7 +2248,7 @@ cudaError_t launch_varlen_tables(const ChunkParams& p, cudaStream_t stream) {
 }
 
 cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream) {
-    static_assert(P_SMEM <= 227 * 1024 && S_SMEM <= 227 * 1024, "shared memory budget");
+    static_assert(P_SMEM <= 227 * 1024, "shared memory budget");
     cudaError_t e = cudaFuncSetAttribute(gdn_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM);
     if (e != cudaSuccess) return e;
     const int64_t nchunks = p.cu_seqlens ? (int64_t)p.max_chunks * p.H : (int64_t)p.B * p.H * p.NC;
@@ -2249,15 +2258,34 @@ cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream) {
     return cudaSuccess;
 }
 
-cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
-    cudaError_t e = cudaFuncSetAttribute(gdn_scan_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM);
+namespace {
+template <int kW>
+cudaError_t launch_scan_w(const ChunkParams& p, cudaStream_t stream) {
+    using L = ScanLayout<kW>;
+    cudaError_t e = cudaFuncSetAttribute(gdn_scan_tc<kW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmem);
     if (e != cudaSuccess) return e;
-    const dim3 grid = p.cu_seqlens ? dim3((unsigned)(p.N * p.H * kScanSlices), 1)
-                                   : dim3((unsigned)(p.B * p.H), (p.scan_mode == 1 ? 2 : 1) * kScanSlices);
-    gdn_scan_tc<<<grid, kScanThreads, S_SMEM, stream>>>(p);
+    const dim3 grid = p.cu_seqlens ? dim3((unsigned)(p.N * p.H * L::kSlices), 1)
+                                   : dim3((unsigned)(p.B * p.H), (p.scan_mode == 1 ? 2 : 1) * L::kSlices);
+    gdn_scan_tc<kW><<<grid, kScanThreads, L::kSmem, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     return cudaSuccess;
+}
+}  // namespace
+
+// The scan is a chain of dependent chunk steps per CTA: 16-column slices shorten each step, but double the
+// CTAs; they are used while all of them fit in one wave (one CTA per SM), 32-column slices otherwise.
+cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
+    static int nsm[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    if (!nsm[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        nsm[dev] = n > 0 ? n : 1;
+    }
+    const int64_t rows = p.cu_seqlens ? (int64_t)p.N * p.H : (int64_t)p.B * p.H * (p.scan_mode == 1 ? 2 : 1);
+    return rows * ScanLayout<16>::kSlices <= nsm[dev] ? launch_scan_w<16>(p, stream) : launch_scan_w<32>(p, stream);
 }
 
 cudaError_t launch_bwd_states_tc(const BwdParams& p, cudaStream_t stream) {

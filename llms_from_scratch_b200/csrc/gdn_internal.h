@@ -25,7 +25,6 @@ constexpr int64_t kTcQ = 32768;         // Q'_c = q e^gc Dk^-1/2 - Aqk w, bf16 K
 constexpr int64_t kTcB = 49152;         // b_c = kd^T u, fp32 [4 column tiles][8 chunks][128 rows][4]    64 KiB
 constexpr int64_t kTcO0 = 114688;       // o0_c = Aqk u, fp32 [4 column tiles][8 chunks][64 rows][4]     32 KiB
 constexpr int64_t kTcChunkBytes = 147456;
-constexpr int kTcDvTile = 16;           // state columns per scan CTA (a contiguous slice of b and of o0)
 
 struct ChunkParams {
     View4 q, k, v;
@@ -41,9 +40,9 @@ struct ChunkParams {
     int l2norm;
     unsigned int* err;  // device error word (bounded waits that gave up set bits here)
     // Tensor-core scan mode: 0 = outputs + final state; 1 = shard summary (no outputs):
-    // the first kDv / kTcDvTile column slices of grid.y write the transition prod_c M_c to hT
-    // (state started from I, b ignored), the next as many the local final state (state started
-    // from 0) to hT2.
+    // the first half of grid.y's column slices write the transition prod_c M_c to hT (state
+    // started from I, b ignored), the second half the local final state (state started from 0)
+    // to hT2.
     int scan_mode;
     float* hT2;
     // Packed variable-length batch (tensor-core path; B == 1): sequence n is tokens
