@@ -17,10 +17,10 @@
 // Launches: the forward's CUDA-core prep (u, w, Qg, Kd, Aqk, e^gc_last per chunk) and
 // scan (recording S_c), then gdn_bwd_scan (one CTA per (b, h, 16 state columns), chunks
 // in reverse), then gdn_bwd_states, gdn_bwd_wy and gdn_bwd_grads (one CTA per chunk each,
-// all chunks in parallel).  With bf16 q/k/v and d_out the forward recompute, the reverse
-// scan and the state products run on the tensor cores instead (gdn_chunk_tc.cu): the
-// tensor-core prep writes the u, w, Kd and Aqk tiles beside its own records, its scan
-// records S_c, and gdn_bwd_wy / gdn_bwd_grads follow as here.
+// all chunks in parallel).  With bf16 q/k/v and d_out every step runs on the tensor cores
+// instead (gdn_chunk_tc.cu: the tensor-core prep also writes the u, w, Kd and Aqk tiles, its
+// scan records S_c, then gdn_bwd_scan_tc, gdn_bwd_states_tc, gdn_bwd_wy_tc and
+// gdn_bwd_grads_tc); the kernels in this file serve fp32 inputs.
 #include "gdn_bwd.cuh"
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
@@ -337,48 +337,27 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
         cp_async16_rec(&s.Xv[i][d4], bw + kBwVn + i * kDv + d4);
     }
     cp_async_commit_rec();
-    const bool bf16 = p.tc_records != nullptr;  // bf16 q/k/v/d_out with 16-byte aligned rows
     if (tid == 0) {  // the back substitution's right-hand sides (dv_new, dw) into L2 meanwhile
         prefetch_l2(bw + kBwDVn, kChunk * kDv * 4);
         prefetch_l2(bw + kBwDW, kChunk * kDk * 4);
     }
     const int ty = tid >> 4, tx = tid & 15;
     const int cols[2] = {4 * tx, 64 + 4 * tx};
-    uint2 vraw[kRt][2];  // bf16 mode: this thread's v entries for the dv phase, requested now
-    if (bf16) {
-#pragma unroll
-        for (int r = 0; r < kRt; ++r) {
-            const int64_t t = t0 + ty + kRg * r;
-#pragma unroll
-            for (int hlf = 0; hlf < 2; ++hlf)
-                vraw[r][hlf] = t < p.T ? *reinterpret_cast<const uint2*>(
-                                             reinterpret_cast<const __nv_bfloat16*>(p.v.p) + (int64_t)b * p.v.sb +
-                                             t * p.v.st + (int64_t)h * p.v.sh + cols[hlf])
-                                       : make_uint2(0u, 0u);
-        }
-    }
     for (int i = warp; i < kChunk; i += kWide / 32) row_to_smem(p.dout, b, t0 + i, p.T, h, lane, &s.Xk[i][0]);
     {  // k rows: a warp's 4 rows loaded together, then normalised
         constexpr int kR = kChunk / (kWide / 32);
         float x[kR][4], r;
 #pragma unroll
-        for (int rr = 0; rr < kR; ++rr) {
-            if (bf16) bwd::row4_bf16(p.k, b, t0 + warp + (kWide / 32) * rr, p.T, h, lane, x[rr]);
-            else qk_load(p.k, b, t0 + warp + (kWide / 32) * rr, p.T, h, lane, x[rr]);
-        }
+        for (int rr = 0; rr < kR; ++rr) qk_load(p.k, b, t0 + warp + (kWide / 32) * rr, p.T, h, lane, x[rr]);
 #pragma unroll
         for (int rr = 0; rr < kR; ++rr) {
             const int i = warp + (kWide / 32) * rr;
             qk_norm(p.k, t0 + i, p.T, p.l2norm, x[rr], r);
-            if (bf16) {
-                st4(&s.K[i][4 * lane], make_float4(x[rr][0], x[rr][1], x[rr][2], x[rr][3]));
-            } else {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) s.K[i][lane + 32 * e] = x[rr][e];
-            }
+            for (int e = 0; e < 4; ++e) s.K[i][lane + 32 * e] = x[rr][e];
         }
     }
-    chunk_gates(p, b, h, t0, s.gc, s.beta, s.egc, s.ekd, bf16);  // ends with a barrier
+    chunk_gates(p, b, h, t0, s.gc, s.beta, s.egc, s.ekd);  // ends with a barrier
 
     {  // L_ij = -(beta_i k_i.k_j) e^(gc_i - gc_j), i > j, stored transposed
         float kk[kRt][4];
@@ -473,11 +452,7 @@ __global__ void __launch_bounds__(kWide) gdn_bwd_wy(BwdParams p) {
                 const int cc = cols[hlf];
                 const float4 xv = ld4(&s.Xv[i][cc]), xk = ld4(&s.Xk[i][cc]), kv = ld4(&s.K[i][cc]);
                 const float xva[4] = {xv.x, xv.y, xv.z, xv.w};
-                if (bf16) {
-                    const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vraw[r][hlf].x));
-                    const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vraw[r][hlf].y));
-                    sv += v01.x * xva[0] + v01.y * xva[1] + v23.x * xva[2] + v23.y * xva[3];
-                } else {
+                {
                     const int64_t vb = (int64_t)b * p.v.sb + t * p.v.st + (int64_t)h * p.v.sh + cc;
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
