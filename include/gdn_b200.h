@@ -50,7 +50,9 @@ typedef enum {
     GDN_ERR_UNSUPPORTED = 2,      /* valid request this build cannot run (Python: RuntimeError)    */
     GDN_ERR_WORKSPACE = 3,        /* workspace missing, too small or misaligned                    */
     GDN_ERR_CUDA = 4,             /* a CUDA runtime call or kernel launch failed                   */
-    GDN_ERR_DEVICE = 5            /* the current device is not an sm_100 GPU                       */
+    GDN_ERR_DEVICE = 5,           /* the current device is not an sm_100 GPU                       */
+    GDN_ERR_KERNEL = 6            /* a kernel reported a failure in the device error word; the
+                                     outputs of the call that set it are not valid                  */
 } gdn_status;
 
 typedef enum { GDN_F32 = 0, GDN_BF16 = 1, GDN_F16 = 2 } gdn_dtype;
@@ -279,9 +281,41 @@ GDN_API void gdn_set_phase_events(void* const* events, int n);
 /* Sticky error bits of the current device.  A kernel whose bounded wait on an
  * internal barrier gives up (a bug, never expected) sets a bit here and exits
  * cleanly instead of hanging: 1 = chunk prep, 2 = chunk scan.  8 = packed
- * sequence offsets that were not a valid cu_seqlens.  Synchronous;
- * `clear` != 0 resets the word. */
+ * sequence offsets that were not a valid cu_seqlens.  16 = the wait of
+ * gdn_selftest_bounded_wait.  The outputs of a call that set a bit are not
+ * valid.  Synchronous (it copies the word from the device); `clear` != 0
+ * resets the word and its host mirror.
+ *
+ * The library caches the device addresses of this word (and of the fixed
+ * scratch of gdn_chunk_gated_delta_rule_noalloc) per device ordinal for the
+ * life of the process: resetting a device (cudaDeviceReset, or a primary
+ * context reset) after the first call on it is not supported. */
 GDN_API unsigned int gdn_device_error(int clear);
+
+/* Mirrors the current device's error bits into `host_word`, 4 bytes of
+ * page-locked host memory mapped into the device (cudaHostAlloc, or
+ * cudaHostRegister with cudaHostRegisterMapped) that the caller owns and keeps
+ * alive: a kernel that sets a bit also stores it there, so a caller can poll
+ * for failures with gdn_device_error_pending() without synchronising the
+ * device.  Resets the word to 0.  NULL stops mirroring.  Synchronous; call it
+ * outside stream capture.  No counterpart in the reference (its torch ops
+ * raise synchronously). */
+GDN_API int gdn_set_error_mirror(unsigned int* host_word);
+
+/* The current device's mirrored error bits (0 without a mirror).  Reads host
+ * memory only: no CUDA call, no synchronisation.  Reflects the kernels that
+ * have finished; a call that failed on the device shows up here once its
+ * kernels have run, so a caller checks it before its next call (and
+ * gdn_device_error(1) then returns and clears the bits). */
+GDN_API unsigned int gdn_device_error_pending(void);
+
+/* Test hook: launches one kernel on `stream` whose bounded wait on a barrier
+ * that nothing arms runs out after timeout_ns (1e3 .. 1e8 ns); it then sets bit
+ * 16 of the error word (and its mirror) and returns, exactly as a chunk kernel
+ * whose wait gave up would.  Lets a caller check that a timed-out wait
+ * surfaces as an error and leaves the context usable.  No counterpart in the
+ * reference. */
+GDN_API int gdn_selftest_bounded_wait(uint64_t timeout_ns, void* stream);
 
 /* Message for the most recent failure on this host thread ("" if none). */
 GDN_API const char* gdn_last_error(void);

@@ -19,6 +19,7 @@ GDN_ERR_UNSUPPORTED = 2
 GDN_ERR_WORKSPACE = 3
 GDN_ERR_CUDA = 4
 GDN_ERR_DEVICE = 5
+GDN_ERR_KERNEL = 6
 
 GDN_F32, GDN_BF16, GDN_F16 = 0, 1, 2
 GDN_NOALLOC_SCRATCH_BYTES = 64 << 20  # include/gdn_b200.h
@@ -67,6 +68,9 @@ SIGNATURES = {
     "gdn_launch_count": (ctypes.c_uint64, []),
     "gdn_set_phase_events": (None, [ctypes.POINTER(c_void_p), c_int]),
     "gdn_device_error": (ctypes.c_uint, [c_int]),
+    "gdn_set_error_mirror": (c_int, [c_void_p]),
+    "gdn_device_error_pending": (ctypes.c_uint, []),
+    "gdn_selftest_bounded_wait": (c_int, [ctypes.c_uint64, c_void_p]),
     "gdn_last_error": (c_char_p, []),
     "gdn_status_name": (c_char_p, [c_int]),
     "gdn_abi_version": (c_int, []),

@@ -8,7 +8,9 @@
 // GDN_ERR_INVALID_ARGUMENT / GDN_ERR_UNSUPPORTED with a message.
 #include <atomic>
 #include <cstdarg>
+#include <cstddef>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "gdn_internal.h"
@@ -18,12 +20,16 @@ namespace {
 thread_local std::string g_last_error;
 
 // Sticky device error word: bounded waits inside the kernels that give up OR a
-// bit in here (gdn_internal.h) instead of hanging or trapping.
-__device__ unsigned int g_device_error;
+// bit in here (gdn_internal.h) instead of hanging or trapping; with a host
+// mirror registered (gdn_set_error_mirror) they also set it in host memory.
+__device__ gdn::DeviceErrorWord g_device_error;
+std::mutex g_err_mu;
 void* g_device_error_addr[64];
+unsigned int* g_error_mirror[64];  // host address of each device's mirror word, or null
 
 unsigned int* device_error_word(int dev) {
     if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_err_mu);
     if (!g_device_error_addr[dev]) {
         void* ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
@@ -551,11 +557,73 @@ unsigned int gdn_device_error(int clear) {
     if (!w) return 0;
     unsigned int v = 0;
     if (cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
+    unsigned int* mirror = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_err_mu);
+        mirror = g_error_mirror[dev];
+    }
+    if (mirror) v |= *reinterpret_cast<volatile unsigned int*>(mirror);
     if (clear && v) {
         const unsigned int zero = 0;
         cudaMemcpy(w, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+        if (mirror) *reinterpret_cast<volatile unsigned int*>(mirror) = 0;
     }
     return v;
+}
+
+int gdn_set_error_mirror(unsigned int* host_word) {
+    g_last_error.clear();
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(GDN_ERR_DEVICE, "device ordinal %d out of range", dev);
+    unsigned int* w = device_error_word(dev);
+    if (!w) return fail(GDN_ERR_CUDA, "device error word not found");
+    unsigned int* dev_alias = nullptr;
+    if (host_word) {
+        if (reinterpret_cast<uintptr_t>(host_word) & 3)
+            return fail(GDN_ERR_INVALID_ARGUMENT, "host_word must be 4-byte aligned");
+        e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev_alias), host_word, 0);
+        if (e != cudaSuccess || !dev_alias) {
+            cudaGetLastError();  // a failed query leaves a (non-sticky) error behind: clear it
+            return fail(GDN_ERR_INVALID_ARGUMENT,
+                        "host_word must be page-locked host memory mapped into device %d (cudaHostAlloc, or "
+                        "cudaHostRegister with cudaHostRegisterMapped): %s", dev, cudaGetErrorString(e));
+        }
+        *reinterpret_cast<volatile unsigned int*>(host_word) = 0;
+    }
+    unsigned char* field = reinterpret_cast<unsigned char*>(w) + offsetof(gdn::DeviceErrorWord, host_mirror);
+    e = cudaMemcpy(field, &dev_alias, sizeof(dev_alias), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "error mirror registration");
+    std::lock_guard<std::mutex> lock(g_err_mu);
+    g_error_mirror[dev] = host_word;
+    return GDN_OK;
+}
+
+unsigned int gdn_device_error_pending(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    unsigned int* mirror;
+    {
+        std::lock_guard<std::mutex> lock(g_err_mu);
+        mirror = g_error_mirror[dev];
+    }
+    return mirror ? *reinterpret_cast<volatile unsigned int*>(mirror) : 0u;
+}
+
+int gdn_selftest_bounded_wait(uint64_t timeout_ns, void* stream) {
+    g_last_error.clear();
+    int rc = check_device();
+    if (rc) return rc;
+    if (timeout_ns < 1000ull || timeout_ns > 100000000ull)
+        return fail(GDN_ERR_INVALID_ARGUMENT, "timeout_ns must be in [1e3, 1e8], got %llu",
+                    (unsigned long long)timeout_ns);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    unsigned int* w = device_error_word(dev);
+    if (!w) return fail(GDN_ERR_CUDA, "device error word not found");
+    cudaError_t e = gdn::launch_selftest_wait(w, timeout_ns, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? GDN_OK : cuda_fail(e, "bounded-wait self-test launch");
 }
 
 const char* gdn_last_error(void) { return g_last_error.c_str(); }
@@ -568,6 +636,7 @@ const char* gdn_status_name(int status) {
         case GDN_ERR_WORKSPACE: return "GDN_ERR_WORKSPACE";
         case GDN_ERR_CUDA: return "GDN_ERR_CUDA";
         case GDN_ERR_DEVICE: return "GDN_ERR_DEVICE";
+        case GDN_ERR_KERNEL: return "GDN_ERR_KERNEL";
         default: return "GDN_UNKNOWN_STATUS";
     }
 }

@@ -59,9 +59,7 @@ using namespace tc;
 
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s; a healthy wait here takes microseconds
 
-__device__ __forceinline__ void report(unsigned int* err, unsigned int bit) {
-    if (err) atomicOr(err, bit);
-}
+__device__ __forceinline__ void report(unsigned int* err, unsigned int bit) { report_device_error(err, bit); }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -2239,6 +2237,29 @@ __global__ void __launch_bounds__(256) gdn_varlen_tables(ChunkParams p, int* chu
 }
 
 }  // namespace
+
+namespace {
+// One bounded wait that must run out: an mbarrier nobody arrives on, waited on with the same
+// mbar_wait the chunk kernels use.  When the limit passes the kernel reports kErrWaitSelftest
+// and returns, as a chunk kernel whose wait gave up would.
+__global__ void __launch_bounds__(32) gdn_selftest_wait(unsigned int* err, uint64_t timeout_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    const bool ok = mbar_wait(&bar, 0, timeout_ns);
+    if (!ok && threadIdx.x == 0) report(err, kErrWaitSelftest);
+}
+}  // namespace
+
+cudaError_t launch_selftest_wait(unsigned int* err, uint64_t timeout_ns, cudaStream_t stream) {
+    gdn_selftest_wait<<<1, 32, 0, stream>>>(err, timeout_ns);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) note_launch();
+    return e;
+}
 
 cudaError_t launch_varlen_tables(const ChunkParams& p, cudaStream_t stream) {
     gdn_varlen_tables<<<1, 256, 0, stream>>>(p, const_cast<int*>(p.chunk_base), const_cast<int*>(p.chunk_seq));

@@ -26,6 +26,29 @@ struct View3 {
     int dtype;
 };
 
+// The per-device error word the kernels report into.  Kernels receive a pointer
+// to `bits`; `host_mirror` is the device address of a page-locked host word the
+// host registered (gdn_set_error_mirror) or null.  A kernel that gives up sets
+// its bit in both, so the host can see the failure without synchronising.
+struct DeviceErrorWord {
+    unsigned int bits;
+    unsigned int reserved;
+    unsigned int* host_mirror;
+};
+
+__device__ __forceinline__ void report_device_error(unsigned int* err, unsigned int bit) {
+    if (!err) return;
+    atomicOr(err, bit);
+    unsigned int* m = reinterpret_cast<const DeviceErrorWord*>(err)->host_mirror;
+    if (m) {
+        // plain stores over the bus (no system-scope atomics needed): concurrent reporters may
+        // overwrite each other's bit, but the word never returns to zero
+        volatile unsigned int* vm = m;
+        *vm = *vm | bit;
+        __threadfence_system();
+    }
+}
+
 __device__ __forceinline__ float load_elem(const void* base, int64_t idx, int dtype) {
     if (dtype == GDN_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
     if (dtype == GDN_F16) return __half2float(reinterpret_cast<const __half*>(base)[idx]);

@@ -155,7 +155,7 @@ void note_launch();
 cudaError_t phase_event(int index, cudaStream_t stream);
 
 // Error bits a kernel ORs into the device error word.
-enum : unsigned int { kErrTimeoutPrep = 1u, kErrTimeoutScan = 2u, kErrBadSeqlens = 8u };
+enum : unsigned int { kErrTimeoutPrep = 1u, kErrTimeoutScan = 2u, kErrBadSeqlens = 8u, kErrWaitSelftest = 16u };
 
 cudaError_t launch_chunk_simt(const ChunkParams& p, cudaStream_t stream);
 cudaError_t launch_chunk_tc(const ChunkParams& p, cudaStream_t stream);
@@ -167,5 +167,7 @@ cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream);
 // leave zero chunks, so nothing runs.
 cudaError_t launch_varlen_tables(const ChunkParams& p, cudaStream_t stream);
 cudaError_t launch_recurrent(const RecurrentParams& p, cudaStream_t stream);
+// One kernel whose bounded barrier wait runs out after timeout_ns and reports kErrWaitSelftest.
+cudaError_t launch_selftest_wait(unsigned int* err, uint64_t timeout_ns, cudaStream_t stream);
 
 }  // namespace gdn

@@ -77,6 +77,52 @@ def _state_in(initial_state: Optional[torch.Tensor], B, H, Dk, Dv, device) -> Op
     return initial_state.to(torch.float32).contiguous()
 
 
+_ERROR_BITS = {1: "a chunk prep wait timed out", 2: "a chunk scan wait timed out",
+               8: "packed-sequence offsets were not a valid cu_seqlens", 16: "bounded-wait self-test"}
+_error_mirrors: dict = {}  # device index -> page-locked int32 word the library mirrors the error bits into
+
+
+def check_device_errors(device: Optional[torch.device] = None) -> None:
+    """Raise ``GDNError`` (``GDN_ERR_KERNEL``) if a kernel on ``device`` (default: the current one) reported a
+    failure in the library's device error word, and clear the word.
+
+    Every op calls this before it launches.  The first call on a device registers a page-locked host mirror
+    of the word (``gdn_set_error_mirror``, one synchronous copy; make it before any stream capture); later
+    checks read that host word only, so they cost no synchronisation.  A failure therefore surfaces at the
+    next op on the device, or here once the failing call has finished on the device (synchronise first to
+    check the latest call)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        word = _error_mirrors.get(dev.index)
+        if word is None:
+            word = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+            _lib.check(lib.gdn_set_error_mirror(word.data_ptr()))
+            _error_mirrors[dev.index] = word
+            bits = lib.gdn_device_error(1)  # anything reported before the mirror existed
+        else:
+            bits = lib.gdn_device_error_pending()
+            if bits:
+                bits = lib.gdn_device_error(1)
+    if bits:
+        what = "; ".join(v for b, v in _ERROR_BITS.items() if bits & b) or "unknown"
+        raise _lib.GDNError(_lib.GDN_ERR_KERNEL, "GDN_ERR_KERNEL",
+                            f"a kernel on {dev} reported device error bits 0x{bits:x} ({what}); the outputs of "
+                            "the call that launched it are not valid")
+
+
+def _workspace(workspace: Optional[torch.Tensor], need: int, dev: torch.device) -> torch.Tensor:
+    """The caller's workspace if it is a large enough CUDA buffer on ``dev``, else a new one.  A workspace on
+    another device or on the host is an error, not a silent reallocation: the kernels would write into it."""
+    if workspace is not None:
+        if not isinstance(workspace, torch.Tensor) or workspace.device != dev:
+            where = workspace.device if isinstance(workspace, torch.Tensor) else type(workspace).__name__
+            raise RuntimeError(f"workspace is on {where}; it must be a CUDA tensor on {dev}")
+        if workspace.numel() * workspace.element_size() >= need and workspace.is_contiguous():
+            return workspace
+    return torch.empty((max(need, 1),), dtype=torch.uint8, device=dev)
+
+
 def _check_backend(backend: str) -> None:
     if backend == "torch":
         raise RuntimeError("backend 'torch' is the reference's pure-PyTorch path; this package runs only its "
@@ -133,9 +179,9 @@ def fast_chunk_gated_delta_rule(
     final = torch.empty((B, H, Dk, Dv), dtype=torch.float32, device=dev) if output_final_state else None
     lib = _lib.load()
     with torch.cuda.device(dev):
+        check_device_errors(dev)
         ws_bytes = lib.gdn_chunk_workspace_bytes(B, T, H, Dk, Dv, _DTYPES[q.dtype])
-        if workspace is None or workspace.numel() < ws_bytes:
-            workspace = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+        workspace = _workspace(workspace, ws_bytes, dev)
         dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
         stream = torch.cuda.current_stream(dev).cuda_stream
         rc = lib.gdn_chunk_gated_delta_rule(
@@ -197,9 +243,9 @@ def _chunk_from_host(query, key, value, g, beta, chunk_size, initial_state, outp
     dev = torch.device("cuda", torch.cuda.current_device())
     lib = _lib.load()
     with torch.cuda.device(dev):
+        check_device_errors(dev)
         need = lib.gdn_chunk_host_workspace_bytes(B, T, H, Dk, Dv, _DTYPES[q.dtype], int(slice_tokens))
-        if workspace is None or workspace.device != dev or workspace.numel() < need:
-            workspace = torch.empty((max(need, 1),), dtype=torch.uint8, device=dev)
+        workspace = _workspace(workspace, need, dev)
         dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
         stream = torch.cuda.current_stream(dev)
         rc = lib.gdn_chunk_gated_delta_rule_host(
@@ -253,6 +299,7 @@ def fast_recurrent_gated_delta_rule(
             final = torch.empty((B, H, Dk, Dv), dtype=torch.float32, device=dev)
     lib = _lib.load()
     with torch.cuda.device(dev):
+        check_device_errors(dev)
         dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
         stream = torch.cuda.current_stream(dev).cuda_stream
         rc = lib.gdn_recurrent_gated_delta_rule(
@@ -307,9 +354,9 @@ def chunk_gated_delta_rule_varlen(
     final = torch.empty((N, H, Dk, Dv), dtype=torch.float32, device=q.device) if output_final_state else None
     lib = _lib.load()
     with torch.cuda.device(q.device):
+        check_device_errors(q.device)
         need = lib.gdn_chunk_varlen_workspace_bytes(T, max(N, 1), H, Dk, Dv, _DTYPES[q.dtype])
-        if workspace is None or workspace.numel() < need:
-            workspace = torch.empty((max(need, 1),), dtype=torch.uint8, device=q.device)
+        workspace = _workspace(workspace, need, q.device)
         dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
         rc = lib.gdn_chunk_gated_delta_rule_varlen(
             ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(dg), ctypes.byref(db),
@@ -367,9 +414,9 @@ def chunk_gated_delta_rule_bwd(
     dh0 = torch.empty((B, H, Dk, Dv), dtype=torch.float32, device=dev) if initial_state is not None else None
     lib = _lib.load()
     with torch.cuda.device(dev):
+        check_device_errors(dev)
         need = lib.gdn_chunk_bwd_workspace_bytes(B, T, H, Dk, Dv, _DTYPES[q.dtype])
-        if workspace is None or workspace.numel() < need:
-            workspace = torch.empty((max(need, 1),), dtype=torch.uint8, device=dev)
+        workspace = _workspace(workspace, need, dev)
         descs = [_desc(x) for x in (q, k, v, gg, bb, do, dq, dk, dv, dg, db)]
         rc = lib.gdn_chunk_gated_delta_rule_bwd(
             *[ctypes.byref(d) for d in descs[:6]], int(chunk_size), h0.data_ptr() if h0 is not None else None,

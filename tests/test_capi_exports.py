@@ -268,6 +268,27 @@ def test_python_op_refuses_cpu_tensors_and_torch_backend():
         fast_chunk_gated_delta_rule(q, q, q, g, g, backend="nope")
 
 
+def test_workspace_on_the_host_or_another_device_is_rejected():
+    """A caller's workspace is handed to the kernels as a raw pointer, so it must be a CUDA buffer on the
+    inputs' device; anything else raises instead of letting the kernels write through a foreign pointer."""
+    import torch
+
+    from llms_from_scratch_b200.ops import _workspace
+    dev0 = torch.device("cuda", 0)
+    with pytest.raises(RuntimeError, match="workspace is on cpu"):
+        _workspace(torch.empty(1 << 10, dtype=torch.uint8), 16, dev0)
+    with pytest.raises(RuntimeError, match="workspace is on"):
+        _workspace(bytearray(64), 16, dev0)
+    if torch.cuda.device_count() >= 2:
+        with pytest.raises(RuntimeError, match="cuda:1"):
+            _workspace(torch.empty(64, dtype=torch.uint8, device="cuda:1"), 16, dev0)
+
+
+def test_status_names_cover_every_status(lib):
+    names = [lib.gdn_status_name(i).decode() for i in range(7)]
+    assert names[6] == "GDN_ERR_KERNEL" and "GDN_UNKNOWN_STATUS" not in names
+
+
 def test_compat_module_exports_reference_names():
     import importlib
     import sys

@@ -29,14 +29,18 @@ def dev(x, dt=torch.float32):
     return torch.from_numpy(np.ascontiguousarray(x)).cuda().to(dt)
 
 
-@pytest.mark.parametrize("gscale", [1.0, 0.05])
-def test_shards_composed_on_one_gpu_match_the_full_sequence(gscale):
+@pytest.mark.parametrize("T,H,cuts,gscale", [
+    (700, 4, [0, 150, 469, 700], 1.0),
+    (700, 4, [0, 150, 469, 700], 0.05),
+    # config 5's layout (H=16, bf16, time shards) at a length the oracle finishes in seconds
+    (8192, 16, [0, 2731, 5461, 8192], 1.0),
+])
+def test_shards_composed_on_one_gpu_match_the_full_sequence(T, H, cuts, gscale):
     from llms_from_scratch_b200 import fast_chunk_gated_delta_rule
     from llms_from_scratch_b200.parallel import chunk_shard_finish, chunk_shard_summary, compose_start_states
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    T, cuts = 700, [0, 150, 469, 700]
-    q, k, v, g, beta, s0 = O.make_inputs(1, T, 4, seed=12, in_dtype="bf16", init_state_std=0.02, normalize_qk=False)
+    q, k, v, g, beta, s0 = O.make_inputs(1, T, H, seed=12, in_dtype="bf16", init_state_std=0.02, normalize_qk=False)
     g = (g * gscale).astype(np.float32)
     tq, tk, tv = (dev(x, torch.bfloat16) for x in (q, k, v))
     tg, tb, ts = dev(g), dev(beta), dev(s0)

@@ -144,7 +144,7 @@ def test_chunk_without_l2norm_and_without_final_state(in_dtype):
     assert_parity(o, ro, in_dtype, "out")
 
 
-@pytest.mark.parametrize("T", [256, 1024, 4096])
+@pytest.mark.parametrize("T", [256, 512, 1024, 2048, 4096])
 def test_config2_bf16_full_size_vs_oracle(T):
     """Benchmark config 2: B=1, H=16, bf16 q/k/v, fp32 g/beta, initial state ~ N(0, 0.02)."""
     q, k, v, g, beta, s0 = O.make_inputs(1, T, 16, seed=0, in_dtype="bf16", init_state_std=0.02)
@@ -210,6 +210,28 @@ def test_batch_independence_config3_sample():
                                                use_qk_l2norm_in_kernel=True)
         torch.testing.assert_close(ob, o[b:b + 1], rtol=0, atol=0)
         torch.testing.assert_close(sb, s[b:b + 1], rtol=0, atol=0)
+
+
+def test_config3_full_size_sequences_vs_oracle():
+    """Config 3 at full size (B=64, T=4096, H=16, bf16, initial state ~ N(0, 0.02)): three sequences of the
+    batched call against the oracle, each on its own."""
+    m = ops()
+    B, T, H = 64, 4096, 16
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    q = torch.nn.functional.normalize(torch.randn(B, T, H, 128, device="cuda", generator=gen), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(B, T, H, 128, device="cuda", generator=gen), dim=-1).bfloat16()
+    v = torch.randn(B, T, H, 128, device="cuda", generator=gen).bfloat16()
+    g = -torch.nn.functional.softplus(torch.randn(B, T, H, device="cuda", generator=gen))
+    beta = torch.randn(B, T, H, device="cuda", generator=gen).sigmoid()
+    s0 = torch.randn(B, H, 128, 128, device="cuda", generator=gen) * 0.02
+    o, s = m.fast_chunk_gated_delta_rule(q, k, v, g, beta, initial_state=s0, output_final_state=True,
+                                         use_qk_l2norm_in_kernel=True)
+    for b in (0, 31, 63):
+        host = [x[b:b + 1].float().cpu().numpy() for x in (q, k, v, g, beta, s0)]
+        ro, rs = O.chunk_gated_delta_rule(*host[:5], initial_state=host[5], output_final_state=True,
+                                          use_qk_l2norm_in_kernel=True, in_dtype="bf16")
+        assert_parity(o[b:b + 1].float().cpu().numpy(), ro, "bf16", f"sequence {b} out")
+        assert_parity(s[b:b + 1].cpu().numpy(), rs, "bf16", f"sequence {b} state")
 
 
 @pytest.mark.parametrize("in_dtype", ["fp32", "bf16"])
