@@ -14,9 +14,14 @@ time per step comes from CUDA events on the launching stream; a 256 MiB buffer
 (2x L2) is written between timed steps so every step starts with a cold L2.
 ``e2e`` times the same op called with page-locked host tensors (inputs copied
 in and outputs copied out inside the timed region, which the op pipelines in
-time slices against its kernels).  rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU
-algorithm (the oracle port; the reference is Python/PyTorch and has no
-compiled CPU code) on rank 0 with all host threads.
+time slices against its kernels).  rank 0 prints one JSON line.
+
+``--impl reference`` times the reference's own CPU path, its
+``torch_chunk_gated_delta_rule`` (qwen3_5_transformers.py:110-187) imported
+unmodified from the reference install in ``baseline/_ref``, on rank 0 with all
+host threads, on the same seeded inputs at the same B, T, H; without that
+install it falls back to the numpy port of the same algorithm
+(``oracle/gdn_oracle.py``, kind "port").
 """
 
 from __future__ import annotations
@@ -54,6 +59,10 @@ def parse_args():
     ap.add_argument("--H", type=int, default=16)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs35", action="store_true", help="skip the config 3 (B=64) and config 5 (--sp-T "
+                                                                    "time-sharded) legs")
+    ap.add_argument("--no-reference-triton", action="store_true",
+                    help="skip timing the reference's Triton path (baseline/_ref) beside this package's")
     ap.add_argument("--soak-seconds", type=float, default=1.0, help="untimed load before timing (clock sampling)")
     ap.add_argument("--sp", action="store_true",
                     help="config 5: one sequence of --sp-T tokens (B=1) split in time across the ranks")
@@ -336,7 +345,11 @@ def load_fla():
         return None, f"{type(e).__name__}: {e}"[:200]
 
 
-def make_inputs(torch, B, T, H, seed, device):
+def make_inputs(torch, B, T, H, seed, device, on_host=False):
+    """Config-2 inputs; ``on_host`` draws them with the host generator and copies them to ``device``, so the
+    reference arm (which draws them on the host) times the very same tensors."""
+    if on_host and str(device) != "cpu":
+        return tuple(x.to(device) for x in make_inputs(torch, B, T, H, seed, "cpu"))
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     q = torch.randn(B, T, H, D, device=device, generator=gen)
@@ -351,6 +364,103 @@ def make_inputs(torch, B, T, H, seed, device):
 
 
 # --------------------------------------------------------------------------- CPU (oracle port)
+
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def load_reference_module(name: str):
+    """A module of the reference as installed (unmodified) in baseline/_ref, loaded by file path under a
+    private name (this package's drop-in shim is also called qwen3_5_cutedsl_kernels), or None when the
+    install is absent."""
+    import importlib.util
+    path = os.path.join(REF_DIR, name + ".py")
+    if not os.path.exists(path):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.append(REF_DIR)  # its modules import each other by plain name
+    key = "_reference_" + name
+    if key in sys.modules:
+        return sys.modules[key]
+    spec = importlib.util.spec_from_file_location(key, path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[key] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def time_reference_torch(T, H, steps=None, warmup=1, seconds=None):
+    """Time the reference's own torch_chunk_gated_delta_rule (qwen3_5_transformers.py:110-187) on the host
+    cores at B=1, T, H on the headline's inputs (same seed, generated on the host); returns (times, cores) or
+    None without the reference install."""
+    ref = load_reference_module("qwen3_5_transformers")
+    if ref is None:
+        return None
+    import torch
+    cores = host_threads()
+    torch.set_num_threads(cores)  # torchrun sets OMP_NUM_THREADS=1; use every core this process may run on
+    q, k, v, g, beta, s0 = make_inputs(torch, 1, T, H, seed=1234, device="cpu")
+
+    def one():
+        ref.torch_chunk_gated_delta_rule(q, k, v, g, beta, chunk_size=CHUNK, initial_state=s0,
+                                         output_final_state=True, use_qk_l2norm_in_kernel=True)
+
+    with torch.no_grad():
+        for _ in range(warmup):
+            one()
+        times = []
+        t_start = time.perf_counter()
+        while True:
+            t = time.perf_counter()
+            one()
+            times.append(time.perf_counter() - t)
+            if steps is not None and len(times) >= steps:
+                break
+            if seconds is not None and time.perf_counter() - t_start >= seconds and len(times) >= 3:
+                break
+    return times, cores
+
+
+def time_reference_triton(torch, flush, device, H, Ts, reps=10):
+    """The reference's GPU path, fast_chunk_gated_delta_rule(backend="triton") (qwen3_5_cutedsl_kernels.py:
+    462-567: its Triton intra-chunk kernel plus the Python inter-chunk loop), at the correct [B,T,H,D] layout,
+    beside this package's call on the same tensors, cold L2, at each T of config 2."""
+    from llms_from_scratch_b200 import fast_chunk_gated_delta_rule
+    try:
+        kern = load_reference_module("qwen3_5_cutedsl_kernels")
+    except Exception as e:  # the reference module failed to import here
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    if kern is None:
+        return {"unavailable": "baseline/_ref (the reference install) is absent"}
+    if not getattr(kern, "_TRITON_OK", False):
+        return {"unavailable": "triton is not importable"}
+    res = {"workload": f"B=1, T in {list(Ts)}, H={H}, bf16 q/k/v, fp32 g/beta/state, l2norm in kernel, initial "
+                       "and final state; cold L2; median of device times"}
+    for T in Ts:
+        q, k, v, g, beta, s0 = make_inputs(torch, 1, T, H, seed=1234, device=device)
+        args = dict(chunk_size=CHUNK, initial_state=s0, output_final_state=True, use_qk_l2norm_in_kernel=True)
+
+        def ref_fn():
+            return kern.fast_chunk_gated_delta_rule(q, k, v, g, beta, backend="triton", **args)
+
+        def our_fn():
+            return fast_chunk_gated_delta_rule(q, k, v, g, beta, **args)
+
+        r_ms = _cold_median(torch, ref_fn, flush, reps)
+        o_ms = _cold_median(torch, our_fn, flush, reps)
+        ro, rs = ref_fn()
+        oo, os_ = our_fn()
+        rel = float((oo.float() - ro.float()).norm() / ro.float().norm())
+        res[str(T)] = {"reference_triton_ms": r_ms, "ours_ms": o_ms, "speedup": r_ms / o_ms,
+                       "out_rel_l2_ours_vs_reference": rel}
+    return res
+
 
 def cpu_threads():
     try:
@@ -390,50 +500,48 @@ def time_oracle(T_sample, H, seconds=None, steps=None, warmup=0):
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    T_sample = min(1024, args.T)
-    times = time_oracle(T_sample, args.H, steps=max(1, args.steps), warmup=max(0, args.warmup))
+    timed = time_reference_torch(args.T, args.H, steps=max(1, args.steps), warmup=max(0, args.warmup))
+    if timed is not None:
+        times, cores = timed
+        T_run, kind = args.T, "reference"
+        sample = (f"B=1, T={args.T}, H={args.H}, bf16 q/k/v, fp32 g/beta/state (the GPU arm's rank-0 inputs, "
+                  f"seed 1234), l2norm in kernel, initial and final state; torch_chunk_gated_delta_rule from "
+                  f"the unmodified reference install, torch on {cores} host threads")
+        note = "the reference's own CPU path (qwen3_5_transformers.py:110-187) at the full configuration"
+    else:  # no reference install on this box: the numpy port of the same algorithm on a sample
+        T_run = min(1024, args.T)
+        times = time_oracle(T_run, args.H, steps=max(1, args.steps), warmup=max(0, args.warmup))
+        cores, kind = cpu_threads(), "port"
+        sample = f"B=1, first {T_run} of T={args.T} tokens, H={args.H}, bf16 inputs (numpy oracle port)"
+        note = "baseline/_ref absent: the numpy port in oracle/gdn_oracle.py (pinned to the reference's outputs)"
     mean_s = statistics.mean(times)
-    value = args.B * T_sample / mean_s  # tok/s of the sample (the algorithm's cost is linear in T)
-    sample = f"B=1, first {T_sample} of T={args.T} tokens, H={args.H}, bf16 inputs (numpy oracle port)"
-    cores = cpu_threads()
+    value = args.B * T_run / mean_s
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": len(times), "warmup": args.warmup, "ms_per_step": mean_s * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": f"gdn_chunk_fwd B={args.B} T={args.T} H={args.H} Dk=Dv=128 chunk=64 (CPU sample)",
-                   "global_batch": args.B, "seq_len": args.T, "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "config": {"workload": f"gdn_chunk_fwd B={args.B} T={args.T} H={args.H} Dk=Dv=128 chunk=64 bf16 q/k/v, "
+                               "fp32 g/beta/state, l2norm in kernel, final state out",
+                   "global_batch": args.B, "seq_len": args.T, "heads": args.H, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "the reference is Python/PyTorch with no compiled CPU code; its algorithm runs as the numpy "
-                "port in oracle/gdn_oracle.py (pinned to the reference's own outputs)",
+        "note": note,
     }
     print(json.dumps(line), flush=True)
 
 
 # --------------------------------------------------------------------------- GPU arm
 
-def run_sequence_parallel(args, rank, world, local):
-    """Config 5: B=1, one sequence of args.sp_T tokens, contiguous time shards, one per rank
-    (strong scaling).  A step = shard summary + all_gather of (transition, local state) +
-    start-state composition + shard finish; device time, max over ranks."""
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-
+def sequence_parallel_leg(torch, dist, rank, world, device, flush, T, H, steps, warmup):
+    """Config 5: B=1, one sequence of T tokens, contiguous time shards, one per rank (strong scaling).  A step =
+    shard summary + all_gather of (transition, local state) + start-state composition + shard finish; device
+    time per step (CUDA events), max over ranks."""
+    from llms_from_scratch_b200 import _lib
     from llms_from_scratch_b200.parallel import chunk_shard_finish, chunk_shard_summary, compose_start_states
-
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
-    T, H = args.sp_T, args.H
     lo, hi = T * rank // world, T * (rank + 1) // world
     q, k, v, g, beta, s0 = make_inputs(torch, 1, hi - lo, H, seed=77 + rank, device=device)
-    from llms_from_scratch_b200 import _lib
     ws = torch.empty(_lib.load().gdn_chunk_workspace_bytes(1, hi - lo, H, D, D, _lib.GDN_BF16), dtype=torch.uint8,
                      device=device)
-    flush = L2Flush(torch, device)
 
     def step():
         M, b, _ = chunk_shard_summary(q, k, v, g, beta, True, ws)
@@ -447,14 +555,14 @@ def run_sequence_parallel(args, rank, world, local):
                                                            [x[1] for x in gathered[:rank]], s0)[rank]
         return chunk_shard_finish(q, k, v, g, beta, start, True, True, ws)
 
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         step()
     torch.cuda.synchronize()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    for i in range(args.steps):
+    for i in range(steps):
         flush(i)
         evs[i][0].record()
         step()
@@ -465,14 +573,73 @@ def run_sequence_parallel(args, rank, world, local):
         t = torch.tensor([ms], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    del q, k, v, g, beta, ws
+    return {"workload": f"config 5: B=1 T={T} H={H} bf16, time-sharded x{world} (summary + all_gather + compose + "
+                        "finish), strong scaling", "ms": ms, "tok_s": T / (ms / 1e3), "n_gpus": world}
+
+
+def batched_leg(torch, dist, rank, world, device, flush, B_global, T, H, steps, warmup):
+    """Config 3: a global batch of B_global sequences of T tokens sharded by batch over the ranks (no
+    collective); whole-job tok/s from the max over ranks of the per-step device time."""
+    from llms_from_scratch_b200 import _lib, fast_chunk_gated_delta_rule
+    Bl = B_global // world
+    q, k, v, g, beta, s0 = make_inputs(torch, Bl, T, H, seed=4321 + rank, device=device)
+    ws = torch.empty(_lib.load().gdn_chunk_workspace_bytes(Bl, T, H, D, D, _lib.GDN_BF16), dtype=torch.uint8,
+                     device=device)
+
+    def step():
+        return fast_chunk_gated_delta_rule(q, k, v, g, beta, initial_state=s0, output_final_state=True,
+                                           use_qk_l2norm_in_kernel=True, workspace=ws)
+
+    ms = _timed_steps(torch, dist, world, device, step, flush, steps, warmup)
+    del q, k, v, g, beta, ws
+    return {"workload": f"config 3: global B={B_global} T={T} H={H} bf16, {Bl} sequences per rank (batch x head "
+                        f"shards, no collective)", "ms": ms, "tok_s": B_global * T / (ms / 1e3), "n_gpus": world}
+
+
+def _timed_steps(torch, dist, world, device, step, flush, steps, warmup):
+    """Mean device time per step (CUDA events, cold L2), max over ranks."""
+    for _ in range(max(3, warmup)):
+        step()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        flush(i)
+        evs[i][0].record()
+        step()
+        evs[i][1].record()
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b_) for a, b_ in evs)
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_sequence_parallel(args, rank, world, local):
+    """``--sp``: config 5 alone, printed as its own JSON line."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    flush = L2Flush(torch, device)
+    r = sequence_parallel_leg(torch, dist, rank, world, device, flush, args.sp_T, args.H, args.steps, args.warmup)
     if rank == 0:
         print(json.dumps({
-            "metric": "GDN chunk-fwd tok/s, sequence parallel @B=1,T=%d" % T, "value": T / (ms / 1e3),
-            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "metric": "GDN chunk-fwd tok/s, sequence parallel @B=1,T=%d" % args.sp_T, "value": r["tok_s"],
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": f"gdn_chunk_fwd B=1 T={T} H={H} time-sharded x{world} (summary + all_gather + "
-                                   "compose + finish)", "global_batch": 1, "seq_len": T,
+            "config": {"workload": r["workload"], "global_batch": 1, "seq_len": args.sp_T,
                        "parallelism": f"sequence-parallel x{world}", "l2": L2_NOTE},
         }), flush=True)
     if world > 1:
@@ -514,7 +681,7 @@ def main():
 
     lib = _lib.load()
     B, T, H = args.B, args.T, args.H
-    q, k, v, g, beta, s0 = make_inputs(torch, B, T, H, seed=1234 + rank, device=device)
+    q, k, v, g, beta, s0 = make_inputs(torch, B, T, H, seed=1234 + rank, device=device, on_host=True)
     ws = torch.empty(lib.gdn_chunk_workspace_bytes(B, T, H, D, D, _lib.GDN_BF16), dtype=torch.uint8, device=device)
     flush = L2Flush(torch, device)
 
@@ -551,10 +718,13 @@ def main():
     torch.cuda.synchronize()
     launches0 = lib.gdn_launch_count()
     t_timed0 = time.perf_counter()
+    host_s = []
     for i in range(K):  # the production call: no instrumentation between its kernels
         flush(i)
         outer[i][0].record()
+        th = time.perf_counter()
         step()
+        host_s.append(time.perf_counter() - th)
         outer[i][1].record()
     torch.cuda.synchronize()
     barrier()
@@ -574,6 +744,13 @@ def main():
     scan_ms = [evs[1].elapsed_time(evs[2]) for evs in phase]
     ms_local = statistics.mean(step_ms)
     ms = max_over_ranks(ms_local)
+    host_us_local = statistics.mean(host_s) * 1e6
+    per_rank = [[ms_local, host_us_local]]
+    if world > 1:
+        mine = torch.tensor([ms_local, host_us_local], device=device, dtype=torch.float64)
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        per_rank = [x.tolist() for x in allr]
     tokens_job = world * B * T
     value = tokens_job / (ms / 1e3)
 
@@ -635,6 +812,15 @@ def main():
     peak_l, _ = load_peaks()
     layer_kernels = time_layer_kernels(torch, lib, flush, device, T, H, Bd, peak_l)
     backward = time_backward(torch, lib, flush, device, T, H)
+    # ---- configs 3 and 5 over the same ranks (extra keys; the headline stays config 2 per rank)
+    batched = sp = None
+    if not args.no_configs35:
+        batched = batched_leg(torch, dist, rank, world, device, flush, 64, 4096, H, steps=5, warmup=3)
+        sp = sequence_parallel_leg(torch, dist, rank, world, device, flush, args.sp_T, H, steps=5, warmup=3)
+        torch.cuda.empty_cache()
+    ref_triton = None
+    if rank == 0 and not args.no_reference_triton:
+        ref_triton = time_reference_triton(torch, flush, device, H, (256, 512, 1024, 2048, 4096))
     fla, fla_err = load_fla() if args.fla else (None, None)
     packed = time_packed(torch, flush, device, H, peak_l, fla=fla)
     fla_headline = None
@@ -663,13 +849,21 @@ def main():
     traffic = load_traffic(dom, workload)
     step_bytes = B * H * T * BYTES_PER_TOKEN_HEAD + 2 * B * H * STATE_BYTES
 
-    cpu = None
+    cpu = cpu_port = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        timed = time_reference_torch(T, H, warmup=1, seconds=args.cpu_seconds)
+        if timed is not None:
+            times, cores = timed
+            cpu = {"value": B * T / statistics.mean(times), "unit": UNIT, "cores": cores, "kind": "reference",
+                   "sample": f"B=1, T={T}, H={H}: the headline's rank-0 inputs, {len(times)} runs of the reference's "
+                             f"own torch_chunk_gated_delta_rule (unmodified install) on {cores} host threads"}
         T_sample = min(1024, T)
-        times = time_oracle(T_sample, H, seconds=args.cpu_seconds, warmup=1)
-        cpu = {"value": T_sample / statistics.mean(times), "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-               "sample": f"B=1, first {T_sample} of T={T} tokens, H={H}, bf16 inputs, {len(times)} runs "
-                         f"(numpy oracle port of torch_chunk_gated_delta_rule)"}
+        times = time_oracle(T_sample, H, seconds=min(3.0, args.cpu_seconds), warmup=1)
+        cpu_port = {"value": T_sample / statistics.mean(times), "unit": UNIT, "cores": cpu_threads(),
+                    "kind": "port", "sample": f"B=1, first {T_sample} of T={T} tokens, H={H}, bf16 inputs, "
+                                              f"{len(times)} runs (numpy oracle port)"}
+        if cpu is None:
+            cpu = cpu_port
 
     if rank == 0:
         line = {
@@ -692,6 +886,9 @@ def main():
             "e2e": {"value": tokens_job / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "gpu_launches": launches,
+            "per_rank": [{"rank": r, "step_ms": v[0], "host_enqueue_us": v[1]} for r, v in enumerate(per_rank)],
+            "batched_b64": batched,
+            "sp": sp,
             "clocks": clocks.summary(t_soak, t_end),
             "layer_kernels": layer_kernels,
             "packed_prefill": packed,
@@ -700,6 +897,8 @@ def main():
                             "ms": dec_ms, "achieved_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
                             "frac_hbm": dec_bytes / (dec_ms / 1e3) / 1e9 / peak},
             "cpu_baseline": cpu,
+            "cpu_port": cpu_port,
+            "reference_triton": ref_triton,
         }
         if fla_headline is not None:
             line["vllm_fla"] = fla_headline
