@@ -61,6 +61,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs35", action="store_true", help="skip the config 3 (B=64) and config 5 (--sp-T "
                                                                     "time-sharded) legs")
+    ap.add_argument("--no-decode-model", action="store_true", help="skip the config 4 decoder leg")
     ap.add_argument("--no-reference-triton", action="store_true",
                     help="skip timing the reference's Triton path (baseline/_ref) beside this package's")
     ap.add_argument("--soak-seconds", type=float, default=1.0, help="untimed load before timing (clock sampling)")
@@ -620,6 +621,107 @@ def _timed_steps(torch, dist, world, device, step, flush, steps, warmup):
     return ms
 
 
+def decode_model_leg(torch, device, peak, batches=(1, 32), steps=200, prompt_len=26):
+    """Config 4: the Qwen3.5-0.8B-shaped decoder with random N(0, 0.02) weights (drawn on the device), a
+    prompt of 26 uniform-random ids per sequence, then `steps` greedy decode steps (each a CUDA-graph replay
+    of the whole step: 18 linear-attention layers through the recurrent kernel, 6 attention layers over the
+    KV cache, the LM head and the argmax), at batch 1 and 32.  Device time by CUDA events; decode tok/s =
+    B * steps / decode time.  A profiled eager pass of a few steps gives each kernel family's share of the
+    step and the recurrent kernel's achieved GB/s."""
+    from llms_from_scratch_b200.model import QWEN3_5_0_8B, Qwen35Decoder, count_parameters, random_weights
+    cfg = QWEN3_5_0_8B
+    w = random_weights(cfg, seed=0, device=device)
+    dec = Qwen35Decoder(cfg, w, device=device, max_len=prompt_len + steps + 2)
+    del w
+    res = {"workload": f"random-init Qwen3.5-0.8B-shaped decoder ({count_parameters(cfg) / 1e6:.0f} M parameters, "
+                       f"hidden 1024, 24 layers: 18 GatedDeltaNet + 6 full attention, vocab {cfg['vocab_size']}, "
+                       f"bf16, weights ~ N(0, 0.02)); prefill of {prompt_len} uniform-random ids, then {steps} greedy "
+                       "decode steps (one CUDA-graph replay each)", "steps": steps}
+    gen = torch.Generator(device=device)
+    gen.manual_seed(11)
+    n_gdn = sum(1 for t in cfg["layer_types"] if t == "linear_attention")
+    for B in batches:
+        prompt = torch.randint(0, cfg["vocab_size"], (B, prompt_len), device=device, generator=gen)
+        cache = dec.new_cache(B)
+        dec.generate(prompt, steps, cache=cache)  # warm-up; captures the decode graph for this cache
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        runs = []
+        for _ in range(3):
+            ev[0].record()
+            logits = dec.prefill(prompt, cache)
+            ev[1].record()
+            dec.step_tokens.copy_(logits.argmax(-1))
+            for _ in range(steps):
+                dec._graph.replay()
+            ev[2].record()
+            torch.cuda.synchronize()
+            runs.append((ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])))
+        prefill_ms = statistics.median(r[0] for r in runs)
+        decode_ms = statistics.median(r[1] for r in runs)
+        ms_tok = decode_ms / steps
+        # kernel shares from a profiled eager pass of 8 decode steps (the same kernels the graph replays)
+        share, rec_us = _decode_kernel_shares(torch, dec, cache, prompt, 8)
+        rec_bytes = B * cfg["linear_num_value_heads"] * (2 * STATE_BYTES + 4 * D * 2 + 8)
+        res[f"batch{B}"] = {
+            "tok_s": B * steps / (decode_ms / 1e3), "ms_per_token": ms_tok, "prefill_ms": prefill_ms,
+            "kernel_share": share,
+            "recurrent_kernel": {"us_per_layer": rec_us, "bytes_per_layer": rec_bytes,
+                                 "achieved_gbs": rec_bytes / (rec_us / 1e6) / 1e9 if rec_us else None,
+                                 "frac_hbm": rec_bytes / (rec_us / 1e6) / 1e9 / peak if rec_us else None,
+                                 "layers_per_step": n_gdn},
+        }
+        del cache
+        dec._graph = None
+        torch.cuda.empty_cache()
+    res["batch1_tok_s"] = res["batch1"]["tok_s"] if "batch1" in res else None
+    res["batch32_tok_s"] = res["batch32"]["tok_s"] if "batch32" in res else None
+    return res
+
+
+def _decode_kernel_shares(torch, dec, cache, prompt, n):
+    """Device-time share of each kernel family over n eager decode steps (torch profiler), and the mean
+    duration of the recurrent kernel in microseconds."""
+    try:
+        return _decode_kernel_shares_inner(torch, dec, cache, prompt, n)
+    except Exception as e:  # a profiler that cannot trace here leaves the shares unreported, not the leg
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}, None
+
+
+def _decode_kernel_shares_inner(torch, dec, cache, prompt, n):
+    from torch.profiler import ProfilerActivity, profile
+    logits = dec.prefill(prompt, cache)
+    tok = logits.argmax(-1)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n):
+            tok = dec.decode_step(tok, cache).argmax(-1)
+        torch.cuda.synchronize()
+    fam = {"recurrent (gdn_recurrent_kernel)": ("gdn_recurrent",), "GEMM (cuBLAS)": ("gemm", "gemv", "nvjet", "cutlass",
+                                                                                    "sm100", "xmma"),
+           "attention (gdn_model_attention + attn_prep)": ("gdn_model_attention", "gdn_model_attn_prep"),
+           "norms (add_rms_norm, gated norm)": ("add_rms_norm", "rms_norm_gated"),
+           "conv update + gates": ("conv_update", "gates_kernel"), "silu_mul": ("silu_mul",)}
+    tot, by, rec = 0.0, {k: 0.0 for k in fam}, []
+    by["other (embedding, argmax, copies)"] = 0.0
+    for e in prof.events():
+        if e.device_type.name != "CUDA":
+            continue
+        t = e.device_time_total if hasattr(e, "device_time_total") else e.cuda_time_total
+        tot += t
+        name = e.name.lower()
+        for k, keys in fam.items():
+            if any(x in name for x in keys):
+                by[k] += t
+                break
+        else:
+            by["other (embedding, argmax, copies)"] += t
+        if "gdn_recurrent" in name:
+            rec.append(t)
+    share = {k: v / tot for k, v in by.items()} if tot else {}
+    return share, (statistics.mean(rec) if rec else None)
+
+
 def run_sequence_parallel(args, rank, world, local):
     """``--sp``: config 5 alone, printed as its own JSON line."""
     import datetime
@@ -818,6 +920,10 @@ def main():
         batched = batched_leg(torch, dist, rank, world, device, flush, 64, 4096, H, steps=5, warmup=3)
         sp = sequence_parallel_leg(torch, dist, rank, world, device, flush, args.sp_T, H, steps=5, warmup=3)
         torch.cuda.empty_cache()
+    decode_model = None
+    if not args.no_decode_model:
+        decode_model = decode_model_leg(torch, device, peak_l)
+        torch.cuda.empty_cache()
     ref_triton = None
     if rank == 0 and not args.no_reference_triton:
         ref_triton = time_reference_triton(torch, flush, device, H, (256, 512, 1024, 2048, 4096))
@@ -887,6 +993,7 @@ def main():
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "gpu_launches": launches,
             "per_rank": [{"rank": r, "step_ms": v[0], "host_enqueue_us": v[1]} for r, v in enumerate(per_rank)],
+            "decode_model": decode_model,
             "batched_b64": batched,
             "sp": sp,
             "clocks": clocks.summary(t_soak, t_end),

@@ -259,7 +259,9 @@ GDN_API int gdn_gates(const gdn_tensor* a, const gdn_tensor* b, const gdn_tensor
                       gdn_tensor* g, gdn_tensor* beta, void* stream);
 
 /* Gated RMS norm: replaces Qwen3_5RMSNormGated.forward(x, gate) (:62-71) over rows
- * of 128 (head_v_dim).  x, gate, out [N,128]; weight [128]; one dtype. */
+ * of 128 (head_v_dim).  x, gate, out [N,128], or [M,H,128] views (each with its
+ * own strides: e.g. the gate z as a strided view of a wider projection, :331-332);
+ * weight [128]; one dtype. */
 GDN_API int gdn_rms_norm_gated(const gdn_tensor* x, const gdn_tensor* gate, const gdn_tensor* weight, float eps,
                                gdn_tensor* out, void* stream);
 
@@ -292,21 +294,18 @@ GDN_API void gdn_set_phase_events(void* const* events, int n);
  * context reset) after the first call on it is not supported. */
 GDN_API unsigned int gdn_device_error(int clear);
 
-/* Mirrors the current device's error bits into `host_word`, 4 bytes of
- * page-locked host memory mapped into the device (cudaHostAlloc, or
- * cudaHostRegister with cudaHostRegisterMapped) that the caller owns and keeps
- * alive: a kernel that sets a bit also stores it there, so a caller can poll
- * for failures with gdn_device_error_pending() without synchronising the
- * device.  Resets the word to 0.  NULL stops mirroring.  Synchronous; call it
- * outside stream capture.  No counterpart in the reference (its torch ops
+/* The current device's error bits as the kernels mirror them into page-locked
+ * host memory: reads host memory only (no synchronisation), so a caller can
+ * check it before every call.  Reflects the kernels that have finished: a call
+ * that failed on the device shows up here once its kernels have run (and
+ * gdn_device_error(1) then returns and clears the bits).  The mirror is a page
+ * of this library's host data, page-locked and mapped into each device by the
+ * first call on that device that sets up the error word (the chunked forward
+ * and its variants, the backward, the self-test below), which also writes the
+ * mirror's address to the device with one synchronous copy: make that first
+ * call before any stream capture.  Returns 0 before that call, or if the page
+ * could not be page-locked.  No counterpart in the reference (its torch ops
  * raise synchronously). */
-GDN_API int gdn_set_error_mirror(unsigned int* host_word);
-
-/* The current device's mirrored error bits (0 without a mirror).  Reads host
- * memory only: no CUDA call, no synchronisation.  Reflects the kernels that
- * have finished; a call that failed on the device shows up here once its
- * kernels have run, so a caller checks it before its next call (and
- * gdn_device_error(1) then returns and clears the bits). */
 GDN_API unsigned int gdn_device_error_pending(void);
 
 /* Test hook: launches one kernel on `stream` whose bounded wait on a barrier

@@ -65,10 +65,14 @@ SIGNATURES = {
                                      c_void_p]),
     "gdn_chunk_sp_finish": (c_int, [_P, _P, _P, _P, _P, c_int, c_void_p, c_int, c_int, _P, c_void_p, c_void_p,
                                     c_size_t, c_void_p]),
+    "gdn_model_add_rms_norm": (c_int, [_P, _P, _P, ctypes.c_float, _P, _P, c_void_p]),
+    "gdn_model_attn_prep": (c_int, [_P, _P, _P, c_void_p, c_void_p, c_int, c_void_p, ctypes.c_float, _P, _P, _P,
+                                    c_void_p]),
+    "gdn_model_attention": (c_int, [_P, _P, _P, _P, c_void_p, _P, c_void_p]),
+    "gdn_model_silu_mul": (c_int, [_P, _P, c_void_p]),
     "gdn_launch_count": (ctypes.c_uint64, []),
     "gdn_set_phase_events": (None, [ctypes.POINTER(c_void_p), c_int]),
     "gdn_device_error": (ctypes.c_uint, [c_int]),
-    "gdn_set_error_mirror": (c_int, [c_void_p]),
     "gdn_device_error_pending": (ctypes.c_uint, []),
     "gdn_selftest_bounded_wait": (c_int, [ctypes.c_uint64, c_void_p]),
     "gdn_last_error": (c_char_p, []),

@@ -92,6 +92,34 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     return LIB
 
 
+TORCH_OPS_SRC = os.path.join(CSRC, "gdn_torch_ops.cpp")
+TORCH_OPS_LIB = os.path.join(PKG, "libgdn_torch_ops.so")
+
+
+def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
+    """Compile the PyTorch operator library (torch.ops.gdn.*, ``csrc/gdn_torch_ops.cpp``) against the
+    installed torch and link it to ``libgdn_b200.so`` (found next to it at run time)."""
+    import torch
+    from torch.utils import cpp_extension as ce
+    deps = [TORCH_OPS_SRC, LIB, os.path.join(INCLUDE, "gdn_b200.h")]
+    if not force and os.path.exists(TORCH_OPS_LIB) and os.path.getmtime(TORCH_OPS_LIB) >= _newest(deps):
+        return TORCH_OPS_LIB
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "c++"
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}"]
+    cmd += [f"-I{p}" for p in ce.include_paths(device_type="cuda")] + ["-I" + INCLUDE, TORCH_OPS_SRC,
+                                                                        "-o", TORCH_OPS_LIB]
+    cmd += [f"-L{p}" for p in ce.library_paths(device_type="cuda")] + ["-L" + PKG, "-lgdn_b200", "-lc10", "-lc10_cuda",
+                                                                       "-ltorch", "-ltorch_cpu", "-ltorch_cuda",
+                                                                       "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch operator library build failed:\n{r.stdout}\n{r.stderr}")
+    return TORCH_OPS_LIB
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -99,4 +127,5 @@ if __name__ == "__main__":
     ap.add_argument("--ptxas-info", action="store_true", help="print registers / spills / smem per kernel")
     a = ap.parse_args()
     print(build(force=a.force, verbose=a.verbose, ptxas_info=a.ptxas_info))
+    print(build_torch_ops(force=a.force, verbose=a.verbose))
     sys.exit(0)

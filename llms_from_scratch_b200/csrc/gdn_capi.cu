@@ -20,12 +20,36 @@ namespace {
 thread_local std::string g_last_error;
 
 // Sticky device error word: bounded waits inside the kernels that give up OR a
-// bit in here (gdn_internal.h) instead of hanging or trapping; with a host
-// mirror registered (gdn_set_error_mirror) they also set it in host memory.
+// bit in here (gdn_internal.h) instead of hanging or trapping, and also store it
+// in a page-locked host mirror, so gdn_device_error_pending() can report it
+// without synchronising.  The mirror is a page of this library's own host data
+// (one word per device ordinal), page-locked and mapped into every device on the
+// first call that needs an error word; its device address is written into the
+// device word's `host_mirror` field then, once per device.
 __device__ gdn::DeviceErrorWord g_device_error;
 std::mutex g_err_mu;
 void* g_device_error_addr[64];
-unsigned int* g_error_mirror[64];  // host address of each device's mirror word, or null
+alignas(4096) unsigned int g_mirror_page[1024];  // host words; [dev] mirrors device `dev`
+bool g_mirror_tried = false, g_mirror_ok = false;
+bool g_mirror_on[64];
+
+// With g_err_mu held: the device address of device `dev`'s mirror word, or null if the page could not be
+// page-locked (the error word then works without a host mirror).
+unsigned int* mirror_alias(int dev) {
+    if (!g_mirror_tried) {
+        g_mirror_tried = true;
+        g_mirror_ok = cudaHostRegister(g_mirror_page, sizeof(g_mirror_page),
+                                       cudaHostRegisterPortable | cudaHostRegisterMapped) == cudaSuccess;
+        if (!g_mirror_ok) cudaGetLastError();  // a failed registration leaves a (non-sticky) error behind
+    }
+    if (!g_mirror_ok) return nullptr;
+    void* d = nullptr;
+    if (cudaHostGetDevicePointer(&d, &g_mirror_page[dev], 0) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return reinterpret_cast<unsigned int*>(d);
+}
 
 unsigned int* device_error_word(int dev) {
     if (dev < 0 || dev >= 64) return nullptr;
@@ -33,6 +57,15 @@ unsigned int* device_error_word(int dev) {
     if (!g_device_error_addr[dev]) {
         void* ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
+        unsigned int* alias = mirror_alias(dev);
+        if (alias) {
+            unsigned char* field = reinterpret_cast<unsigned char*>(ptr) + offsetof(gdn::DeviceErrorWord, host_mirror);
+            if (cudaMemcpy(field, &alias, sizeof(alias), cudaMemcpyHostToDevice) == cudaSuccess) {
+                g_mirror_on[dev] = true;
+            } else {
+                cudaGetLastError();
+            }
+        }
         g_device_error_addr[dev] = ptr;
     }
     return reinterpret_cast<unsigned int*>(g_device_error_addr[dev]);
@@ -557,58 +590,20 @@ unsigned int gdn_device_error(int clear) {
     if (!w) return 0;
     unsigned int v = 0;
     if (cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
-    unsigned int* mirror = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(g_err_mu);
-        mirror = g_error_mirror[dev];
-    }
-    if (mirror) v |= *reinterpret_cast<volatile unsigned int*>(mirror);
+    volatile unsigned int* mirror = g_mirror_on[dev] ? &g_mirror_page[dev] : nullptr;
+    if (mirror) v |= *mirror;
     if (clear && v) {
         const unsigned int zero = 0;
         cudaMemcpy(w, &zero, sizeof(zero), cudaMemcpyHostToDevice);
-        if (mirror) *reinterpret_cast<volatile unsigned int*>(mirror) = 0;
+        if (mirror) *mirror = 0;
     }
     return v;
-}
-
-int gdn_set_error_mirror(unsigned int* host_word) {
-    g_last_error.clear();
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    if (dev < 0 || dev >= 64) return fail(GDN_ERR_DEVICE, "device ordinal %d out of range", dev);
-    unsigned int* w = device_error_word(dev);
-    if (!w) return fail(GDN_ERR_CUDA, "device error word not found");
-    unsigned int* dev_alias = nullptr;
-    if (host_word) {
-        if (reinterpret_cast<uintptr_t>(host_word) & 3)
-            return fail(GDN_ERR_INVALID_ARGUMENT, "host_word must be 4-byte aligned");
-        e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev_alias), host_word, 0);
-        if (e != cudaSuccess || !dev_alias) {
-            cudaGetLastError();  // a failed query leaves a (non-sticky) error behind: clear it
-            return fail(GDN_ERR_INVALID_ARGUMENT,
-                        "host_word must be page-locked host memory mapped into device %d (cudaHostAlloc, or "
-                        "cudaHostRegister with cudaHostRegisterMapped): %s", dev, cudaGetErrorString(e));
-        }
-        *reinterpret_cast<volatile unsigned int*>(host_word) = 0;
-    }
-    unsigned char* field = reinterpret_cast<unsigned char*>(w) + offsetof(gdn::DeviceErrorWord, host_mirror);
-    e = cudaMemcpy(field, &dev_alias, sizeof(dev_alias), cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) return cuda_fail(e, "error mirror registration");
-    std::lock_guard<std::mutex> lock(g_err_mu);
-    g_error_mirror[dev] = host_word;
-    return GDN_OK;
 }
 
 unsigned int gdn_device_error_pending(void) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-    unsigned int* mirror;
-    {
-        std::lock_guard<std::mutex> lock(g_err_mu);
-        mirror = g_error_mirror[dev];
-    }
-    return mirror ? *reinterpret_cast<volatile unsigned int*>(mirror) : 0u;
+    return g_mirror_on[dev] ? *reinterpret_cast<volatile unsigned int*>(&g_mirror_page[dev]) : 0u;
 }
 
 int gdn_selftest_bounded_wait(uint64_t timeout_ns, void* stream) {

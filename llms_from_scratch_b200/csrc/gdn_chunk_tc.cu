@@ -47,6 +47,8 @@
 //   the next state has been handed over, while the next chunk's MMAs run.
 #include <cuda_bf16.h>
 
+#include <atomic>
+
 #include "gdn_bwd.cuh"
 #include "gdn_common.cuh"
 #include "gdn_internal.h"
@@ -2268,9 +2270,24 @@ cudaError_t launch_varlen_tables(const ChunkParams& p, cudaStream_t stream) {
     return e;
 }
 
+// cudaFuncSetAttribute once per (kernel, device): the per-call host path stays short and free of
+// calls that stream capture might refuse.
+template <typename Kernel>
+cudaError_t smem_attr_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done_mask) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done_mask.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done_mask.fetch_or(bit, std::memory_order_release);
+    return e;
+}
+
 cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream) {
     static_assert(P_SMEM <= 227 * 1024, "shared memory budget");
-    cudaError_t e = cudaFuncSetAttribute(gdn_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P_SMEM);
+    static std::atomic<uint64_t> attr_done{0};
+    cudaError_t e = smem_attr_once(gdn_prep_tc, (int)P_SMEM, attr_done);
     if (e != cudaSuccess) return e;
     const int64_t nchunks = p.cu_seqlens ? (int64_t)p.max_chunks * p.H : (int64_t)p.B * p.H * p.NC;
     gdn_prep_tc<<<(unsigned)nchunks, kPrepThreads, P_SMEM, stream>>>(p);
@@ -2283,7 +2300,8 @@ namespace {
 template <int kW>
 cudaError_t launch_scan_w(const ChunkParams& p, cudaStream_t stream) {
     using L = ScanLayout<kW>;
-    cudaError_t e = cudaFuncSetAttribute(gdn_scan_tc<kW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmem);
+    static std::atomic<uint64_t> attr_done{0};
+    cudaError_t e = smem_attr_once(gdn_scan_tc<kW>, (int)L::kSmem, attr_done);
     if (e != cudaSuccess) return e;
     const dim3 grid = p.cu_seqlens ? dim3((unsigned)(p.N * p.H * L::kSlices), 1)
                                    : dim3((unsigned)(p.B * p.H), (p.scan_mode == 1 ? 2 : 1) * L::kSlices);

@@ -247,16 +247,22 @@ __global__ void __launch_bounds__(256) gdn_gates_kernel(GateParams p) {
 }
 
 struct NormParams {
-    const void* x;      // [N, D] rows
+    const void* x;      // rows of D; row r = (group r / H, head r % H) at (r / H) * x_sg + (r % H) * x_sr
     int64_t x_sr;
-    const void* gate;   // [N, D]
+    const void* gate;
     int64_t g_sr;
     const void* w;      // [D]
-    void* out;          // [N, D]
+    void* out;
     int64_t o_sr;
-    int64_t N;
+    int64_t N;          // rows
     float eps;
+    int64_t x_sg, g_sg, o_sg;  // group strides ([M, H, D] views; == the row strides for [N, D] views)
+    int H;              // rows per group (1 for [N, D] views)
 };
+
+__device__ __forceinline__ int64_t norm_row_offset(int64_t r, int H, int64_t s_group, int64_t s_row) {
+    return H == 1 ? r * s_row : (r / H) * s_group + (r % H) * s_row;
+}
 
 constexpr int kNormD = 128;  // head_v_dim
 
@@ -284,8 +290,10 @@ __global__ void __launch_bounds__(256) gdn_rms_norm_gated_vec_kernel(NormParams 
     const int64_t row = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * RPW + sub;
     const bool live = row < p.N;
     const int64_t r = live ? row : 0;
-    const uint4 xu = *reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(p.x) + r * p.x_sr + V * l);
-    const uint4 gu = *reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(p.gate) + r * p.g_sr + V * l);
+    const uint4 xu = *reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(p.x) +
+                                                      norm_row_offset(r, p.H, p.x_sg, p.x_sr) + V * l);
+    const uint4 gu = *reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(p.gate) +
+                                                      norm_row_offset(r, p.H, p.g_sg, p.g_sr) + V * l);
     const uint4 wu = *reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(p.w) + V * l);
     const E* xe = reinterpret_cast<const E*>(&xu);
     const E* ge = reinterpret_cast<const E*>(&gu);
@@ -308,7 +316,7 @@ __global__ void __launch_bounds__(256) gdn_rms_norm_gated_vec_kernel(NormParams 
     E* oe = reinterpret_cast<E*>(&ou);
 #pragma unroll
     for (int e = 0; e < V; ++e) oe[e] = Elem<E>::st(o[e]);
-    *reinterpret_cast<uint4*>(reinterpret_cast<E*>(p.out) + row * p.o_sr + V * l) = ou;
+    *reinterpret_cast<uint4*>(reinterpret_cast<E*>(p.out) + norm_row_offset(row, p.H, p.o_sg, p.o_sr) + V * l) = ou;
 }
 
 // Scalar form for rows that are not 16-byte aligned: one warp per row, 4 elements per lane.
@@ -317,8 +325,8 @@ __global__ void __launch_bounds__(256) gdn_rms_norm_gated_kernel(NormParams p) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (row >= p.N) return;
-    const E* xr = reinterpret_cast<const E*>(p.x) + row * p.x_sr + 4 * lane;
-    const E* gr = reinterpret_cast<const E*>(p.gate) + row * p.g_sr + 4 * lane;
+    const E* xr = reinterpret_cast<const E*>(p.x) + norm_row_offset(row, p.H, p.x_sg, p.x_sr) + 4 * lane;
+    const E* gr = reinterpret_cast<const E*>(p.gate) + norm_row_offset(row, p.H, p.g_sg, p.g_sr) + 4 * lane;
     const E* wr = reinterpret_cast<const E*>(p.w) + 4 * lane;
     float h[4], z[4], w[4];
     float ss = 0.f;
@@ -332,7 +340,7 @@ __global__ void __launch_bounds__(256) gdn_rms_norm_gated_kernel(NormParams p) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float inv = rsqrtf(ss * (1.0f / kNormD) + p.eps);
-    E* orow = reinterpret_cast<E*>(p.out) + row * p.o_sr + 4 * lane;
+    E* orow = reinterpret_cast<E*>(p.out) + norm_row_offset(row, p.H, p.o_sg, p.o_sr) + 4 * lane;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         const float n = Elem<E>::rnd(h[e] * inv);
@@ -537,19 +545,28 @@ int gdn_gates(const gdn_tensor* a, const gdn_tensor* b, const gdn_tensor* A_log,
 int gdn_rms_norm_gated(const gdn_tensor* x, const gdn_tensor* gate, const gdn_tensor* weight, float eps,
                        gdn_tensor* out, void* stream) {
     int rc;
-    const int64_t rows[2] = {-1, gdn::kNormD};
-    if ((rc = gdn::check_view("x", x, 2, rows))) return rc;
-    const int64_t shp[2] = {x->shape[0], gdn::kNormD};
+    if (!x) return gdn::set_last_error(GDN_ERR_INVALID_ARGUMENT, "x is NULL");
+    const int nd = x->ndim;
+    if (nd != 2 && nd != 3)
+        return gdn::set_last_error(GDN_ERR_INVALID_ARGUMENT, "x must be [N,128] or [M,H,128], got ndim=%d", nd);
+    const int64_t rows2[2] = {-1, gdn::kNormD};
+    const int64_t rows3[3] = {-1, -1, gdn::kNormD};
+    if ((rc = gdn::check_view("x", x, nd, nd == 2 ? rows2 : rows3))) return rc;
+    const int64_t shp[3] = {x->shape[0], x->shape[1], nd == 2 ? -1 : gdn::kNormD};
     const int64_t wshape[1] = {gdn::kNormD};
-    if ((rc = gdn::check_view("gate", gate, 2, shp)) || (rc = gdn::check_view("weight", weight, 1, wshape)) ||
-        (rc = gdn::check_view("out", out, 2, shp)))
+    if ((rc = gdn::check_view("gate", gate, nd, shp)) || (rc = gdn::check_view("weight", weight, 1, wshape)) ||
+        (rc = gdn::check_view("out", out, nd, shp)))
         return rc;
     if (gate->dtype != x->dtype || weight->dtype != x->dtype || out->dtype != x->dtype)
         return gdn::set_last_error(GDN_ERR_UNSUPPORTED, "x, gate, weight and out must share one dtype");
     if (!(eps >= 0.f)) return gdn::set_last_error(GDN_ERR_INVALID_ARGUMENT, "eps must be >= 0");
-    if (x->shape[0] == 0) return GDN_OK;
-    gdn::NormParams p{x->data, x->stride[0], gate->data, gate->stride[0], weight->data, out->data, out->stride[0],
-                      x->shape[0], eps};
+    const int64_t H = nd == 2 ? 1 : x->shape[1];
+    const int64_t N = x->shape[0] * H;
+    if (N == 0) return GDN_OK;
+    if (H > 0x7fffffffLL) return gdn::set_last_error(GDN_ERR_INVALID_ARGUMENT, "x: too many rows per group");
+    const int r = nd - 2;  // index of the row-stride dim
+    gdn::NormParams p{x->data, x->stride[r], gate->data, gate->stride[r], weight->data, out->data, out->stride[r],
+                      N, eps, x->stride[0], gate->stride[0], out->stride[0], (int)H};
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     gdn::phase_event(0, st);
     const bool vec = gdn::vec16(x) && gdn::vec16(gate) && gdn::vec16(out) && gdn::vec16(weight);

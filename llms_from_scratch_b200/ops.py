@@ -20,6 +20,7 @@ path: without a CUDA device, CPU tensors raise.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Optional, Tuple
 
 import torch
@@ -79,36 +80,35 @@ def _state_in(initial_state: Optional[torch.Tensor], B, H, Dk, Dv, device) -> Op
 
 _ERROR_BITS = {1: "a chunk prep wait timed out", 2: "a chunk scan wait timed out",
                8: "packed-sequence offsets were not a valid cu_seqlens", 16: "bounded-wait self-test"}
-_error_mirrors: dict = {}  # device index -> page-locked int32 word the library mirrors the error bits into
 
 
-def check_device_errors(device: Optional[torch.device] = None) -> None:
-    """Raise ``GDNError`` (``GDN_ERR_KERNEL``) if a kernel on ``device`` (default: the current one) reported a
-    failure in the library's device error word, and clear the word.
-
-    Every op calls this before it launches.  The first call on a device registers a page-locked host mirror
-    of the word (``gdn_set_error_mirror``, one synchronous copy; make it before any stream capture); later
-    checks read that host word only, so they cost no synchronisation.  A failure therefore surfaces at the
-    next op on the device, or here once the failing call has finished on the device (synchronise first to
-    check the latest call)."""
-    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
-    lib = _lib.load()
-    with torch.cuda.device(dev):
-        word = _error_mirrors.get(dev.index)
-        if word is None:
-            word = torch.zeros(1, dtype=torch.int32, pin_memory=True)
-            _lib.check(lib.gdn_set_error_mirror(word.data_ptr()))
-            _error_mirrors[dev.index] = word
-            bits = lib.gdn_device_error(1)  # anything reported before the mirror existed
-        else:
-            bits = lib.gdn_device_error_pending()
-            if bits:
-                bits = lib.gdn_device_error(1)
+def _raise_pending(lib, dev: torch.device) -> None:
+    """With ``dev`` current: raise GDNError (GDN_ERR_KERNEL) if the library's host mirror of the device error
+    word shows a failure (one host read, no synchronisation), clearing the word."""
+    bits = lib.gdn_device_error_pending()
     if bits:
+        bits = lib.gdn_device_error(1) or bits
         what = "; ".join(v for b, v in _ERROR_BITS.items() if bits & b) or "unknown"
         raise _lib.GDNError(_lib.GDN_ERR_KERNEL, "GDN_ERR_KERNEL",
                             f"a kernel on {dev} reported device error bits 0x{bits:x} ({what}); the outputs of "
                             "the call that launched it are not valid")
+
+
+def check_device_errors(device: Optional[torch.device] = None, sync: bool = False) -> None:
+    """Raise ``GDNError`` (``GDN_ERR_KERNEL``) if a kernel on ``device`` (default: the current one) reported a
+    failure in the library's device error word, and clear the word.
+
+    Every op runs this check before it launches: it reads the page-locked host mirror the kernels write their
+    error bits into, so it costs no synchronisation, and a failure surfaces at the next op on the device.
+    ``sync=True`` first waits for the device, so the latest call's kernels are covered too."""
+    dev = torch.device(device) if device is not None else None
+    if dev is None or dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        if sync:
+            torch.cuda.synchronize(dev)
+        _raise_pending(lib, dev)
 
 
 def _workspace(workspace: Optional[torch.Tensor], need: int, dev: torch.device) -> torch.Tensor:
@@ -121,6 +121,37 @@ def _workspace(workspace: Optional[torch.Tensor], need: int, dev: torch.device) 
         if workspace.numel() * workspace.element_size() >= need and workspace.is_contiguous():
             return workspace
     return torch.empty((max(need, 1),), dtype=torch.uint8, device=dev)
+
+
+TORCH_OPS_PATH = os.path.join(os.path.dirname(_lib.LIB_PATH), "libgdn_torch_ops.so")
+_torch_ops_loaded: Optional[bool] = None
+
+
+def _torch_ops() -> bool:
+    """Load (once) the PyTorch operator library (torch.ops.gdn.chunk_fwd / decode_step, built beside
+    libgdn_b200.so by ``build``); False if it was not built, in which case the ops call the C ABI through
+    ctypes.  Both routes run the same kernels through the same C entry points."""
+    global _torch_ops_loaded
+    if _torch_ops_loaded is None:
+        _lib.load()  # the operator library links libgdn_b200.so: the same loaded instance serves both
+        _torch_ops_loaded = os.path.exists(TORCH_OPS_PATH)
+        if _torch_ops_loaded:
+            torch.ops.load_library(TORCH_OPS_PATH)
+    return _torch_ops_loaded
+
+
+_STATUS = {"GDN_ERR_INVALID_ARGUMENT": _lib.GDN_ERR_INVALID_ARGUMENT, "GDN_ERR_UNSUPPORTED": _lib.GDN_ERR_UNSUPPORTED,
+           "GDN_ERR_WORKSPACE": _lib.GDN_ERR_WORKSPACE, "GDN_ERR_CUDA": _lib.GDN_ERR_CUDA,
+           "GDN_ERR_DEVICE": _lib.GDN_ERR_DEVICE, "GDN_ERR_KERNEL": _lib.GDN_ERR_KERNEL}
+
+
+def _op_error(e: RuntimeError) -> RuntimeError:
+    """A torch.ops.gdn error as the GDNError the C ABI status names (argument errors stay RuntimeError)."""
+    msg = str(e).split("\nException raised from")[0].strip()
+    name, _, rest = msg.partition(": ")
+    if name in _STATUS:
+        return _lib.GDNError(_STATUS[name], name, rest)
+    return RuntimeError(msg)
 
 
 def _check_backend(backend: str) -> None:
@@ -162,6 +193,13 @@ def fast_chunk_gated_delta_rule(
     if isinstance(query, torch.Tensor) and query.device.type == "cpu":
         return _chunk_from_host(query, key, value, g, beta, chunk_size, initial_state, output_final_state,
                                 use_qk_l2norm_in_kernel, workspace, slice_tokens)
+    if isinstance(query, torch.Tensor) and query.is_cuda and _torch_ops():
+        try:
+            out, final = torch.ops.gdn.chunk_fwd(query, key, value, g, beta, int(chunk_size), initial_state,
+                                                 bool(output_final_state), bool(use_qk_l2norm_in_kernel), workspace)
+        except RuntimeError as e:
+            raise _op_error(e) from None
+        return out, (final if output_final_state else None)
     q = _as_kernel_tensor(query, "query", 4)
     k = _as_kernel_tensor(key, "key", 4)
     v = _as_kernel_tensor(value, "value", 4)
@@ -179,7 +217,7 @@ def fast_chunk_gated_delta_rule(
     final = torch.empty((B, H, Dk, Dv), dtype=torch.float32, device=dev) if output_final_state else None
     lib = _lib.load()
     with torch.cuda.device(dev):
-        check_device_errors(dev)
+        _raise_pending(lib, dev)
         ws_bytes = lib.gdn_chunk_workspace_bytes(B, T, H, Dk, Dv, _DTYPES[q.dtype])
         workspace = _workspace(workspace, ws_bytes, dev)
         dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
@@ -243,7 +281,7 @@ def _chunk_from_host(query, key, value, g, beta, chunk_size, initial_state, outp
     dev = torch.device("cuda", torch.cuda.current_device())
     lib = _lib.load()
     with torch.cuda.device(dev):
-        check_device_errors(dev)
+        _raise_pending(lib, dev)
         need = lib.gdn_chunk_host_workspace_bytes(B, T, H, Dk, Dv, _DTYPES[q.dtype], int(slice_tokens))
         workspace = _workspace(workspace, need, dev)
         dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
@@ -277,6 +315,13 @@ def fast_recurrent_gated_delta_rule(
     optionally names an fp32 ``[B,H,Dk,Dv]`` tensor to receive the final state;
     it may be ``initial_state`` itself for an in-place decode update.
     """
+    if isinstance(query, torch.Tensor) and query.is_cuda and _torch_ops():
+        try:
+            out, final = torch.ops.gdn.decode_step(query, key, value, g, beta, initial_state, bool(output_final_state),
+                                                   bool(use_qk_l2norm_in_kernel), out_state)
+        except RuntimeError as e:
+            raise _op_error(e) from None
+        return out, (final if output_final_state else None)
     q = _as_kernel_tensor(query, "query", 4)
     k = _as_kernel_tensor(key, "key", 4)
     v = _as_kernel_tensor(value, "value", 4)
@@ -299,7 +344,7 @@ def fast_recurrent_gated_delta_rule(
             final = torch.empty((B, H, Dk, Dv), dtype=torch.float32, device=dev)
     lib = _lib.load()
     with torch.cuda.device(dev):
-        check_device_errors(dev)
+        _raise_pending(lib, dev)
         dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
         stream = torch.cuda.current_stream(dev).cuda_stream
         rc = lib.gdn_recurrent_gated_delta_rule(
@@ -354,7 +399,7 @@ def chunk_gated_delta_rule_varlen(
     final = torch.empty((N, H, Dk, Dv), dtype=torch.float32, device=q.device) if output_final_state else None
     lib = _lib.load()
     with torch.cuda.device(q.device):
-        check_device_errors(q.device)
+        _raise_pending(lib, q.device)
         need = lib.gdn_chunk_varlen_workspace_bytes(T, max(N, 1), H, Dk, Dv, _DTYPES[q.dtype])
         workspace = _workspace(workspace, need, q.device)
         dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
@@ -414,7 +459,7 @@ def chunk_gated_delta_rule_bwd(
     dh0 = torch.empty((B, H, Dk, Dv), dtype=torch.float32, device=dev) if initial_state is not None else None
     lib = _lib.load()
     with torch.cuda.device(dev):
-        check_device_errors(dev)
+        _raise_pending(lib, dev)
         need = lib.gdn_chunk_bwd_workspace_bytes(B, T, H, Dk, Dv, _DTYPES[q.dtype])
         workspace = _workspace(workspace, need, dev)
         descs = [_desc(x) for x in (q, k, v, gg, bb, do, dq, dk, dv, dg, db)]

@@ -26,7 +26,7 @@ from typing import Callable, List, Optional, Sequence, Tuple
 import torch
 
 from . import _lib
-from .ops import _DTYPES, _as_kernel_tensor, _desc, _workspace, check_device_errors
+from .ops import _DTYPES, _as_kernel_tensor, _desc, _raise_pending, _workspace
 
 D = 128
 
@@ -77,7 +77,7 @@ def chunk_shard_summary(query, key, value, g, beta, use_qk_l2norm_in_kernel: boo
     M = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device)
     b = torch.empty((B, H, D, D), dtype=torch.float32, device=q.device)
     with torch.cuda.device(q.device):
-        check_device_errors(q.device)
+        _raise_pending(lib, q.device)
         dq, dk, dv, dg, db = (_desc(x) for x in (q, k, v, gg, bb))
         rc = lib.gdn_chunk_sp_summary(ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(dg),
                                       ctypes.byref(db), 64, int(bool(use_qk_l2norm_in_kernel)), M.data_ptr(),
@@ -100,7 +100,7 @@ def chunk_shard_finish(query, key, value, g, beta, initial_state: Optional[torch
     if not isinstance(workspace, torch.Tensor) or workspace.device != q.device:
         raise RuntimeError(f"workspace must be the shard summary's CUDA workspace on {q.device}")
     with torch.cuda.device(q.device):
-        check_device_errors(q.device)
+        _raise_pending(lib, q.device)
         dq, dk, dv, dg, db, do = (_desc(x) for x in (q, k, v, gg, bb, out))
         rc = lib.gdn_chunk_sp_finish(ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(dg),
                                      ctypes.byref(db), 64, h0.data_ptr() if h0 is not None else None,

@@ -284,6 +284,27 @@ def test_workspace_on_the_host_or_another_device_is_rejected():
             _workspace(torch.empty(64, dtype=torch.uint8, device="cuda:1"), 16, dev0)
 
 
+def test_torch_operator_library_registers_the_ops(lib):
+    """torch.ops.gdn.chunk_fwd / decode_step (the drop-in's native entry) load and keep the reference's
+    argument names; with CPU tensors they raise (there is no CPU path)."""
+    import torch
+
+    from llms_from_scratch_b200.build import build_torch_ops
+    from llms_from_scratch_b200.ops import _torch_ops
+    build_torch_ops()
+    assert _torch_ops()
+    schema = str(torch.ops.gdn.chunk_fwd.default._schema)
+    for arg in ("Tensor query", "Tensor key", "Tensor value", "Tensor g", "Tensor beta", "int chunk_size=64",
+                "Tensor? initial_state=None", "bool output_final_state=False", "bool use_qk_l2norm_in_kernel=False"):
+        assert arg in schema, (arg, schema)
+    assert "Tensor(a!)? out_state" in str(torch.ops.gdn.decode_step.default._schema)
+    q, g = torch.zeros(1, 4, 1, 128), torch.zeros(1, 4, 1)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        torch.ops.gdn.chunk_fwd(q, q, q, g, g)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        torch.ops.gdn.decode_step(q, q, q, g, g, None, False)
+
+
 def test_status_names_cover_every_status(lib):
     names = [lib.gdn_status_name(i).decode() for i in range(7)]
     assert names[6] == "GDN_ERR_KERNEL" and "GDN_UNKNOWN_STATUS" not in names

@@ -45,7 +45,7 @@ def test_timed_out_wait_raises_at_the_next_call_and_the_context_survives():
     from llms_from_scratch_b200 import _lib
     from llms_from_scratch_b200.ops import check_device_errors
     lib = _lib.load()
-    check_device_errors()  # registers the host mirror; nothing pending
+    check_device_errors(sync=True)  # nothing pending
     assert lib.gdn_device_error_pending() == 0
     stream = torch.cuda.current_stream()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -77,7 +77,7 @@ def run_rec(q, k, v, g, beta, state, in_dtype, l2=True, ofs=True):
 
 
 GOLDEN_FILES = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
-                      if not os.path.basename(p).startswith(("config1", "layer_", "bwd_")))  # layer_*, bwd_*: own tests
+                      if not os.path.basename(p).startswith(("config1", "layer_", "bwd_", "model_")))  # layer_*, bwd_*, model_*: own tests
 
 
 @pytest.mark.parametrize("path", GOLDEN_FILES, ids=[os.path.basename(p)[:-4] for p in GOLDEN_FILES])

@@ -14,7 +14,7 @@ from oracle import gdn_oracle as O
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 CASES = sorted(p for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
-               if not os.path.basename(p).startswith(("config1", "layer_", "bwd_")))  # layer_*, bwd_*: their own tests
+               if not os.path.basename(p).startswith(("config1", "layer_", "bwd_", "model_")))  # layer_*, bwd_*, model_*: their own tests
 
 
 def _load(path):
