@@ -93,15 +93,20 @@ def causal_conv1d_update(hidden_states: torch.Tensor, conv_state: torch.Tensor, 
         raise RuntimeError(f"activation {activation!r} is not supported; the layer uses 'silu'")
     x = _cuda(hidden_states.transpose(1, 2), "hidden_states")
     w = _cuda(weight, "weight")
-    if conv_state.device != x.device or conv_state.stride(-1) != 1:
-        raise RuntimeError("conv_state must be a CUDA tensor [B, C, 4] on the input's device with a contiguous last dim")
+    if not isinstance(conv_state, torch.Tensor) or conv_state.device != x.device:
+        raise RuntimeError("conv_state must be a CUDA tensor [B, C, 4] on the input's device")
+    # The layer's prefill keeps F.pad(mixed_qkv, ...) as the state (:346-348), which can be a strided view; the
+    # kernel updates a contiguous state, so such a view is updated through a copy (still in place for the caller).
+    state = conv_state if conv_state.stride(-1) == 1 else conv_state.contiguous()
     out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
     lib = _lib.load()
     with torch.cuda.device(x.device):
-        dx, ds, dw, do = _desc(x), _desc(conv_state), _desc(w), _desc(out)
+        dx, ds, dw, do = _desc(x), _desc(state), _desc(w), _desc(out)
         rc = lib.gdn_causal_conv1d_update(ctypes.byref(dx), ctypes.byref(ds), ctypes.byref(dw), ctypes.byref(do),
                                           _stream(x.device))
         _lib.check(rc)
+    if state is not conv_state:
+        conv_state.copy_(state)
     return out.transpose(1, 2)
 
 
