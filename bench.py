@@ -662,11 +662,16 @@ def decode_model_leg(torch, device, peak, batches=(1, 32), steps=200, prompt_len
         ms_tok = decode_ms / steps
         # kernel shares from a profiled eager pass of 8 decode steps (the same kernels the graph replays)
         share, rec_us = _decode_kernel_shares(torch, dec, cache, prompt, 8)
-        rec_bytes = B * cfg["linear_num_value_heads"] * (2 * STATE_BYTES + 4 * D * 2 + 8)
+        # per (sequence, head): the fp32 state in and out; its 3 x 128 conv channels (4 bf16 taps in and out,
+        # 4 weights, the new input); z and the output row; g/beta inputs
+        Hh = cfg["linear_num_value_heads"]
+        rec_bytes = B * Hh * (2 * STATE_BYTES + 384 * (8 + 8 + 8 + 2) + 2 * D * 2 + 4)
         res[f"batch{B}"] = {
             "tok_s": B * steps / (decode_ms / 1e3), "ms_per_token": ms_tok, "prefill_ms": prefill_ms,
             "kernel_share": share,
-            "recurrent_kernel": {"us_per_layer": rec_us, "bytes_per_layer": rec_bytes,
+            "recurrent_kernel": {"kernel": "gdn_model_gdn_decode_kernel (conv update + gates + recurrent rule + "
+                                           "gated norm, one token)", "us_per_layer": rec_us,
+                                 "bytes_per_layer": rec_bytes,
                                  "achieved_gbs": rec_bytes / (rec_us / 1e6) / 1e9 if rec_us else None,
                                  "frac_hbm": rec_bytes / (rec_us / 1e6) / 1e9 / peak if rec_us else None,
                                  "layers_per_step": n_gdn},
@@ -697,11 +702,12 @@ def _decode_kernel_shares_inner(torch, dec, cache, prompt, n):
         for _ in range(n):
             tok = dec.decode_step(tok, cache).argmax(-1)
         torch.cuda.synchronize()
-    fam = {"recurrent (gdn_recurrent_kernel)": ("gdn_recurrent",), "GEMM (cuBLAS)": ("gemm", "gemv", "nvjet", "cutlass",
-                                                                                    "sm100", "xmma"),
+    fam = {"GatedDeltaNet decode (gdn_model_gdn_decode: conv update, gates, recurrent rule, gated norm)":
+               ("gdn_model_gdn_decode", "gdn_recurrent", "conv_update", "gates_kernel", "rms_norm_gated"),
+           "projections (gdn_model_gemm_kernel; cuBLAS for the prefill)": ("gemm", "gemv", "nvjet", "cutlass", "sm100",
+                                                                           "xmma"),
            "attention (gdn_model_attention + attn_prep)": ("gdn_model_attention", "gdn_model_attn_prep"),
-           "norms (add_rms_norm, gated norm)": ("add_rms_norm", "rms_norm_gated"),
-           "conv update + gates": ("conv_update", "gates_kernel"), "silu_mul": ("silu_mul",)}
+           "residual add + RMSNorm (gdn_model_add_rms_norm)": ("add_rms_norm",), "silu_mul": ("silu_mul",)}
     tot, by, rec = 0.0, {k: 0.0 for k in fam}, []
     by["other (embedding, argmax, copies)"] = 0.0
     for e in prof.events():
@@ -716,7 +722,7 @@ def _decode_kernel_shares_inner(torch, dec, cache, prompt, n):
                 break
         else:
             by["other (embedding, argmax, copies)"] += t
-        if "gdn_recurrent" in name:
+        if "gdn_model_gdn_decode" in name or "gdn_recurrent" in name:
             rec.append(t)
     share = {k: v / tot for k, v in by.items()} if tot else {}
     return share, (statistics.mean(rec) if rec else None)

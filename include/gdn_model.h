@@ -39,6 +39,42 @@ extern "C" {
 GDN_API int gdn_model_add_rms_norm(const gdn_tensor* x, const gdn_tensor* residual, const gdn_tensor* weight, float eps,
                                    gdn_tensor* out, gdn_tensor* residual_out, void* stream);
 
+/* gdn_model_add_rms_norm with x given as the fp32 partial sums of a split-K projection
+ * (gdn_model_linear, GDN_MODEL_EPI_PARTIAL): x = bf16(sum over the nsplit planes [nsplit][rows][dim], in
+ * plane order), the bf16 output the reference's Linear rounds to. */
+GDN_API int gdn_model_add_rms_norm_partials(const float* partial, int nsplit, int64_t rows, int64_t dim,
+                                            const gdn_tensor* residual, const gdn_tensor* weight, float eps,
+                                            gdn_tensor* out, gdn_tensor* residual_out, void* stream);
+
+/* A decode-step projection, out = x W^T (the reference's bias-free bf16 nn.Linear, qwen3_5.py:38-40,
+ * :131-134; qwen3_5_transformers.py:252-300), for x [M, K] with M <= 32 (the decode batch; prefill
+ * projections use a library GEMM) and W [N, K] read once: W's rows stream through the tensor cores
+ * (mma.sync m16n8k16) with K split over the warps of a CTA; N a multiple of 16, K of 64.  epilogue:
+ *   GDN_MODEL_EPI_STORE     out [M, N] bf16;
+ *   GDN_MODEL_EPI_SILU_MUL  W holds fc1 and fc2 interleaved in row groups of 8 (rows 16j..16j+7 = fc1 rows
+ *                           8j..8j+7, rows 16j+8..16j+15 = fc2 rows 8j..8j+7): out [M, N/2] =
+ *                           SiLU(fc1 x) * (fc2 x), rounded as FeedForward rounds it (qwen3_5.py:42-46);
+ *   GDN_MODEL_EPI_PARTIAL   K split over `ksplit` CTAs, fp32 partial sums into partial [ksplit][M][N]
+ *                           (consumed by gdn_model_add_rms_norm_partials); out unused. */
+#define GDN_MODEL_EPI_STORE 0
+#define GDN_MODEL_EPI_SILU_MUL 1
+#define GDN_MODEL_EPI_PARTIAL 2
+GDN_API int gdn_model_linear(const gdn_tensor* x, const gdn_tensor* w, gdn_tensor* out, float* partial, int ksplit,
+                             int epilogue, void* stream);
+
+/* One decode token of a GatedDeltaNet layer after its input projection, fused: the conv update
+ * (torch_causal_conv1d_update, qwen3_5_transformers.py:85-101), the gates (:377-379), the recurrent rule with
+ * q/k l2-normalised (:190-229, :396-410) on the cached state, and the gated RMS norm with z (:56-71, :413-415).
+ *   proj        [B, 3*H*128 + H*128 + 2H]: the layer's fused input projection row (mixed q|k|v, z, b, a)
+ *   conv_state  [B, 3*H*128, 4] updated in place;  conv_w [3*H*128, 4];  A_log, dt_bias [H]
+ *   state       fp32 [B, H, 128, 128] updated in place;  norm_w [128]
+ *   out         [B, H*128]: the normed output (the input of out_proj)
+ * The same roundings as the separate gdn_causal_conv1d_update, gdn_gates, gdn_recurrent_gated_delta_rule and
+ * gdn_rms_norm_gated calls; equal key and value head counts (Qwen3.5: 16 / 16). */
+GDN_API int gdn_model_gdn_decode(const gdn_tensor* proj, gdn_tensor* conv_state, const gdn_tensor* conv_w,
+                                 const gdn_tensor* A_log, const gdn_tensor* dt_bias, float* state,
+                                 const gdn_tensor* norm_w, float eps, gdn_tensor* out, void* stream);
+
 /* Full-attention prologue for T new tokens at positions pos[0] .. pos[0] + T - 1 (pos: one device int32, so
  * a captured decode step can advance it): from the fused projection qkv [B, T, Hq*2*Dh + 2*Hkv*Dh] (per
  * token: Hq blocks of [query Dh | gate Dh] (qwen3_5.py:148-151), then Hkv keys, then Hkv values),

@@ -133,10 +133,20 @@ def _stream(dev) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
-def add_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
+def add_rms_norm(x, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
                  out: Optional[torch.Tensor] = None):
     """``RMSNorm(x + residual)`` with the (1 + weight) scale (``gdn_model_add_rms_norm``); returns
-    ``(normed, x + residual)`` (the new residual stream written into ``residual``) or ``(normed, x)``."""
+    ``(normed, x + residual)`` (the new residual stream written into ``residual``) or ``(normed, x)``.
+    ``x`` may be a ``Partial`` (then ``residual`` is required and shapes follow it)."""
+    if isinstance(x, Partial):
+        ns, rows, D = x.buf.shape
+        r2 = residual.reshape(rows, D)
+        o = torch.empty((rows, D), dtype=residual.dtype, device=residual.device) if out is None else out.reshape(rows, D)
+        dr, dw, do = _desc(r2), _desc(weight), _desc(o)
+        _lib.check(_lib.load().gdn_model_add_rms_norm_partials(x.buf.data_ptr(), ns, rows, D, ctypes.byref(dr),
+                                                               ctypes.byref(dw), float(eps), ctypes.byref(do),
+                                                               ctypes.byref(dr), _stream(residual.device)))
+        return o.reshape(residual.shape), residual
     D = x.shape[-1]
     x2 = x.reshape(-1, D)
     o = torch.empty_like(x2) if out is None else out.reshape(-1, D)
@@ -152,6 +162,44 @@ def add_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Op
                                         None, _stream(x.device))
     _lib.check(rc)
     return o.reshape(x.shape), (residual if residual is not None else x)
+
+
+EPI_STORE, EPI_SILU_MUL, EPI_PARTIAL = 0, 1, 2
+DECODE_MAX_ROWS = 32  # gdn_model_linear's batch limit
+
+
+class Partial:
+    """fp32 split-K partial sums ``[nsplit, rows, dim]`` of a projection, summed (in plane order) and rounded
+    to bf16 by the ``add_rms_norm`` that consumes them."""
+
+    def __init__(self, buf: torch.Tensor):
+        self.buf = buf
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, epilogue: int = EPI_STORE, ksplit: int = 1):
+    """``x [M, K] @ w.T`` for a decode batch (M <= 32) on ``gdn_model_linear``: bf16 ``[M, N]``
+    (``EPI_STORE``), the FFN's ``SiLU(fc1) * fc2`` ``[M, N / 2]`` from fc1/fc2 rows interleaved in groups of 8
+    (``EPI_SILU_MUL``), or a ``Partial`` over ``ksplit`` CTAs along K (``EPI_PARTIAL``)."""
+    M, N = x.shape[0], w.shape[0]
+    lib = _lib.load()
+    dx, dw = _desc(x), _desc(w)
+    if epilogue == EPI_PARTIAL:
+        buf = torch.empty((ksplit, M, N), dtype=torch.float32, device=x.device)
+        _lib.check(lib.gdn_model_linear(ctypes.byref(dx), ctypes.byref(dw), None, buf.data_ptr(), int(ksplit),
+                                        EPI_PARTIAL, _stream(x.device)))
+        return Partial(buf)
+    out = torch.empty((M, N // 2 if epilogue == EPI_SILU_MUL else N), dtype=x.dtype, device=x.device)
+    do = _desc(out)
+    _lib.check(lib.gdn_model_linear(ctypes.byref(dx), ctypes.byref(dw), ctypes.byref(do), None, 1, int(epilogue),
+                                    _stream(x.device)))
+    return out
+
+
+def interleave_fc12(fc1: torch.Tensor, fc2: torch.Tensor) -> torch.Tensor:
+    """fc1 / fc2 ``[F, E]`` as one ``[2F, E]`` weight in row groups of 8 (fc1 rows 8j..8j+7, then fc2 rows
+    8j..8j+7): the layout ``EPI_SILU_MUL`` pairs."""
+    F_, E = fc1.shape
+    return torch.stack([fc1.view(F_ // 8, 8, E), fc2.view(F_ // 8, 8, E)], 1).reshape(2 * F_, E).contiguous()
 
 
 def silu_mul(u: torch.Tensor) -> torch.Tensor:
@@ -171,6 +219,22 @@ def gated_norm(core: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: f
     dx, dz, dw, do = _desc(core), _desc(z), _desc(weight), _desc(out)
     _lib.check(_lib.load().gdn_rms_norm_gated(ctypes.byref(dx), ctypes.byref(dz), ctypes.byref(dw), float(eps),
                                               ctypes.byref(do), _stream(core.device)))
+    return out
+
+
+def gdn_decode(proj: torch.Tensor, conv_state: torch.Tensor, conv_w: torch.Tensor, A_log: torch.Tensor,
+               dt_bias: torch.Tensor, state: torch.Tensor, norm_w: torch.Tensor, eps: float) -> torch.Tensor:
+    """One decode token of a GatedDeltaNet layer from its fused input projection ``proj [B, 3HD + HD + 2H]``
+    (``gdn_model_gdn_decode``: conv update, gates, recurrent rule and gated norm in one kernel; ``conv_state``
+    and ``state`` updated in place); returns the normed output ``[B, H*128]``."""
+    B = proj.shape[0]
+    H = A_log.shape[0]
+    out = torch.empty((B, H * 128), dtype=proj.dtype, device=proj.device)
+    d = [_desc(t) for t in (proj, conv_state, conv_w, A_log, dt_bias, norm_w, out)]
+    _lib.check(_lib.load().gdn_model_gdn_decode(ctypes.byref(d[0]), ctypes.byref(d[1]), ctypes.byref(d[2]),
+                                                ctypes.byref(d[3]), ctypes.byref(d[4]), state.data_ptr(),
+                                                ctypes.byref(d[5]), float(eps), ctypes.byref(d[6]),
+                                                _stream(proj.device)))
     return out
 
 
@@ -233,7 +297,7 @@ class Qwen35Decoder:
             p = f"trf_blocks.{i}."
             m = p + "token_mixer."
             L = SimpleNamespace(kind=kind, idx=i, norm1=w(p + "norm1.weight"), norm2=w(p + "norm2.weight"),
-                                fc12=torch.cat([w(p + "ff.fc1.weight"), w(p + "ff.fc2.weight")]).contiguous(),
+                                fc12=interleave_fc12(w(p + "ff.fc1.weight"), w(p + "ff.fc2.weight")),
                                 fc3=w(p + "ff.fc3.weight"))
             if kind == "linear_attention":
                 L.w_in = torch.cat([w(m + "in_proj_qkv.weight"), w(m + "in_proj_z.weight"),
@@ -253,16 +317,35 @@ class Qwen35Decoder:
 
     # ------------------------------------------------------------------ mixers
 
+    def _proj(self, h: torch.Tensor, w: torch.Tensor, epilogue: int = EPI_STORE, ksplit: int = 1):
+        """``h [..., K] -> [..., N]``: the decode kernel (``linear``) for at most 32 rows, the library GEMM
+        otherwise; ``EPI_SILU_MUL`` applies the FFN activation to fc1/fc2 interleaved rows either way, and
+        ``EPI_PARTIAL`` may return a ``Partial`` (any consumer takes both forms through ``add_rms_norm``)."""
+        lead = h.shape[:-1]
+        x = h.reshape(-1, h.shape[-1])
+        if x.shape[0] <= DECODE_MAX_ROWS:
+            y = linear(x, w, epilogue, ksplit)
+            return y if isinstance(y, Partial) else y.view(*lead, y.shape[-1])
+        y = F.linear(x, w)
+        if epilogue == EPI_SILU_MUL:
+            u = y.unflatten(-1, (-1, 2, 8))
+            y = (F.silu(u[..., 0, :]) * u[..., 1, :]).flatten(-2)
+        return y.view(*lead, y.shape[-1])
+
     def _gdn(self, L, h: torch.Tensor, cache: Qwen35Cache, decode: bool) -> torch.Tensor:
         g_ = self.gdn
         B, T, _ = h.shape
-        proj = F.linear(h, L.w_in)  # [B, T, C + value_dim + 2 Hv]
+        proj = self._proj(h, L.w_in)  # [B, T, C + value_dim + 2 Hv]
         C, Vd, Hv = g_.C, g_.value_dim, g_.Hv
         mixed = proj[..., :C]
         z = proj[..., C:C + Vd]
         b = proj[..., C + Vd:C + Vd + Hv]
         a = proj[..., C + Vd + Hv:C + Vd + 2 * Hv]
         conv_state = cache.conv_states[L.idx]
+        if decode and T == 1:  # one token: conv update, gates, recurrent rule and gated norm in one kernel
+            normed = gdn_decode(proj.reshape(B, -1), conv_state, L.conv_w, L.A_log, L.dt_bias,
+                                cache.recurrent_states[L.idx], L.gnorm, self.eps)
+            return self._proj(normed.view(B, 1, Vd), L.w_out, EPI_PARTIAL, 8)
         if decode:  # torch_causal_conv1d_update against the cached state (qwen3_5_transformers.py:337-343)
             conv = layer.causal_conv1d_update(mixed.transpose(1, 2), conv_state, L.conv_w, None, "silu")
             conv = conv.transpose(1, 2)
@@ -282,13 +365,13 @@ class Qwen35Decoder:
                                                       use_qk_l2norm_in_kernel=True)
             state.copy_(final)
         normed = gated_norm(core.reshape(B * T, Hv, g_.Dv), z.reshape(B * T, Hv, g_.Dv), L.gnorm, self.eps)
-        return F.linear(normed.reshape(B, T, Vd), L.w_out)
+        return self._proj(normed.reshape(B, T, Vd), L.w_out, EPI_PARTIAL, 8)
 
     def _attention(self, L, h: torch.Tensor, cache: Qwen35Cache) -> torch.Tensor:
         cfg = self.cfg
         B, T, _ = h.shape
         Hq, Hkv, Dh = cfg["n_heads"], cfg["n_kv_groups"], cfg["head_dim"]
-        qkv = F.linear(h, L.w_qkv)  # [B, T, Hq (q | gate) + Hkv k + Hkv v]
+        qkv = self._proj(h, L.w_qkv)  # [B, T, Hq (q | gate) + Hkv k + Hkv v]
         q = torch.empty((B, T, Hq, Dh), dtype=h.dtype, device=h.device)
         kc, vc = cache.key_cache[L.idx], cache.value_cache[L.idx]
         lib = _lib.load()
@@ -302,7 +385,7 @@ class Qwen35Decoder:
         dg, dctx = _desc(gate), _desc(ctx)
         _lib.check(lib.gdn_model_attention(ctypes.byref(dq), ctypes.byref(dkc), ctypes.byref(dvc), ctypes.byref(dg),
                                            cache.pos.data_ptr(), ctypes.byref(dctx), _stream(h.device)))
-        return F.linear(ctx, L.w_out)
+        return self._proj(ctx, L.w_out, EPI_PARTIAL, 8)
 
     # ------------------------------------------------------------------ model
 
@@ -319,10 +402,10 @@ class Qwen35Decoder:
                 h, res = add_rms_norm(delta, L.norm1, self.eps, residual=res)
             mix = self._attention(L, h, cache) if L.kind == "full_attention" else self._gdn(L, h, cache, decode)
             h, res = add_rms_norm(mix, L.norm2, self.eps, residual=res)
-            delta = F.linear(silu_mul(F.linear(h, L.fc12)), L.fc3)
-        h, res = add_rms_norm(delta[:, -1:], self.final_norm, self.eps, residual=res[:, -1:].contiguous())
+            delta = self._proj(self._proj(h, L.fc12, EPI_SILU_MUL), L.fc3, EPI_PARTIAL, 8)
+        h, res = add_rms_norm(delta, self.final_norm, self.eps, residual=res)
         cache.pos.add_(T)
-        return F.linear(h[:, -1], self.head)
+        return self._proj(h[:, -1], self.head)
 
     def new_cache(self, batch: int) -> Qwen35Cache:
         return Qwen35Cache(self.cfg, batch, self.max_len, self.device)

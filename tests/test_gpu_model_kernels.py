@@ -131,3 +131,69 @@ def test_cached_attention_matches_full_recompute():
     scale = want.abs().max()
     assert err.max() <= 0.02 * scale, (err.max().item(), scale.item())
     assert (err / scale).mean() < 2e-3
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 17, 32])
+def test_decode_linear_matches_fp32_matmul(M):
+    """gdn_model_linear (the decode projections) against the fp32 product of the same bf16 operands."""
+    from llms_from_scratch_b200.model import EPI_PARTIAL, EPI_SILU_MUL, EPI_STORE, interleave_fc12, linear
+    torch.manual_seed(10 + M)
+    K, N = 1024, 272
+    x = torch.randn(M, K, device="cuda").to(bf)
+    w = (torch.randn(N, K, device="cuda") * 0.05).to(bf)
+    want = x.float() @ w.float().T
+    got = linear(x, w, EPI_STORE)
+    # one bf16 rounding step, or a tiny absolute slack for results near zero (fp32 sums in another order)
+    near = (got.float() - want).abs() <= 1e-4 * want.abs().max()
+    assert ((_ulps_apart(got, want.to(bf)) <= 1) | near).all()
+    # split-K partials sum to the fp32 product
+    K2 = 3584
+    x2 = torch.randn(M, K2, device="cuda").to(bf)
+    w2 = (torch.randn(N, K2, device="cuda") * 0.05).to(bf)
+    part = linear(x2, w2, EPI_PARTIAL, ksplit=4).buf
+    assert part.shape == (4, M, N)
+    ref2 = x2.float() @ w2.float().T
+    assert ((part.sum(0) - ref2).abs() <= 1e-4 * ref2.abs().max()).all()
+    # the FFN epilogue on interleaved fc1 / fc2 rows: SiLU(fc1 x) * (fc2 x) with the reference's roundings
+    F_ = 136
+    fc1 = (torch.randn(F_, K, device="cuda") * 0.05).to(bf)
+    fc2 = (torch.randn(F_, K, device="cuda") * 0.05).to(bf)
+    act = linear(x, interleave_fc12(fc1, fc2), EPI_SILU_MUL)
+    want_act = F.silu((x.float() @ fc1.float().T).to(bf)) * (x.float() @ fc2.float().T).to(bf)
+    assert act.shape == (M, F_)
+    near = (act.float() - want_act.float()).abs() <= 1e-3 * want_act.float().abs().max()
+    assert ((_ulps_apart(act, want_act) <= 2) | near).all()
+
+
+def test_fused_gdn_decode_matches_the_separate_kernels():
+    """gdn_model_gdn_decode (conv update + gates + recurrent rule + gated norm for one token) equals the
+    four separate kernels it replaces, on random states and projections."""
+    from llms_from_scratch_b200 import fast_recurrent_gated_delta_rule, layer
+    from llms_from_scratch_b200.model import gdn_decode
+    torch.manual_seed(4)
+    B, H, D = 5, 16, 128
+    C = 3 * H * D
+    proj = torch.randn(B, C + H * D + 2 * H, device="cuda").to(bf)
+    conv_state = torch.randn(B, C, 4, device="cuda").to(bf)
+    conv_w = (torch.randn(C, 4, device="cuda") * 0.5).to(bf)
+    A_log = torch.log(torch.rand(H, device="cuda") * 15 + 0.5).to(bf)
+    dt_bias = torch.randn(H, device="cuda").to(bf)
+    state = torch.randn(B, H, D, D, device="cuda") * 0.05
+    norm_w = (1 + 0.1 * torch.randn(D, device="cuda")).to(bf)
+    # the separate kernels
+    cs1, st1 = conv_state.clone(), state.clone()
+    mixed = proj[:, :C].unsqueeze(1)
+    conv = layer.causal_conv1d_update(mixed.transpose(1, 2), cs1, conv_w, None, "silu").transpose(1, 2)
+    z = proj[:, C:C + H * D]
+    b_, a_ = proj[:, C + H * D:C + H * D + H].unsqueeze(1), proj[:, C + H * D + H:].unsqueeze(1)
+    g, beta = layer.gates(a_, b_, A_log, dt_bias)
+    q, k, v = (conv[..., i * H * D:(i + 1) * H * D].unflatten(-1, (H, D)) for i in range(3))
+    core, _ = fast_recurrent_gated_delta_rule(q, k, v, g, beta, st1, True, use_qk_l2norm_in_kernel=True, out_state=st1)
+    want = layer.rms_norm_gated(core.reshape(B, H, D), z.reshape(B, H, D), norm_w, 1e-6).reshape(B, H * D)
+    # fused
+    cs2, st2 = conv_state.clone(), state.clone()
+    got = gdn_decode(proj, cs2, conv_w, A_log, dt_bias, st2, norm_w, 1e-6)
+    assert torch.equal(cs1, cs2)
+    assert torch.equal(st1, st2)
+    d = _ulps_apart(got, want)
+    assert (d <= 1).all() and (d > 0).float().mean() < 0.01, (d.max().item(), (d > 0).float().mean().item())
