@@ -467,6 +467,7 @@ int gdn_recurrent_gated_delta_rule(const gdn_tensor* query, const gdn_tensor* ke
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     float* hT = output_final_state ? final_state : nullptr;
     if (B * H == 0) return GDN_OK;
+    if (B * H > 0x7fffffffLL / 4) return fail(GDN_ERR_INVALID_ARGUMENT, "B*H too large for the recurrent rule");
     if (T == 0) return empty_sequence(B, H, initial_state, hT, st);
 
     gdn::RecurrentParams p{};

@@ -194,6 +194,7 @@ def test_fused_gdn_decode_matches_the_separate_kernels():
     cs2, st2 = conv_state.clone(), state.clone()
     got = gdn_decode(proj, cs2, conv_w, A_log, dt_bias, st2, norm_w, 1e-6)
     assert torch.equal(cs1, cs2)
-    assert torch.equal(st1, st2)
+    # the same arithmetic per state element; the kv / o sums over the 128 rows run in another order
+    torch.testing.assert_close(st2, st1, rtol=1e-5, atol=1e-6)
     d = _ulps_apart(got, want)
     assert (d <= 1).all() and (d > 0).float().mean() < 0.01, (d.max().item(), (d > 0).float().mean().item())
