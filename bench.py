@@ -684,6 +684,62 @@ def decode_model_leg(torch, device, peak, batches=(1, 32), steps=200, prompt_len
     return res
 
 
+def reference_decode_leg(torch, device, batches=(1, 32), steps=200, prompt_len=26):
+    """The reference's own decode on the GPU, for comparison with ``decode_model``: its ``Qwen3_5Model``
+    (unmodified install in baseline/_ref) at the same shape and random N(0, 0.02) weights, bf16, its
+    GatedDeltaNet layers on its Triton path (``benchmark.patch_model_backend("triton")``,
+    benchmark.py:254-280), greedy generation by its ``generate_text_basic_stream`` (qwen3_5.py:483-495:
+    the whole prefix re-run for every token, no cache).  Device time by CUDA events around the
+    generation of ``steps`` tokens after the same 26-token prompt."""
+    if not os.path.exists(os.path.join(REF_DIR, "qwen3_5.py")):
+        return {"unavailable": "baseline/_ref (the reference install) is absent"}
+    names = ("qwen3_5_cutedsl_kernels", "qwen3_5_transformers", "qwen3_5", "benchmark")
+    saved = {k: sys.modules.pop(k) for k in names if k in sys.modules}
+    sys.path.insert(0, REF_DIR)
+    try:
+        import benchmark as ref_bench
+        import qwen3_5 as ref_model
+        from llms_from_scratch_b200.model import QWEN3_5_0_8B, random_weights
+        ref_bench.patch_model_backend("triton")
+        cfg = dict(ref_model.QWEN3_5_CONFIG)
+        cfg.update({k: v for k, v in QWEN3_5_0_8B.items() if k in cfg})
+        cfg.update(layer_types=list(QWEN3_5_0_8B["layer_types"]), context_length=prompt_len + steps + 8,
+                   dtype=torch.bfloat16)
+        with torch.device(device):
+            model = ref_model.Qwen3_5Model(cfg)
+        model.load_state_dict(random_weights(QWEN3_5_0_8B, seed=0, device=device), strict=True)
+        model.eval()
+        res = {"workload": f"the reference's Qwen3_5Model, same shape and weights as decode_model, bf16, GatedDeltaNet "
+                           f"layers on its Triton backend; prompt of {prompt_len} ids, {steps} greedy tokens by its "
+                           "generate_text_basic_stream (no cache: the whole prefix re-run per token)", "steps": steps}
+        gen = torch.Generator(device=device)
+        gen.manual_seed(11)
+        for B in batches:
+            prompt = torch.randint(0, cfg["vocab_size"], (B, prompt_len), device=device, generator=gen)
+            for _ in ref_model.generate_text_basic_stream(model, prompt, 2):  # warm-up (Triton compile)
+                pass
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            n = 0
+            for _ in ref_model.generate_text_basic_stream(model, prompt, steps):
+                n += 1
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b)
+            res[f"batch{B}"] = {"tok_s": B * n / (ms / 1e3), "ms_per_token": ms / n}
+        del model
+        torch.cuda.empty_cache()
+        return res
+    except Exception as e:  # the reference's GPU path failed to run here: report, do not fail the bench
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    finally:
+        sys.path.remove(REF_DIR)
+        for k in names:
+            sys.modules.pop(k, None)
+        sys.modules.update(saved)
+
+
 def _decode_kernel_shares(torch, dec, cache, prompt, n):
     """Device-time share of each kernel family over n eager decode steps (torch profiler), and the mean
     duration of the recurrent kernel in microseconds."""
@@ -930,6 +986,8 @@ def main():
     if not args.no_decode_model:
         decode_model = decode_model_leg(torch, device, peak_l)
         torch.cuda.empty_cache()
+        if rank == 0 and not args.no_reference_triton:
+            decode_model["reference_decode"] = reference_decode_leg(torch, device)
     ref_triton = None
     if rank == 0 and not args.no_reference_triton:
         ref_triton = time_reference_triton(torch, flush, device, H, (256, 512, 1024, 2048, 4096))
