@@ -32,6 +32,13 @@
 extern "C" {
 #endif
 
+/* Every kernel below is launched with programmatic stream serialization (programmatic dependent launch):
+ * the next kernel in the stream may be scheduled while the previous one runs and read its weights, but
+ * waits for the previous grid to complete before it reads anything else or writes (griddepcontrol.wait), so
+ * results do not depend on it.  In a captured decode step this overlaps each kernel's launch and weight
+ * prefetch with the tail of the one before.  enable = 0 launches them plainly (for comparison). */
+GDN_API void gdn_model_set_programmatic_launch(int enable);
+
 /* out = RMSNorm(h) with h = x (+ residual): h * rsqrt(mean(h^2) + eps) * (1 + weight) in fp32, rounded to
  * bf16 (qwen3_5.py:49-63).  x, out [N, D] (D a multiple of 8, at most 8192); weight [D].  With `residual`
  * non-NULL, h = bf16(x + residual) (the block's `x = x + shortcut`, qwen3_5.py:231, :236) and h is written

@@ -74,6 +74,7 @@ SIGNATURES = {
                                                 c_void_p]),
     "gdn_model_linear": (c_int, [_P, _P, _P, c_void_p, c_int, c_int, c_void_p]),
     "gdn_model_gdn_decode": (c_int, [_P, _P, _P, _P, _P, c_void_p, _P, ctypes.c_float, _P, c_void_p]),
+    "gdn_model_set_programmatic_launch": (None, [c_int]),
     "gdn_launch_count": (ctypes.c_uint64, []),
     "gdn_set_phase_events": (None, [ctypes.POINTER(c_void_p), c_int]),
     "gdn_device_error": (ctypes.c_uint, [c_int]),

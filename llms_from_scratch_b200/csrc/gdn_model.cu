@@ -52,6 +52,35 @@ __device__ __forceinline__ float warp_max(float x) {
     return x;
 }
 
+// Programmatic dependent launch: every kernel here is launched with programmatic stream serialization, so
+// the next kernel of a decode step may be scheduled while this one runs.  A kernel reads nothing the
+// previous kernel may write, and writes nothing, before griddep_wait() (which returns once the previous
+// grid has completed and its memory is visible); before it, it may only read weights.  Right after the
+// wait it lets the next kernel launch.  Launched without the attribute, both are no-ops.
+__device__ __forceinline__ void griddep_wait_and_release() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+std::atomic<int> g_pdl{1};
+
+// Launch with programmatic stream serialization (the next kernel of the stream may start while this one runs;
+// see griddep_wait_and_release), unless switched off by gdn_model_set_programmatic_launch(0).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = g_pdl.load(std::memory_order_relaxed) ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // --------------------------------------------------------------------------- residual add + RMSNorm
 
 struct AddNormArgs {
@@ -76,6 +105,9 @@ __global__ void __launch_bounds__(1024) gdn_model_add_rms_norm_kernel(AddNormArg
     const int64_t row = blockIdx.x;
     const int c = threadIdx.x * 8;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    float w[8];
+    load8(a.w + c, w);  // the weight only: nothing the previous kernel writes is read before the wait
+    griddep_wait_and_release();
     float h[8];
     if (a.xp) {
         const int64_t plane = (int64_t)gridDim.x * a.D;
@@ -112,8 +144,7 @@ __global__ void __launch_bounds__(1024) gdn_model_add_rms_norm_kernel(AddNormArg
     }
     __syncthreads();
     const float inv = rsqrtf(part[0] / (float)a.D + a.eps);
-    float w[8], o[8];
-    load8(a.w + c, w);
+    float o[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(__fmul_rn(h[i], inv), 1.0f + w[i]);
     store8(a.out + row * a.o_s + c, o);
@@ -147,6 +178,7 @@ struct PrepArgs {
 __global__ void __launch_bounds__(1024) gdn_model_attn_prep_kernel(PrepArgs a) {
     const int t = blockIdx.x, b = blockIdx.y;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    griddep_wait_and_release();
     const int p = a.pos[0] + t;
     if (p < 0 || p >= a.L) return;
     const bf16* tok = a.qkv + (int64_t)b * a.q_sb + (int64_t)t * a.q_st;
@@ -239,6 +271,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) gdn_model_attention_kernel(At
     const int t = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kh = h / (a.Hq / a.Hkv);
+    griddep_wait_and_release();
     int p = a.pos[0] + t;
     if (p >= a.L) p = a.L - 1;
     if (p < 0) p = 0;
@@ -303,6 +336,7 @@ struct SiluArgs {
 __global__ void __launch_bounds__(256) gdn_model_silu_mul_kernel(SiluArgs a) {
     const int per_row = a.F / 8;
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    griddep_wait_and_release();
     if (idx >= a.N * per_row) return;
     const int64_t row = idx / per_row;
     const int c = (int)(idx % per_row) * 8;
@@ -381,7 +415,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32) gdn_model_gemm_kernel(GemmArg
     // copy plan of one stage: W pieces i = tid + 128 j (j < 4): row i / 8 (rows past N are skipped), piece i % 8;
     // x pieces i = tid + 128 j (j < MT*8*8/128): row i / 8 (rows past M are zero-filled)
     constexpr int kXPieces = MT * 8 * 8;
-    auto issue = [&](int b) {
+    auto issue_w = [&](int b) {
         const uint32_t st = ring + (uint32_t)(b % kStages) * kStage;
         const int64_t k0 = (int64_t)(kb0 + b) * 64;
 #pragma unroll
@@ -393,6 +427,10 @@ __global__ void __launch_bounds__(kGemmWarps * 32) gdn_model_gemm_kernel(GemmArg
             const uint32_t bytes = n < a.N ? 16u : 0u;
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(bytes) : "memory");
         }
+    };
+    auto issue_x = [&](int b) {
+        const uint32_t st = ring + (uint32_t)(b % kStages) * kStage;
+        const int64_t k0 = (int64_t)(kb0 + b) * 64;
 #pragma unroll
         for (int j = 0; j < (kXPieces + 127) / 128; ++j) {
             const int i = tid + 128 * j;
@@ -405,11 +443,16 @@ __global__ void __launch_bounds__(kGemmWarps * 32) gdn_model_gemm_kernel(GemmArg
             }
         }
     };
+    // the first blocks' weights before the wait (weights are never written by a kernel of the step), x after
 #pragma unroll
-    for (int b = 0; b < kStages - 1; ++b) {
-        if (b < nkb) issue(b);
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    }
+    for (int b = 0; b < kStages - 1; ++b)
+        if (b < nkb) issue_w(b);
+    griddep_wait_and_release();
+#pragma unroll
+    for (int b = 0; b < kStages - 1; ++b)
+        if (b < nkb) issue_x(b);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // the prologue's blocks, then the steady pipeline
     float acc[MT][4];
 #pragma unroll
     for (int t = 0; t < MT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
@@ -423,7 +466,10 @@ __global__ void __launch_bounds__(kGemmWarps * 32) gdn_model_gemm_kernel(GemmArg
     for (int b = 0; b < nkb; ++b) {
         asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 2) : "memory");
         __syncthreads();  // block b has landed for every thread, and every warp is done with block b - 1's stage
-        if (b + kStages - 1 < nkb) issue(b + kStages - 1);  // refills the stage block b - 1 used
+        if (b + kStages - 1 < nkb) {  // refills the stage block b - 1 used
+            issue_w(b + kStages - 1);
+            issue_x(b + kStages - 1);
+        }
         asm volatile("cp.async.commit_group;" ::: "memory");
         const uint32_t st = ring + (uint32_t)(b % kStages) * kStage;
         uint4 ra[2], rb[2];
@@ -487,8 +533,7 @@ cudaError_t launch_gemm_mt(const GemmArgs& a, cudaStream_t st) {
         attr_done.fetch_or(bit, std::memory_order_release);
     }
     const dim3 grid((unsigned)((a.N + kGemmRows - 1) / kGemmRows), (unsigned)a.ksplit);
-    gdn_model_gemm_kernel<MT, EPI><<<grid, kGemmWarps * 32, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_k(gdn_model_gemm_kernel<MT, EPI>, grid, dim3(kGemmWarps * 32), smem, st, a);
 }
 
 template <int EPI>
@@ -551,6 +596,7 @@ __global__ void __launch_bounds__(kDecThreads, 4) gdn_model_gdn_decode_kernel(Gd
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
     const int r0 = kDecRows * warp, c0 = 4 * lane;
+    griddep_wait_and_release();
     // 1. the state: shared-memory rows by cp.async, register rows by plain loads, all in flight now
     float* st = a.state + (int64_t)bh * 128 * 128 + c0;
 #pragma unroll
@@ -770,10 +816,13 @@ int add_rms_norm_impl(const gdn_tensor* x, const float* partial, int nsplit, int
                   reinterpret_cast<const bf16*>(weight->data), reinterpret_cast<bf16*>(out->data), out->stride[0],
                   residual ? reinterpret_cast<bf16*>(residual_out->data) : nullptr,
                   residual ? residual_out->stride[0] : 0, (int)D, eps};
-    gdn_model_add_rms_norm_kernel<<<(unsigned)N, (unsigned)(D / 8), 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-    return launched(cudaGetLastError(), "add_rms_norm launch");
+    return launched(launch_k(gdn_model_add_rms_norm_kernel, dim3((unsigned)N), dim3((unsigned)(D / 8)), 0,
+                             reinterpret_cast<cudaStream_t>(stream), a),
+                    "add_rms_norm launch");
 }
 }  // namespace
+
+void gdn_model_set_programmatic_launch(int enable) { gdn::g_pdl.store(enable ? 1 : 0); }
 
 int gdn_model_add_rms_norm(const gdn_tensor* x, const gdn_tensor* residual, const gdn_tensor* weight, float eps,
                            gdn_tensor* out, gdn_tensor* residual_out, void* stream) {
@@ -820,8 +869,9 @@ int gdn_model_gdn_decode(const gdn_tensor* proj, gdn_tensor* conv_state, const g
                        reinterpret_cast<const bf16*>(A_log->data), reinterpret_cast<const bf16*>(dt_bias->data), state,
                        reinterpret_cast<const bf16*>(norm_w->data), eps, reinterpret_cast<bf16*>(out->data),
                        out->stride[0], (int)H, (int)C};
-    gdn_model_gdn_decode_kernel<<<(unsigned)(B * H), kDecThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(args);
-    return launched(cudaGetLastError(), "gdn decode launch");
+    return launched(launch_k(gdn_model_gdn_decode_kernel, dim3((unsigned)(B * H)), dim3(kDecThreads), 0,
+                             reinterpret_cast<cudaStream_t>(stream), args),
+                    "gdn decode launch");
 }
 
 int gdn_model_linear(const gdn_tensor* x, const gdn_tensor* w, gdn_tensor* out, float* partial, int ksplit,
@@ -887,9 +937,9 @@ int gdn_model_attn_prep(const gdn_tensor* qkv, const gdn_tensor* q_norm_w, const
                q_out->stride[1], q_out->stride[2], reinterpret_cast<bf16*>(k_cache->data), k_cache->stride[0],
                k_cache->stride[1], k_cache->stride[2], reinterpret_cast<bf16*>(v_cache->data), v_cache->stride[0],
                v_cache->stride[1], v_cache->stride[2], (int)Hq, (int)Hkv, (int)L};
-    gdn_model_attn_prep_kernel<<<dim3((unsigned)T, (unsigned)B), (unsigned)(32 * (Hq + 2 * Hkv)), 0,
-                                 reinterpret_cast<cudaStream_t>(stream)>>>(a);
-    return launched(cudaGetLastError(), "attn_prep launch");
+    return launched(launch_k(gdn_model_attn_prep_kernel, dim3((unsigned)T, (unsigned)B), dim3((unsigned)(32 * (Hq + 2 * Hkv))),
+                             0, reinterpret_cast<cudaStream_t>(stream), a),
+                    "attn_prep launch");
 }
 
 int gdn_model_attention(const gdn_tensor* q, const gdn_tensor* k_cache, const gdn_tensor* v_cache,
@@ -923,9 +973,9 @@ int gdn_model_attention(const gdn_tensor* q, const gdn_tensor* k_cache, const gd
                                              (int)smem);
         if (e != cudaSuccess) return launched(e, "attention attribute");
     }
-    gdn_model_attention_kernel<<<dim3((unsigned)T, (unsigned)Hq, (unsigned)B), kAttnWarps * 32, smem,
-                                 reinterpret_cast<cudaStream_t>(stream)>>>(a);
-    return launched(cudaGetLastError(), "attention launch");
+    return launched(launch_k(gdn_model_attention_kernel, dim3((unsigned)T, (unsigned)Hq, (unsigned)B),
+                             dim3(kAttnWarps * 32), smem, reinterpret_cast<cudaStream_t>(stream), a),
+                    "attention launch");
 }
 
 int gdn_model_silu_mul(const gdn_tensor* x, gdn_tensor* out, void* stream) {
@@ -941,8 +991,9 @@ int gdn_model_silu_mul(const gdn_tensor* x, gdn_tensor* out, void* stream) {
     if (work > (int64_t)0x7fffffff * 256) return bad("x too large");
     SiluArgs a{reinterpret_cast<const bf16*>(x->data), x->stride[0], reinterpret_cast<bf16*>(out->data),
                out->stride[0], N, (int)(F2 / 2)};
-    gdn_model_silu_mul_kernel<<<(unsigned)((work + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-    return launched(cudaGetLastError(), "silu_mul launch");
+    return launched(launch_k(gdn_model_silu_mul_kernel, dim3((unsigned)((work + 255) / 256)), dim3(256), 0,
+                             reinterpret_cast<cudaStream_t>(stream), a),
+                    "silu_mul launch");
 }
 
 }  // extern "C"

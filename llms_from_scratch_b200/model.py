@@ -404,8 +404,9 @@ class Qwen35Decoder:
             h, res = add_rms_norm(mix, L.norm2, self.eps, residual=res)
             delta = self._proj(self._proj(h, L.fc12, EPI_SILU_MUL), L.fc3, EPI_PARTIAL, 8)
         h, res = add_rms_norm(delta, self.final_norm, self.eps, residual=res)
-        cache.pos.add_(T)
-        return self._proj(h[:, -1], self.head)
+        logits = self._proj(h[:, -1], self.head)
+        cache.pos.add_(T)  # after the head, so the norm -> head launches stay programmatically chained
+        return logits
 
     def new_cache(self, batch: int) -> Qwen35Cache:
         return Qwen35Cache(self.cfg, batch, self.max_len, self.device)
