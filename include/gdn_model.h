@@ -77,10 +77,16 @@ GDN_API int gdn_model_linear(const gdn_tensor* x, const gdn_tensor* w, gdn_tenso
  *   state       fp32 [B, H, 128, 128] updated in place;  norm_w [128]
  *   out         [B, H*128]: the normed output (the input of out_proj)
  * The same roundings as the separate gdn_causal_conv1d_update, gdn_gates, gdn_recurrent_gated_delta_rule and
- * gdn_rms_norm_gated calls; equal key and value head counts (Qwen3.5: 16 / 16). */
+ * gdn_rms_norm_gated calls; equal key and value head counts (Qwen3.5: 16 / 16).
+ *   prefetch_state  nonzero: the caller guarantees that no kernel that may still be running when this one
+ *                   starts writes `state` (in a decode step the state is written only by this layer's call
+ *                   of the previous step, and a plainly launched kernel -- the step's embedding -- lies in
+ *                   between), so the kernel starts loading it before the kernel launched just before it
+ *                   completes.  0: it waits for that kernel first, like every other input. */
 GDN_API int gdn_model_gdn_decode(const gdn_tensor* proj, gdn_tensor* conv_state, const gdn_tensor* conv_w,
                                  const gdn_tensor* A_log, const gdn_tensor* dt_bias, float* state,
-                                 const gdn_tensor* norm_w, float eps, gdn_tensor* out, void* stream);
+                                 const gdn_tensor* norm_w, float eps, gdn_tensor* out, int prefetch_state,
+                                 void* stream);
 
 /* Full-attention prologue for T new tokens at positions pos[0] .. pos[0] + T - 1 (pos: one device int32, so
  * a captured decode step can advance it): from the fused projection qkv [B, T, Hq*2*Dh + 2*Hkv*Dh] (per

@@ -73,7 +73,7 @@ SIGNATURES = {
     "gdn_model_add_rms_norm_partials": (c_int, [c_void_p, c_int, c_int64, c_int64, _P, _P, ctypes.c_float, _P, _P,
                                                 c_void_p]),
     "gdn_model_linear": (c_int, [_P, _P, _P, c_void_p, c_int, c_int, c_void_p]),
-    "gdn_model_gdn_decode": (c_int, [_P, _P, _P, _P, _P, c_void_p, _P, ctypes.c_float, _P, c_void_p]),
+    "gdn_model_gdn_decode": (c_int, [_P, _P, _P, _P, _P, c_void_p, _P, ctypes.c_float, _P, c_int, c_void_p]),
     "gdn_model_set_programmatic_launch": (None, [c_int]),
     "gdn_launch_count": (ctypes.c_uint64, []),
     "gdn_set_phase_events": (None, [ctypes.POINTER(c_void_p), c_int]),

@@ -571,6 +571,7 @@ struct GdnDecodeArgs {
     bf16* out;          // [B, H * 128]
     int64_t out_s;
     int H, C;
+    int prefetch_state;  // the state is not written by any kernel that may still run (see the C ABI)
 };
 
 constexpr int kDecThreads = 256;
@@ -596,8 +597,9 @@ __global__ void __launch_bounds__(kDecThreads, 4) gdn_model_gdn_decode_kernel(Gd
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
     const int r0 = kDecRows * warp, c0 = 4 * lane;
-    griddep_wait_and_release();
-    // 1. the state: shared-memory rows by cp.async, register rows by plain loads, all in flight now
+    if (!a.prefetch_state) griddep_wait_and_release();
+    // 1. the state: shared-memory rows by cp.async, register rows by plain loads, all in flight now (with
+    //    prefetch_state, while the kernel before this one still runs)
     float* st = a.state + (int64_t)bh * 128 * 128 + c0;
 #pragma unroll
     for (int r = 0; r < kDecRows - kDecRegRows; ++r)
@@ -609,6 +611,7 @@ __global__ void __launch_bounds__(kDecThreads, 4) gdn_model_gdn_decode_kernel(Gd
         const float4 v = *reinterpret_cast<const float4*>(st + (int64_t)(r0 + r) * 128);
         S[r][0] = v.x, S[r][1] = v.y, S[r][2] = v.z, S[r][3] = v.w;
     }
+    if (a.prefetch_state) griddep_wait_and_release();  // the projection row and conv state come from here on
     // 2. conv update of the head's q / k / v channels (window [s1, s2, s3, x]), conv + SiLU rounded to bf16
     const bf16* prow = a.proj + (int64_t)b * a.proj_s;
     const int key_dim = a.H * 128;
@@ -837,7 +840,7 @@ int gdn_model_add_rms_norm_partials(const float* partial, int nsplit, int64_t ro
 
 int gdn_model_gdn_decode(const gdn_tensor* proj, gdn_tensor* conv_state, const gdn_tensor* conv_w,
                          const gdn_tensor* A_log, const gdn_tensor* dt_bias, float* state, const gdn_tensor* norm_w,
-                         float eps, gdn_tensor* out, void* stream) {
+                         float eps, gdn_tensor* out, int prefetch_state, void* stream) {
     using namespace gdn;
     int rc;
     if ((rc = view("out", out, 2, nullptr))) return rc;
@@ -868,7 +871,7 @@ int gdn_model_gdn_decode(const gdn_tensor* proj, gdn_tensor* conv_state, const g
                        conv_state->stride[0], reinterpret_cast<const bf16*>(conv_w->data),
                        reinterpret_cast<const bf16*>(A_log->data), reinterpret_cast<const bf16*>(dt_bias->data), state,
                        reinterpret_cast<const bf16*>(norm_w->data), eps, reinterpret_cast<bf16*>(out->data),
-                       out->stride[0], (int)H, (int)C};
+                       out->stride[0], (int)H, (int)C, prefetch_state ? 1 : 0};
     return launched(launch_k(gdn_model_gdn_decode_kernel, dim3((unsigned)(B * H)), dim3(kDecThreads), 0,
                              reinterpret_cast<cudaStream_t>(stream), args),
                     "gdn decode launch");

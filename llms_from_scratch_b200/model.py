@@ -223,10 +223,12 @@ def gated_norm(core: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: f
 
 
 def gdn_decode(proj: torch.Tensor, conv_state: torch.Tensor, conv_w: torch.Tensor, A_log: torch.Tensor,
-               dt_bias: torch.Tensor, state: torch.Tensor, norm_w: torch.Tensor, eps: float) -> torch.Tensor:
+               dt_bias: torch.Tensor, state: torch.Tensor, norm_w: torch.Tensor, eps: float,
+               prefetch_state: bool = False) -> torch.Tensor:
     """One decode token of a GatedDeltaNet layer from its fused input projection ``proj [B, 3HD + HD + 2H]``
     (``gdn_model_gdn_decode``: conv update, gates, recurrent rule and gated norm in one kernel; ``conv_state``
-    and ``state`` updated in place); returns the normed output ``[B, H*128]``."""
+    and ``state`` updated in place); returns the normed output ``[B, H*128]``.  ``prefetch_state``: no kernel
+    that may still run writes ``state`` (the decoder's steps guarantee it), so its loads start early."""
     B = proj.shape[0]
     H = A_log.shape[0]
     out = torch.empty((B, H * 128), dtype=proj.dtype, device=proj.device)
@@ -234,7 +236,7 @@ def gdn_decode(proj: torch.Tensor, conv_state: torch.Tensor, conv_w: torch.Tenso
     _lib.check(_lib.load().gdn_model_gdn_decode(ctypes.byref(d[0]), ctypes.byref(d[1]), ctypes.byref(d[2]),
                                                 ctypes.byref(d[3]), ctypes.byref(d[4]), state.data_ptr(),
                                                 ctypes.byref(d[5]), float(eps), ctypes.byref(d[6]),
-                                                _stream(proj.device)))
+                                                int(bool(prefetch_state)), _stream(proj.device)))
     return out
 
 
@@ -343,8 +345,10 @@ class Qwen35Decoder:
         a = proj[..., C + Vd + Hv:C + Vd + 2 * Hv]
         conv_state = cache.conv_states[L.idx]
         if decode and T == 1:  # one token: conv update, gates, recurrent rule and gated norm in one kernel
+            # the state was last written by this layer's call in the previous step, before the step's
+            # embedding (a plain launch): its loads may start while the projection before runs
             normed = gdn_decode(proj.reshape(B, -1), conv_state, L.conv_w, L.A_log, L.dt_bias,
-                                cache.recurrent_states[L.idx], L.gnorm, self.eps)
+                                cache.recurrent_states[L.idx], L.gnorm, self.eps, prefetch_state=True)
             return self._proj(normed.view(B, 1, Vd), L.w_out, EPI_PARTIAL, 8)
         if decode:  # torch_causal_conv1d_update against the cached state (qwen3_5_transformers.py:337-343)
             conv = layer.causal_conv1d_update(mixed.transpose(1, 2), conv_state, L.conv_w, None, "silu")
