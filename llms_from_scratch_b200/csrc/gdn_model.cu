@@ -368,13 +368,13 @@ __global__ void __launch_bounds__(256) gdn_model_silu_mul_kernel(SiluArgs a) {
 //             gdn_model_add_rms_norm_partials), so no atomics and a deterministic result.
 enum : int { kStore = 0, kSiluMul = 1, kPartial = 2 };
 constexpr int kGemmMaxM = 32;
-constexpr int kGemmWarps = 4;
-constexpr int kGemmRows = 16 * kGemmWarps;
 constexpr int kStages = 6;
-constexpr int kWStage = kGemmRows * 128;  // 64 rows x 64 bf16 columns
 
+// NW warps per CTA own 16 NW rows of W; a stage holds those rows' and x's 64 columns (bf16)
+template <int MT, int NW>
+constexpr int gemm_stage_bytes() { return 16 * NW * 128 + 8 * MT * 128; }
 template <int MT>
-constexpr int gemm_stage_bytes() { return kWStage + 8 * MT * 128; }
+constexpr int gemm_warps() { return MT >= 3 ? 2 : 4; }  // wide batches: more, smaller CTAs
 
 struct GemmArgs {
     const bf16* x;
@@ -402,9 +402,13 @@ __device__ __forceinline__ void lds128(uint4& v, uint32_t addr) {
 }
 
 template <int MT, int EPI>
-__global__ void __launch_bounds__(kGemmWarps * 32) gdn_model_gemm_kernel(GemmArgs a) {
+__global__ void __launch_bounds__(gemm_warps<MT>() * 32) gdn_model_gemm_kernel(GemmArgs a) {
     extern __shared__ __align__(128) unsigned char gsm_raw[];
-    constexpr int kStage = gemm_stage_bytes<MT>();
+    constexpr int NW = gemm_warps<MT>();
+    constexpr int kThreads = 32 * NW;
+    constexpr int kGemmRows = 16 * NW;
+    constexpr int kWStage = kGemmRows * 128;
+    constexpr int kStage = gemm_stage_bytes<MT, NW>();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, c = lane & 3;
     const int rows0 = blockIdx.x * kGemmRows;                 // first W row of this CTA
@@ -420,7 +424,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32) gdn_model_gemm_kernel(GemmArg
         const int64_t k0 = (int64_t)(kb0 + b) * 64;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const int i = tid + 128 * j, r = i >> 3, pc = i & 7;
+            const int i = tid + kThreads * j, r = i >> 3, pc = i & 7;
             const int n = rows0 + r;
             const uint32_t d = st + r * 128 + ((pc ^ (r & 7)) << 4);
             const bf16* src = a.w + (int64_t)(n < a.N ? n : 0) * a.w_s + k0 + pc * 8;
@@ -432,8 +436,8 @@ __global__ void __launch_bounds__(kGemmWarps * 32) gdn_model_gemm_kernel(GemmArg
         const uint32_t st = ring + (uint32_t)(b % kStages) * kStage;
         const int64_t k0 = (int64_t)(kb0 + b) * 64;
 #pragma unroll
-        for (int j = 0; j < (kXPieces + 127) / 128; ++j) {
-            const int i = tid + 128 * j;
+        for (int j = 0; j < (kXPieces + kThreads - 1) / kThreads; ++j) {
+            const int i = tid + kThreads * j;
             if (i < kXPieces) {
                 const int r = i >> 3, pc = i & 7;
                 const uint32_t d = st + kWStage + r * 128 + ((pc ^ (r & 7)) << 4);
@@ -521,7 +525,9 @@ __global__ void __launch_bounds__(kGemmWarps * 32) gdn_model_gemm_kernel(GemmArg
 
 template <int MT, int EPI>
 cudaError_t launch_gemm_mt(const GemmArgs& a, cudaStream_t st) {
-    constexpr int smem = kStages * gemm_stage_bytes<MT>();
+    constexpr int NW = gemm_warps<MT>();
+    constexpr int kGemmRows = 16 * NW;
+    constexpr int smem = kStages * gemm_stage_bytes<MT, NW>();
     static std::atomic<uint64_t> attr_done{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -533,7 +539,7 @@ cudaError_t launch_gemm_mt(const GemmArgs& a, cudaStream_t st) {
         attr_done.fetch_or(bit, std::memory_order_release);
     }
     const dim3 grid((unsigned)((a.N + kGemmRows - 1) / kGemmRows), (unsigned)a.ksplit);
-    return launch_k(gdn_model_gemm_kernel<MT, EPI>, grid, dim3(kGemmWarps * 32), smem, st, a);
+    return launch_k(gdn_model_gemm_kernel<MT, EPI>, grid, dim3(NW * 32), smem, st, a);
 }
 
 template <int EPI>
@@ -899,7 +905,7 @@ int gdn_model_linear(const gdn_tensor* x, const gdn_tensor* w, gdn_tensor* out, 
     }
     const int per = (kblocks + ksplit - 1) / ksplit;
     if ((int64_t)(ksplit - 1) * per >= kblocks) return bad("ksplit %d leaves an empty K range", ksplit);
-    if (N / kGemmRows + 1 > 0x7fffffffLL) return bad("N too large");
+    if (N / 32 + 1 > 0x7fffffffLL) return bad("N too large");
     GemmArgs a{reinterpret_cast<const bf16*>(x->data), x->stride[0], reinterpret_cast<const bf16*>(w->data), w->stride[0],
                epilogue == kPartial ? nullptr : reinterpret_cast<bf16*>(out->data),
                epilogue == kPartial ? 0 : out->stride[0], partial, (int)M, (int)N, (int)K, ksplit, per};
