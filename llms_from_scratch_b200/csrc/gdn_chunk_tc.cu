@@ -45,7 +45,9 @@
 //   shared memory (then the output MMAs, into alternating TMEM columns) from one
 //   elected lane of a converged warp; a chunk's output rows are written after
 //   the next state has been handed over, while the next chunk's MMAs run.
+#include <cuda.h>
 #include <cuda_bf16.h>
+#include <cudaTypedefs.h>
 
 #include <atomic>
 
@@ -102,7 +104,16 @@ struct PrepMisc {
     float egc[64];
     float ekd[64];
     uint64_t bar;
+    uint64_t bar_in;  // the q/k/v boxes landed (TMA)
     uint32_t tmem;
+};
+
+// Tensor maps of q, k and v for the prep's input boxes: 4-D over (D, H, T, B) of the caller's bf16 view, box
+// (128, 1, 64, 1) = the 64 token rows of one (batch, head, chunk) as 256-byte rows.  `use` = 0: the maps could
+// not be encoded (e.g. a stride of 0) and the rows are staged with per-thread cp.async copies instead.
+struct PrepMaps {
+    CUtensorMap m[3];
+    int use;
 };
 
 __device__ __forceinline__ void store_bf16x4(unsigned char* tile, uint32_t off, const float (&x)[4]) {
@@ -199,7 +210,7 @@ __device__ __forceinline__ void mma_split_a(uint32_t d_tmem, uint32_t a_hi, uint
                     make_sdesc(b_tile + ks * 2048, b_lbo, 1024, kSwizzle128B), idesc, (s2 | ks) != 0);
 }
 
-__global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
+__global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p, const __grid_constant__ PrepMaps maps) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     PrepMisc& ms = *reinterpret_cast<PrepMisc*>(sm + P_MISC);
@@ -236,25 +247,35 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
     const float scale = rsqrtf((float)kDk);
     unsigned char* wrec = reinterpret_cast<unsigned char*>(p.ws) + chunk * kTcChunkBytes;
 
-    // raw q/k/v rows of the chunk into the (still unused) work region, all in flight at once:
-    // 3 x 64 rows x 16 pieces of 16 bytes, 12 per thread; rows past T are zero-filled
-    for (int i = tid; i < 3 * kChunk * 16; i += kPrepThreads) {
-        const int tsr = i >> 10, row = (i >> 4) & 63, piece = i & 15;
-        const View4& V = tsr == 0 ? p.q : (tsr == 1 ? p.k : p.v);
-        const int64_t t = t0 + row;
-        const bool in = t < t_lim;
-        const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(V.p) + (int64_t)b * V.sb +
-                                   (in ? t : t0) * V.st + (int64_t)h * V.sh + 8 * piece;
-        cp_async16(sm + P_RAW + (tsr * kChunk + row) * 256 + piece * 16, src, in ? 16u : 0u);
+    // raw q/k/v rows of the chunk into the (still unused) work region [3][64 rows][256 B]: three TMA boxes
+    // (rows past T read as zero), or without tensor maps 3 x 64 rows x 16 pieces of 16 bytes, 12 per thread,
+    // all in flight at once (rows past the sequence's end zero-filled)
+    if (tid == 32) {
+        mbar_init(&ms.bar, 1);
+        mbar_init(&ms.bar_in, 1);
+        fence_mbar_init();
+        if (maps.use) {
+            mbar_arrive_expect_tx(&ms.bar_in, 3 * kChunk * 256);
+#pragma unroll
+            for (int tsr = 0; tsr < 3; ++tsr)
+                tma_load_4d(sm + P_RAW + tsr * kChunk * 256, &maps.m[tsr], 0, h, (int)t0, b, &ms.bar_in);
+        }
     }
-    cp_async_commit();
+    if (!maps.use) {
+        for (int i = tid; i < 3 * kChunk * 16; i += kPrepThreads) {
+            const int tsr = i >> 10, row = (i >> 4) & 63, piece = i & 15;
+            const View4& V = tsr == 0 ? p.q : (tsr == 1 ? p.k : p.v);
+            const int64_t t = t0 + row;
+            const bool in = t < t_lim;
+            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(V.p) + (int64_t)b * V.sb +
+                                       (in ? t : t0) * V.st + (int64_t)h * V.sh + 8 * piece;
+            cp_async16(sm + P_RAW + (tsr * kChunk + row) * 256 + piece * 16, src, in ? 16u : 0u);
+        }
+        cp_async_commit();
+    }
     if (warp == 0) {
         tmem_alloc(&ms.tmem, kPrepTmemCols);
         tmem_relinquish();
-    }
-    if (tid == 32) {
-        mbar_init(&ms.bar, 1);
-        fence_mbar_init();
     }
     if (tid < kChunk) {  // g, beta of the chunk (rows past the sequence's end are the zero padding)
         const int64_t t = t0 + tid;
@@ -267,7 +288,21 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         ms.beta[tid] = bv;
     }
 
-    cp_async_wait_all();
+    bool in_ok = true;
+    if (maps.use) {
+        __syncthreads();  // the barrier is initialised before anyone waits on it
+        in_ok = mbar_wait(&ms.bar_in, 0, kWaitNs);
+        if (t0 + kChunk > t_lim) {  // a packed sequence's last chunk: the rows past its end belong to the next
+            const int valid = (int)(t_lim - t0);
+            for (int i = tid; i < 3 * kChunk * 16; i += kPrepThreads) {
+                const int tsr = i >> 10, row = (i >> 4) & 63, piece = i & 15;
+                if (row >= valid)
+                    *reinterpret_cast<uint4*>(sm + P_RAW + (tsr * kChunk + row) * 256 + piece * 16) = make_uint4(0, 0, 0, 0);
+            }
+        }
+    } else {
+        cp_async_wait_all();
+    }
     __syncthreads();
     // ---- 1. normalised rows -> swizzled bf16 tiles (qwen3_5_transformers.py:122-137).
     //      Each warp owns 4 rows of the staged copy, in batches of 2 whose 4 sums of squares are
@@ -351,7 +386,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         ms.ekd[2 * lane] = __expf(gcl - gc0);
         ms.ekd[2 * lane + 1] = __expf(gcl - x);
     }
-    bool ok = mbar_wait(&ms.bar, 0, kWaitNs);  // the barrier below publishes gc, e^gc and e^(gc_last - gc)
+    bool ok = mbar_wait(&ms.bar, 0, kWaitNs) && in_ok;  // the barrier below publishes gc, e^gc and e^(gc_last - gc)
     tc_fence_after();
 
     // ---- 3. L = -(beta_i G_k e^(gc_i-gc_j)) strictly lower (:152-153), Aqk = Dk^-1/2 G_q e^(gc_i-gc_j) causal (:172)
@@ -724,6 +759,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p) {
         bulk_wait_read_all();  // shared memory must outlive every copy that reads it
     }
     if (!ok && tid == 0) report(p.err, kErrTimeoutPrep);
+    if (!in_ok) mbar_wait(&ms.bar_in, 0, kWaitNs);  // no box may land after the CTA has left
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tm, kPrepTmemCols);
@@ -2284,13 +2320,50 @@ cudaError_t smem_attr_once(Kernel kernel, int bytes, std::atomic<uint64_t>& done
     return e;
 }
 
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            f = nullptr;
+        }
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// The prep's box map of a bf16 [B, T, H, 128] view (strides in elements, all multiples of 8: the tensor-core
+// path's condition).  A dimension of extent 1 gets a nominal stride (its coordinate is always 0).
+bool encode_rows_map(CUtensorMap* m, const View4& v, int64_t B, int64_t T, int64_t H) {
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc || B <= 0 || T <= 0 || H <= 0) return false;
+    const cuuint64_t sh = H > 1 ? (cuuint64_t)v.sh * 2 : 256;
+    const cuuint64_t st = T > 1 ? (cuuint64_t)v.st * 2 : sh * (cuuint64_t)H;
+    const cuuint64_t sb = B > 1 ? (cuuint64_t)v.sb * 2 : st * (cuuint64_t)T;
+    const cuuint64_t dims[4] = {(cuuint64_t)kDk, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+    const cuuint64_t strides[3] = {sh, st, sb};
+    const cuuint32_t box[4] = {(cuuint32_t)kDk, 1, (cuuint32_t)kChunk, 1}, estr[4] = {1, 1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(v.p), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
 cudaError_t launch_chunk_tc_prep(const ChunkParams& p, cudaStream_t stream) {
     static_assert(P_SMEM <= 227 * 1024, "shared memory budget");
+    static_assert(sizeof(PrepMisc) <= 1088, "misc region");
     static std::atomic<uint64_t> attr_done{0};
     cudaError_t e = smem_attr_once(gdn_prep_tc, (int)P_SMEM, attr_done);
     if (e != cudaSuccess) return e;
     const int64_t nchunks = p.cu_seqlens ? (int64_t)p.max_chunks * p.H : (int64_t)p.B * p.H * p.NC;
-    gdn_prep_tc<<<(unsigned)nchunks, kPrepThreads, P_SMEM, stream>>>(p);
+    PrepMaps maps{};
+    // the maps are 4-D over (D, H, T, B) with a 32-bit token coordinate
+    maps.use = p.T <= 0x7fffffffLL && encode_rows_map(&maps.m[0], p.q, p.B, p.T, p.H) &&
+               encode_rows_map(&maps.m[1], p.k, p.B, p.T, p.H) && encode_rows_map(&maps.m[2], p.v, p.B, p.T, p.H);
+    gdn_prep_tc<<<(unsigned)nchunks, kPrepThreads, P_SMEM, stream>>>(p, maps);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     note_launch();
     return cudaSuccess;

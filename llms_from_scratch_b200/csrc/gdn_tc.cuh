@@ -141,6 +141,19 @@ __device__ __forceinline__ void bulk_wait_read_keep1() {
     asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 
+// Tiled TMA load of one box of a 4-D tensor map (cp.async.bulk.tensor, tile mode) into this CTA's shared
+// memory, completing its bytes on `bar`.  `tmap` is the address of a CUtensorMap in kernel-parameter
+// (__grid_constant__), constant or global memory; c0 is the innermost coordinate.  Elements outside the
+// tensor read as zero.
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // 16-byte asynchronous global -> shared copy (cp.async); src_bytes = 0 zero-fills the destination.
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),

@@ -246,6 +246,50 @@ def test_recurrent_vs_oracle(in_dtype, T):
     assert_parity(s, rs, in_dtype, "state")
 
 
+@pytest.mark.parametrize("in_dtype", ["fp32", "bf16"])
+@pytest.mark.parametrize("B,H,std", [(10, 16, 0.02), (19, 16, 0.5), (32, 16, 0.5), (3, 64, 0.02)])
+def test_recurrent_decode_batches_vs_oracle(in_dtype, B, H, std):
+    """One decode token over decode-sized batches (160 to 512 heads, the config-4 batch of 32 among them),
+    with small and large initial states."""
+    q, k, v, g, beta, s0 = O.make_inputs(B, 1, H, seed=300 + B, in_dtype=in_dtype, init_state_std=std,
+                                         normalize_qk=False)
+    o, s = run_rec(q, k, v, g, beta, s0, in_dtype)
+    ro, rs = O.recurrent_gated_delta_rule(q, k, v, g, beta, s0, True, use_qk_l2norm_in_kernel=True,
+                                          in_dtype=in_dtype)
+    assert_parity(o, ro, in_dtype, "out")
+    assert_parity(s, rs, in_dtype, "state")
+
+
+def test_recurrent_decode_batch_variants():
+    """A decode batch without an initial state, without a final state and in place, each equal to the
+    oracle; and the batch equals the same sequences decoded one call each."""
+    m = ops()
+    B, H = 20, 16
+    q, k, v, g, beta, s0 = O.make_inputs(B, 1, H, seed=41, in_dtype="bf16", init_state_std=0.3, normalize_qk=False)
+    tq, tk, tv = (dev(x, torch.bfloat16) for x in (q, k, v))
+    tg, tb, ts = dev(g), dev(beta), dev(s0)
+    ro, rs = O.recurrent_gated_delta_rule(q, k, v, g, beta, s0, True, use_qk_l2norm_in_kernel=True, in_dtype="bf16")
+    zo, zs = O.recurrent_gated_delta_rule(q, k, v, g, beta, None, True, use_qk_l2norm_in_kernel=True, in_dtype="bf16")
+    o, s = m.fast_recurrent_gated_delta_rule(tq, tk, tv, tg, tb, None, True, use_qk_l2norm_in_kernel=True)
+    assert_parity(o.float().cpu().numpy(), zo, "bf16", "zero initial state: out")
+    assert_parity(s.cpu().numpy(), zs, "bf16", "zero initial state: state")
+    o, s = m.fast_recurrent_gated_delta_rule(tq, tk, tv, tg, tb, ts, False, use_qk_l2norm_in_kernel=True)
+    assert s is None
+    assert_parity(o.float().cpu().numpy(), ro, "bf16", "no final state: out")
+    groups = [m.fast_recurrent_gated_delta_rule(tq[b:b + 1], tk[b:b + 1], tv[b:b + 1], tg[b:b + 1], tb[b:b + 1],
+                                                ts[b:b + 1], True, use_qk_l2norm_in_kernel=True) for b in range(B)]
+    state = ts.clone()
+    o, s = m.fast_recurrent_gated_delta_rule(tq, tk, tv, tg, tb, state, True, use_qk_l2norm_in_kernel=True,
+                                             out_state=state)
+    assert s.data_ptr() == state.data_ptr()
+    assert_parity(o.float().cpu().numpy(), ro, "bf16", "in place: out")
+    assert_parity(state.cpu().numpy(), rs, "bf16", "in place: state")
+    torch.testing.assert_close(o, torch.cat([x[0] for x in groups]), rtol=1e-2, atol=1e-5)
+    torch.testing.assert_close(state, torch.cat([x[1] for x in groups]), rtol=1e-5, atol=1e-6)
+    from llms_from_scratch_b200.ops import check_device_errors
+    check_device_errors(sync=True)  # raises if a bounded wait gave up
+
+
 def test_recurrent_in_place_decode_matches_chunk_prefix():
     """Prefill via the chunk kernel, then 8 in-place single-token decode steps ==
     the chunk kernel over the whole sequence (the model's prefill->decode path)."""
