@@ -709,7 +709,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p, co
     if (tid == 32) bulk_wait_read_all();       // KQ is rewritten below: the Q' copy must have read it
     tc_fence_after();
 
-    // ---- 9. M = e^gc_last I - M' (bf16 image into KQ), b (fp32 column tiles into V / the P tiles)
+    // ---- 9. M = e^gc_last I - M' (bf16 image into KQ, then one bulk copy), b (fp32, straight to the record)
     if (!__syncthreads_or(!ok)) {
         const int dk = 32 * quad + lane;
         const float gamma = ms.egc[kChunk - 1];
@@ -728,17 +728,18 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p, co
                 store_bf16x8(sm + P_KQ, sw128_offset(dk, col, 128), m);
             }
         }
-        const uint32_t btile[4] = {P_V, P_W, P_W + 16384, P_W + 32768};
+        // b straight from the accumulator to the record (chunk-major tiles: a warp's store is 512 contiguous
+        // bytes), so only the M image is left for the bulk copy to drain before the CTA can leave
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
             float v[16];
             const int c0 = 32 * part + 16 * cc;
             tmem_ld16(tmem_addr(tm, 32 * quad, 128 + c0), v);
             tmem_ld_wait();
-            unsigned char* blk = sm + btile[c0 >> 5];
+            unsigned char* blk = wrec + kTcB + (c0 >> 5) * 16384;
 #pragma unroll
             for (int q4 = 0; q4 < 4; ++q4)
-                *reinterpret_cast<float4*>(blk + ((((c0 & 31) >> 2) + q4) * 128 + dk) * 16) =  // chunk-major tile
+                *reinterpret_cast<float4*>(blk + ((((c0 & 31) >> 2) + q4) * 128 + dk) * 16) =
                     make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]);
         }
     } else {
@@ -750,10 +751,6 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_tc(ChunkParams p, co
     if (tid == 32) {
         if (ok) {
             bulk_s2g(wrec + kTcM, sm + P_KQ, 32768);
-            bulk_s2g(wrec + kTcB + 0 * 16384, sm + P_V, 16384);
-            bulk_s2g(wrec + kTcB + 1 * 16384, sm + P_W, 16384);
-            bulk_s2g(wrec + kTcB + 2 * 16384, sm + P_W + 16384, 16384);
-            bulk_s2g(wrec + kTcB + 3 * 16384, sm + P_W + 32768, 16384);
             bulk_commit();
         }
         bulk_wait_read_all();  // shared memory must outlive every copy that reads it
