@@ -20,10 +20,11 @@
 //
 // gdn_prep_tc: one CTA (16 warps) per (batch, head, 64-token chunk), two CTAs per
 // SM (105 KB of shared memory each, one work region reused phase by phase), so
-// one CTA's memory and barrier waits overlap the other's work; the output images
-// leave with asynchronous bulk copies.  Operands that share a B matrix are
-// stacked into M=128 MMAs so every accumulator fills all 128 TMEM lanes.
-//   1. rows of q, k, v (cp.async-staged at entry, all in flight at once) ->
+// one CTA's memory and barrier waits overlap the other's work; the bf16 images
+// leave with asynchronous bulk copies, the fp32 tiles straight from TMEM.
+// Operands that share a B matrix are stacked into M=128 MMAs so every
+// accumulator fills all 128 TMEM lanes.
+//   1. rows of q, k, v (three TMA boxes of the caller's view at entry) ->
 //      l2norm (16-bit rounding as the reference) -> bf16 128B-swizzled tiles
 //      [k^; q^] and v in shared memory
 //   2. [k^; q^] k^T on the tensor cores -> G_k (lanes 0-63) and G_q (64-127)
