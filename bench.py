@@ -986,6 +986,17 @@ def main():
     if not args.no_decode_model:
         decode_model = decode_model_leg(torch, device, peak_l)
         torch.cuda.empty_cache()
+        if world > 1:  # config 4 runs as replicas: every GPU decodes its own batch, no exchange
+            mine = torch.tensor([decode_model["batch1_tok_s"] or 0.0, decode_model["batch32_tok_s"] or 0.0],
+                                dtype=torch.float64, device=device)
+            allr = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(allr, mine)
+            per = [x.tolist() for x in allr]
+            decode_model["replicas"] = {"n": world, "scaling": "replicas (each GPU decodes its own batch; no exchange)",
+                                        "batch1_tok_s_total": sum(x[0] for x in per),
+                                        "batch32_tok_s_total": sum(x[1] for x in per),
+                                        "per_rank": [{"rank": r, "batch1_tok_s": x[0], "batch32_tok_s": x[1]}
+                                                     for r, x in enumerate(per)]}
         if rank == 0 and not args.no_reference_triton:
             decode_model["reference_decode"] = reference_decode_leg(torch, device)
     ref_triton = None
