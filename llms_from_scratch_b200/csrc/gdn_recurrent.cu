@@ -27,7 +27,8 @@ __global__ void __launch_bounds__(kRecThreads, 8) gdn_recurrent_kernel(Recurrent
     __shared__ __align__(16) float ks[kDk];
     __shared__ float vs[kRecCols];
     __shared__ float gb[2];
-    __shared__ float red[kRecWarps][kRecCols];
+    __shared__ float red[kRecWarps][kRecCols];   // kv partials
+    __shared__ float red2[kRecWarps][kRecCols];  // o partials (their own array: no barrier between the two)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bh = blockIdx.x / kRecSlices, slice = blockIdx.x % kRecSlices;
@@ -110,16 +111,17 @@ __global__ void __launch_bounds__(kRecThreads, 8) gdn_recurrent_kernel(Recurrent
                 op += S[r + i] * qq[i];
             }
         }
-        __syncthreads();  // every warp has read red (kv) and vs/gb/qs/ks of this token
-        red[warp][lane] = op;
+        red2[warp][lane] = op;
         __syncthreads();
         if (warp == 0) {
             float o = 0.f;
 #pragma unroll
-            for (int w = 0; w < kRecWarps; ++w) o += red[w][lane];
+            for (int w = 0; w < kRecWarps; ++w) o += red2[w][lane];
             store_elem(p.out, (int64_t)b * p.out_sb + t * p.out_st + (int64_t)h * p.out_sh + col, p.out_dtype, o);
         }
-        __syncthreads();  // red is rewritten by the next token's kv partials
+        // No barrier before the next token: its writes of qs/ks/vs/gb come before its first barrier, and
+        // every read of them (and of red) for this token came before the barrier above; red2, which warp 0
+        // is still reading, is rewritten only after the next token's second barrier.
     }
 
     if (p.hT) {
