@@ -599,7 +599,8 @@ __global__ void __launch_bounds__(kDecThreads, 4) gdn_model_gdn_decode_kernel(Gd
     __shared__ __align__(16) float ks[128];
     __shared__ __align__(16) float vs[128];
     __shared__ float gb[2];
-    __shared__ __align__(16) float red[kDecWarps][128];
+    __shared__ __align__(16) float red[kDecWarps][128];   // kv partials
+    __shared__ __align__(16) float red2[kDecWarps][128];  // o partials (their own array: no barrier between the two)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
     const int r0 = kDecRows * warp, c0 = 4 * lane;
@@ -710,8 +711,7 @@ __global__ void __launch_bounds__(kDecThreads, 4) gdn_model_gdn_decode_kernel(Gd
         srows[warp][r][lane] = x;
         op.x += x.x * qr, op.y += x.y * qr, op.z += x.z * qr, op.w += x.w * qr;
     }
-    __syncthreads();  // every warp has read red (kv)
-    *reinterpret_cast<float4*>(&red[warp][c0]) = op;
+    *reinterpret_cast<float4*>(&red2[warp][c0]) = op;
     // the new state leaves while the output is reduced
 #pragma unroll
     for (int r = 0; r < kDecRegRows; ++r)
@@ -724,7 +724,7 @@ __global__ void __launch_bounds__(kDecThreads, 4) gdn_model_gdn_decode_kernel(Gd
         float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int w = 0; w < kDecWarps; ++w) {
-            const float4 x = *reinterpret_cast<const float4*>(&red[w][c0]);
+            const float4 x = *reinterpret_cast<const float4*>(&red2[w][c0]);
             o[0] += x.x, o[1] += x.y, o[2] += x.z, o[3] += x.w;
         }
         float ss = 0.f;
