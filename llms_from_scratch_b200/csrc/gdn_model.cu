@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(256) gdn_model_silu_mul_kernel(SiluArgs a) {
 //             gdn_model_add_rms_norm_partials), so no atomics and a deterministic result.
 enum : int { kStore = 0, kSiluMul = 1, kPartial = 2 };
 constexpr int kGemmMaxM = 32;
-constexpr int kStages = 6;
+constexpr int kStages = 10;
 
 // NW warps per CTA own 16 NW rows of W; a stage holds those rows' and x's 64 columns (bf16)
 template <int MT, int NW>
