@@ -1756,7 +1756,6 @@ __global__ void __launch_bounds__(kWtThreads, 1) gdn_bwd_wy_tc(BwdParams p) {
 
     // ---- 4. row-wise terms (rows ty + 32 r, columns cols[hlf] .. + 3), X read back as hi + lo
     if (ok) {
-        const __nv_bfloat16* xtile = reinterpret_cast<const __nv_bfloat16*>(sm + W_XA);
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int i = ty + 32 * r;
