@@ -1070,6 +1070,309 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
     if (warp == 0) tmem_dealloc(tm, L::kTmemCols);
 }
 
+// ============================================================================ lean scan (many heads)
+//
+// gdn_scan_lean_tc: the scan for problems with more (batch, head) chains than SMs.  gdn_scan_tc holds an SM per
+// chain (~160-200 KB of shared memory); with the records in DRAM rather than L2 a chain then waits on its record
+// loads (~2.4 us a chunk at B=64, H=16), and one chain per SM leaves that latency exposed.  This kernel runs a
+// chain in 112 KiB and 512 threads, so two share an SM.  One CTA per (batch, head, 32-column slice of Dv):
+//   warps 0-7   chain: thread = state row dk = 32 (w % 4) + lane (its TMEM lane), columns 16 (w / 4) .. +15;
+//               S_{c+1} = accumulator + b_c as the next bf16 operand tile, handed to the MMA warp through
+//               named barrier 1; b read straight from the record into registers two chunks ahead
+//   warps 8-11  outputs: thread = output row 16 (w - 8) + lane (lanes 0-15, the M=64 accumulator's rows), the
+//               CTA's 32 columns; o_c = accumulator + o0_c (o0 read from the record one chunk ahead)
+//   warp 12     M images into the stage freed by the state product of chunk c-2, and every record pulled into
+//               L2 four chunks ahead
+//   warp 13     MMAs (one elected lane of the converged warp): the state product M_c S_c, then the output
+//               product Q'_c S_c
+//   warp 14     Q' images into the stage freed by the output product of chunk c-2
+//   warp 15     idle
+// Shared memory: M images [2][32 KiB] | S_c operand tiles [2][8 KiB] (bf16 [128 dk][32], MN-major, 64B-swizzled) |
+// Q' images [2][16 KiB], with the barriers in the 1 KiB alignment slack.  TMEM: state accumulator [0, 32),
+// output accumulators [32, 64) and [64, 96) by chunk parity.
+
+constexpr int kLeanW = 32;                      // state columns per CTA
+constexpr int kLeanSlices = kDv / kLeanW;       // CTAs per (batch, head)
+constexpr int kLeanThreads = 512;
+constexpr uint32_t LN_M = 0;
+constexpr uint32_t LN_S = 65536;
+constexpr uint32_t LN_Q = 81920;
+constexpr uint32_t LN_TILES = 114688;
+constexpr uint32_t kLeanSmem = LN_TILES + 1024;  // + alignment slack, which also holds LeanMisc
+constexpr uint32_t kLeanTmemCols = 128;
+constexpr uint32_t kLeanBar = 1;                 // named barrier: chain warps (256) arrive with S_c stored, MMA warp waits
+constexpr uint32_t kLeanBarCount = 288;
+constexpr int kLnOut = 8, kLnProdM = 12, kLnMma = 13, kLnProdQ = 14;
+constexpr int kLeanPrefetch = 4;                 // chunks ahead that the M producer pulls into L2
+static_assert(kLeanSmem <= 227 * 1024, "lean scan shared memory");
+
+struct LeanMisc {
+    uint64_t full_m[2];  // M image of the stage landed (tx)
+    uint64_t m_free[2];  // the state product that read the stage completed (tcgen05.commit)
+    uint64_t full_q[2];  // Q' image of the stage landed (tx)
+    uint64_t q_free[2];  // the output product that read the stage completed
+    uint64_t mma_s;      // chunk c's state product completed
+    uint64_t mma_o[2];   // output product of chunk c completed, by chunk parity
+    uint64_t o_free[2];  // the output warps read output accumulator p (128 arrivals)
+    uint64_t done;       // every product the MMA warp issued has completed
+    uint32_t tmem;
+    int abort;           // a party gave up: the others stop waiting and skip their work
+};
+
+// Byte offset of element (row, col), col < 32, in an MN-major 64B-swizzled tile of 16-bit elements: 64-byte
+// rows, 8-row atoms of 512 bytes packed along the rows (SBO = 512); the 16-byte chunk c of row r is stored at
+// chunk c ^ ((r / 2) % 4).
+__device__ __forceinline__ uint32_t sw64_offset(uint32_t row, uint32_t col) {
+    return row * 64u + ((((col >> 3) ^ (row >> 1)) & 3u) << 4) + (col & 7u) * 2u;
+}
+
+__device__ __forceinline__ bool lean_aborted(const LeanMisc& ms) {
+    return *reinterpret_cast<const volatile int*>(&ms.abort) != 0;
+}
+
+// Bounded wait on an mbarrier phase that also gives up once another party has aborted.
+__device__ __forceinline__ bool lean_wait(uint64_t* bar, uint32_t parity, const LeanMisc& ms) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    const long long budget = (long long)(kWaitNs * 2);
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (lean_aborted(ms) || clock64() - t0 > budget) return false;
+    }
+}
+
+// 16 or 32 fp32 values of one row of a chunk-major record tile (element (row, col) at ((col / 4) * rows + row) * 4
+// + col % 4): columns col0 .. col0+kN-1, 16-byte loads, each a 512- or 256-byte run across the warp.
+template <int kRows, int kN>
+__device__ __forceinline__ void load_cm(const unsigned char* tile, int row, int col0, float (&v)[kN]) {
+#pragma unroll
+    for (int q4 = 0; q4 < kN / 4; ++q4) {
+        const float4 x = *reinterpret_cast<const float4*>(tile + ((int64_t)((col0 >> 2) + q4) * kRows + row) * 16);
+        v[4 * q4] = x.x;
+        v[4 * q4 + 1] = x.y;
+        v[4 * q4 + 2] = x.z;
+        v[4 * q4 + 3] = x.w;
+    }
+}
+
+__global__ void __launch_bounds__(kLeanThreads, 2) gdn_scan_lean_tc(ChunkParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+    unsigned char* sm = smem_raw + pad;
+    LeanMisc& ms = *reinterpret_cast<LeanMisc*>(pad >= sizeof(LeanMisc) ? smem_raw : sm + LN_TILES);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int bh = (int)(blockIdx.x / kLeanSlices), slice = (int)(blockIdx.x % kLeanSlices);
+    const int b = bh / p.H, h = bh % p.H, NC = p.NC;
+    const int dv0 = slice * kLeanW;  // first state column of the CTA
+    const int64_t rec0 = (int64_t)bh * NC;
+    const unsigned char* wsb = reinterpret_cast<const unsigned char*>(p.ws);
+    auto record = [&](int c) { return wsb + (rec0 + c) * kTcChunkBytes; };
+
+    if (tid == 0) {
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&ms.full_m[s], 1);
+            mbar_init(&ms.m_free[s], 1);
+            mbar_init(&ms.full_q[s], 1);
+            mbar_init(&ms.q_free[s], 1);
+            mbar_init(&ms.mma_o[s], 1);
+            mbar_init(&ms.o_free[s], 128);
+        }
+        mbar_init(&ms.mma_s, 1);
+        mbar_init(&ms.done, 1);
+        ms.abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&ms.tmem, kLeanTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = ms.tmem;
+    const uint32_t sbase = smem_u32(sm);
+    bool ok = true;
+
+    if (warp == kLnMma) {
+        // ---------------- MMAs: the whole warp runs the loop, one elected lane issues
+        const uint32_t leader = elect_one();
+        const uint32_t idS = make_idesc_f16(128, kLeanW, false, true, true);
+        const uint32_t idO = make_idesc_f16(64, kLeanW, false, true, true);
+        const uint64_t dM = make_sdesc(sbase + LN_M, 16, 1024, kSwizzle128B);
+        const uint64_t dQ = make_sdesc(sbase + LN_Q, 16, 1024, kSwizzle128B);
+        const uint64_t dS = make_sdesc(sbase + LN_S, 8192, 512, kSwizzle64B);
+        for (int c = 0; c < NC; ++c) {
+            const int s = c & 1;
+            named_bar_sync(kLeanBar, kLeanBarCount);  // S_c is in operand tile s
+            bool go = ok && !lean_aborted(ms);
+            if (go) go = lean_wait(&ms.full_m[s], (c >> 1) & 1, ms);
+            if (!__all_sync(0xffffffffu, go)) {
+                ok = false;
+                ms.abort = 1;
+                continue;
+            }
+            tc_fence_after();
+            // state first: it is the only product on the sequential path
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+                mma_f16_if(leader, tm + 0, dM + (uint64_t)(((s * 32768) + ((ks >> 2) * 16384) + (ks & 3) * 32) >> 4),
+                           dS + (uint64_t)((s * 8192 + ks * 1024) >> 4), idS, ks > 0);
+            mma_commit_if(leader, &ms.mma_s);
+            mma_commit_if(leader, &ms.m_free[s]);
+            go = lean_wait(&ms.full_q[s], (c >> 1) & 1, ms);
+            if (go && c >= 2) go = lean_wait(&ms.o_free[s], ((c >> 1) - 1) & 1, ms);
+            if (!__all_sync(0xffffffffu, go)) {
+                ok = false;
+                ms.abort = 1;
+                continue;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+                mma_f16_if(leader, tm + 32 + 32 * s,
+                           dQ + (uint64_t)(((s * 16384) + ((ks >> 2) * 8192) + (ks & 3) * 32) >> 4),
+                           dS + (uint64_t)((s * 8192 + ks * 1024) >> 4), idO, ks > 0);
+            mma_commit_if(leader, &ms.mma_o[s]);
+            mma_commit_if(leader, &ms.q_free[s]);
+            __syncwarp();
+        }
+        mma_commit_if(leader, &ms.done);  // arrives once every product issued above has completed
+        __syncwarp();
+        if (!mbar_wait(&ms.done, 0, kWaitNs)) ok = false;
+    } else if (warp == kLnProdM || warp == kLnProdQ) {
+        // ---------------- producers (lane 0): M and Q' images into the stage the chunk two back freed
+        if (lane == 0) {
+            const bool mq = warp == kLnProdM;
+            int issued = 0;
+            for (int j = 0; j < NC; ++j) {
+                if (lean_aborted(ms)) break;
+                const int st = j & 1;
+                if (mq && j + kLeanPrefetch < NC) {  // the whole record of a later chunk into L2
+                    const unsigned char* pre = record(j + kLeanPrefetch);
+                    bulk_prefetch_l2(pre + kTcM, 32768 + 16384);
+                    bulk_prefetch_l2(pre + kTcB + (int64_t)slice * 128 * kLeanW * 4, 128 * kLeanW * 4);
+                    bulk_prefetch_l2(pre + kTcO0 + (int64_t)slice * 64 * kLeanW * 4, 64 * kLeanW * 4);
+                }
+                if (j >= 2 && !lean_wait(mq ? &ms.m_free[st] : &ms.q_free[st], ((j >> 1) - 1) & 1, ms)) {
+                    ok = false;
+                    break;
+                }
+                if (mq) {
+                    mbar_arrive_expect_tx(&ms.full_m[st], 32768);
+                    bulk_g2s(sm + LN_M + st * 32768, record(j) + kTcM, 32768, &ms.full_m[st]);
+                } else {
+                    mbar_arrive_expect_tx(&ms.full_q[st], 16384);
+                    bulk_g2s(sm + LN_Q + st * 16384, record(j) + kTcQ, 16384, &ms.full_q[st]);
+                }
+                ++issued;
+            }
+            // no copy may land after the CTA has left
+            for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
+                if (!mbar_wait(mq ? &ms.full_m[j & 1] : &ms.full_q[j & 1], (j >> 1) & 1, kWaitNs)) ok = false;
+        }
+    } else if (warp < kLnOut) {
+        // ---------------- chain: thread = state row dk (TMEM lane 32 (w % 4) + lane), columns 16 (w / 4) .. +15
+        const int dk = 32 * (warp & 3) + lane, cb = 16 * (warp >> 2);
+        const int64_t srow = ((int64_t)bh * kDk + dk) * kDv + dv0 + cb;
+        {
+            float s0[16];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+                const float4 v = p.h0 ? *reinterpret_cast<const float4*>(p.h0 + srow + 4 * q4)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                s0[4 * q4] = v.x;
+                s0[4 * q4 + 1] = v.y;
+                s0[4 * q4 + 2] = v.z;
+                s0[4 * q4 + 3] = v.w;
+            }
+#pragma unroll
+            for (int q8 = 0; q8 < 2; ++q8) store_bf16x8(sm + LN_S, sw64_offset(dk, cb + 8 * q8), s0 + 8 * q8);
+            fence_proxy_async_smem();
+        }
+        if (NC > 0) named_bar_arrive(kLeanBar, kLeanBarCount);  // S_0 for chunk 0
+        // b_c of this thread's row and columns lives in bA (c even) or bB (c odd), read two chunks ahead
+        float bA[16], bB[16];
+        if (NC > 0) load_cm<128, 16>(record(0) + kTcB, dk, dv0 + cb, bA);
+        if (NC > 1) load_cm<128, 16>(record(1) + kTcB, dk, dv0 + cb, bB);
+        auto chain_step = [&](int c, float (&bc)[16]) {
+            // ---- S_{c+1} = M_c S_c + b_c (the sequential path)
+            if (ok && lean_aborted(ms)) ok = false;
+            if (ok) ok = lean_wait(&ms.mma_s, c & 1, ms);
+            ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: the warp loads or skips together
+            if (ok) {
+                tc_fence_after();
+                float d[16];
+                tmem_ld16(tmem_addr(tm, 32 * (warp & 3), cb), d);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) d[e] += bc[e];
+                if (c + 1 < NC) {  // tile (c+1) % 2 held S_{c-1}, whose products completed before chunk c's state
+#pragma unroll
+                    for (int q8 = 0; q8 < 2; ++q8)
+                        store_bf16x8(sm + LN_S + ((c + 1) & 1) * 8192, sw64_offset(dk, cb + 8 * q8), d + 8 * q8);
+                    fence_proxy_async_smem();
+                } else if (p.hT) {
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4)
+                        *reinterpret_cast<float4*>(p.hT + srow + 4 * q4) =
+                            make_float4(d[4 * q4], d[4 * q4 + 1], d[4 * q4 + 2], d[4 * q4 + 3]);
+                }
+            }
+            if (c + 1 < NC) {
+                tc_fence_before();
+                named_bar_arrive(kLeanBar, kLeanBarCount);  // every chunk, also after a failure
+            }
+            if (ok && c + 2 < NC) load_cm<128, 16>(record(c + 2) + kTcB, dk, dv0 + cb, bc);  // bc is free: b_{c+2}
+            if (!ok) ms.abort = 1;
+        };
+        for (int c = 0; c < NC; c += 2) {
+            chain_step(c, bA);
+            if (c + 1 < NC) chain_step(c + 1, bB);
+        }
+    } else if (warp < kLnProdM) {
+        // ---------------- outputs: thread = output row 16 q + lane (lanes 0-15), the CTA's 32 columns
+        const int q = warp - kLnOut, tok = 16 * q + lane;
+        float ov[32];
+        if (NC > 0 && lane < 16) load_cm<64, 32>(record(0) + kTcO0, tok, dv0, ov);
+        for (int c = 0; c < NC; ++c) {
+            if (ok && lean_aborted(ms)) ok = false;
+            if (ok) ok = lean_wait(&ms.mma_o[c & 1], (c >> 1) & 1, ms);
+            ok = __all_sync(0xffffffffu, ok);
+            if (ok) {
+                tc_fence_after();
+                const int64_t t = (int64_t)c * kChunk + tok;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    float o[16];
+                    tmem_ld16(tmem_addr(tm, 32 * q, 32 + 32 * (c & 1) + 16 * half), o);
+                    tmem_ld_wait();
+                    if (lane < 16 && t < p.T && p.out) {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) o[e] += ov[16 * half + e];
+                        unsigned char* dst = reinterpret_cast<unsigned char*>(p.out) +
+                                             2 * ((int64_t)b * p.out_sb + t * p.out_st + (int64_t)h * p.out_sh + dv0 +
+                                                  16 * half);
+                        store_bf16x8(dst, 0, o);
+                        store_bf16x8(dst, 16, o + 8);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&ms.o_free[c & 1]);  // every chunk, also after a failure
+            if (ok && c + 1 < NC && lane < 16) load_cm<64, 32>(record(c + 1) + kTcO0, tok, dv0, ov);
+            if (!ok) ms.abort = 1;
+        }
+    }
+    if (!ok) ms.abort = 1;
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tm, kLeanTmemCols);
+    }
+    if (tid == 0 && lean_aborted(ms)) report(p.err, kErrTimeoutScan);
+}
+
 // ============================================================================ reverse scan (backward)
 //
 // dS_c = M_c^T dS_{c+1} + Q'_c^T do_c over the forward's records, chunks in reverse: the transposed affine
@@ -2382,8 +2685,20 @@ cudaError_t launch_scan_w(const ChunkParams& p, cudaStream_t stream) {
 }
 }  // namespace
 
+cudaError_t launch_scan_lean(const ChunkParams& p, cudaStream_t stream) {
+    static std::atomic<uint64_t> attr_done{0};
+    cudaError_t e = smem_attr_once(gdn_scan_lean_tc, (int)kLeanSmem, attr_done);
+    if (e != cudaSuccess) return e;
+    gdn_scan_lean_tc<<<(unsigned)((int64_t)p.B * p.H * kLeanSlices), kLeanThreads, kLeanSmem, stream>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    note_launch();
+    return cudaSuccess;
+}
+
 // The scan is a chain of dependent chunk steps per CTA: 16-column slices shorten each step, but double the
-// CTAs; they are used while all of them fit in one wave (one CTA per SM), 32-column slices otherwise.
+// CTAs; they are used while all of them fit in one wave (one CTA per SM).  Beyond that the lean scan runs two
+// 32-column chains per SM (the 32-column gdn_scan_tc for packed batches, shard summaries and the backward's
+// recompute).
 cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
     static int nsm[64];
     int dev = 0;
@@ -2394,7 +2709,10 @@ cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
         nsm[dev] = n > 0 ? n : 1;
     }
     const int64_t rows = p.cu_seqlens ? (int64_t)p.N * p.H : (int64_t)p.B * p.H * (p.scan_mode == 1 ? 2 : 1);
-    return rows * ScanLayout<16>::kSlices <= nsm[dev] ? launch_scan_w<16>(p, stream) : launch_scan_w<32>(p, stream);
+    if (rows * ScanLayout<16>::kSlices <= nsm[dev]) return launch_scan_w<16>(p, stream);
+    // more chains than one wave of one-per-SM CTAs: two chains per SM (fixed-length forward)
+    if (!p.cu_seqlens && p.scan_mode == 0 && !p.states) return launch_scan_lean(p, stream);
+    return launch_scan_w<32>(p, stream);
 }
 
 cudaError_t launch_bwd_states_tc(const BwdParams& p, cudaStream_t stream) {
