@@ -1,6 +1,7 @@
 """Small, fixed workloads for running a profiler (ncu) on this package's kernels.
 
     python -m llms_from_scratch_b200.profile chunk     # chunked forward, B=1, T=4096, H=16 (bench shape), 4 calls
+    python -m llms_from_scratch_b200.profile batched   # chunked forward, B=8, T=4096, H=16 (the lean scan), 3 calls
     python -m llms_from_scratch_b200.profile rec       # recurrent decode step, B=32, H=16, 4 calls
     python -m llms_from_scratch_b200.profile decode    # decoder: prefill 26 tokens + 8 decode steps, batch 32
 
@@ -39,6 +40,11 @@ def main(argv=None) -> int:
         for _ in range(4):
             fast_chunk_gated_delta_rule(q, k, v, g, beta, initial_state=s0, output_final_state=True,
                                         use_qk_l2norm_in_kernel=True)
+    elif what == "batched":  # 128 (b, h) chains: gdn_scan_lean_tc; 1.2 GB of records
+        q, k, v, g, beta, s0 = _inputs(8, 4096, 16, gen)
+        for _ in range(3):
+            fast_chunk_gated_delta_rule(q, k, v, g, beta, initial_state=s0, output_final_state=True,
+                                        use_qk_l2norm_in_kernel=True)
     elif what == "rec":
         q, k, v, g, beta, s0 = _inputs(32, 1, 16, gen)
         for _ in range(4):
@@ -49,7 +55,7 @@ def main(argv=None) -> int:
         prompt = torch.randint(0, QWEN3_5_0_8B["vocab_size"], (32, 26), device="cuda", generator=gen)
         dec.generate(prompt, 8, use_graph=False)
     else:
-        print(f"unknown workload {what!r}: chunk | rec | decode", file=sys.stderr)
+        print(f"unknown workload {what!r}: chunk | batched | rec | decode", file=sys.stderr)
         return 2
     torch.cuda.synchronize()
     print("ok")
