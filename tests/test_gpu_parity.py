@@ -212,6 +212,39 @@ def test_batch_independence_config3_sample():
         torch.testing.assert_close(sb, s[b:b + 1], rtol=0, atol=0)
 
 
+@pytest.mark.parametrize("B,T,H,with_state,ofs", [
+    (3, 777, 8, True, True),     # 24 (b, h) chains: the lean scan (more than one wave of 16-column slices); ragged
+    (2, 65, 16, False, True),    # two chunks, the second of one token, zero start
+    (4, 300, 6, True, False),    # no final state
+])
+def test_many_chains_ragged_vs_oracle(B, T, H, with_state, ofs):
+    """More (b, h) chains than the 16-column scan fits in one wave (B*H > 18): the lean scan, held to the
+    oracle on ragged lengths, with and without initial and final states; and each sequence equals its own
+    B=1 call (16-column scan) bit for bit."""
+    m = ops()
+    q, k, v, g, beta, s0 = O.make_inputs(B, T, H, seed=40 + T, in_dtype="bf16", init_state_std=0.02,
+                                         normalize_qk=False)
+    s0 = s0 if with_state else None
+    ro, rs = O.chunk_gated_delta_rule(q, k, v, g, beta, initial_state=s0, output_final_state=True,
+                                      use_qk_l2norm_in_kernel=True, in_dtype="bf16")
+    tq, tk, tv = (dev(x, torch.bfloat16) for x in (q, k, v))
+    tg, tb, ts = dev(g), dev(beta), dev(s0)
+    o, s = m.fast_chunk_gated_delta_rule(tq, tk, tv, tg, tb, initial_state=ts, output_final_state=ofs,
+                                         use_qk_l2norm_in_kernel=True)
+    assert_parity(o.float().cpu().numpy(), ro, "bf16", "out")
+    if ofs:
+        assert_parity(s.cpu().numpy(), rs, "bf16", "final_state")
+    else:
+        assert s is None
+    for b in (0, B - 1):
+        ob, sb = m.fast_chunk_gated_delta_rule(tq[b:b + 1], tk[b:b + 1], tv[b:b + 1], tg[b:b + 1], tb[b:b + 1],
+                                               initial_state=None if ts is None else ts[b:b + 1],
+                                               output_final_state=ofs, use_qk_l2norm_in_kernel=True)
+        assert torch.equal(ob, o[b:b + 1])
+        if ofs:
+            assert torch.equal(sb, s[b:b + 1])
+
+
 def test_config3_full_size_sequences_vs_oracle():
     """Config 3 at full size (B=64, T=4096, H=16, bf16, initial state ~ N(0, 0.02)): three sequences of the
     batched call against the oracle, each on its own."""
