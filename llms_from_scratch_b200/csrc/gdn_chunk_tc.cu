@@ -66,6 +66,22 @@ constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s; a healthy wait here takes m
 
 __device__ __forceinline__ void report(unsigned int* err, unsigned int bit) { report_device_error(err, bit); }
 
+// The scans hand each chunk's state to their MMA-issue warp through a named barrier: the state warps arrive
+// (bar.arrive), the MMA warp waits (bar.sync) and then stores the number of barrier steps it has passed in
+// `synced`.  A state warp that has given up (a failed wait) still takes every arrival, so that the MMA warp's
+// syncs are never short of one, but first waits here until the MMA warp has passed the previous step.  The
+// barrier counts threads, not steps: without this wait a warp that skips its work could arrive twice while
+// another has not arrived once, complete a step without the MMA warp and leave its last sync waiting for good.
+// The MMA warp waits on nothing unbounded except that barrier, so the wait ends; it is bounded all the same.
+__device__ __forceinline__ void wait_barrier_step(const int* synced, int step) {
+    const long long t0 = clock64();
+    while (*reinterpret_cast<const volatile int*>(synced) < step && clock64() - t0 < (long long)(kWaitNs * 2)) {
+    }
+}
+__device__ __forceinline__ void mark_barrier_step(int* synced, int step, int lane) {
+    if (lane == 0) *reinterpret_cast<volatile int*>(synced) = step;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&h);
@@ -799,6 +815,7 @@ struct ScanMisc {
     uint64_t mma_o[2];     // output accumulator of chunk c ready, alternating by chunk parity
     uint32_t tmem;
     int abort;
+    int synced;            // named-barrier steps the MMA warp has passed
 };
 
 __device__ __forceinline__ bool scan_aborted(const ScanMisc& ms) {
@@ -887,6 +904,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
         mbar_init(&ms.mma_o[0], 1);
         mbar_init(&ms.mma_o[1], 1);
         ms.abort = 0;
+        ms.synced = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -911,6 +929,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
         for (int c = 0; c < NC; ++c) {
             const int s = c & 1;
             named_bar_sync(kScanBarS, kScanBarCount);  // S_c is in operand tile s
+            mark_barrier_step(&ms.synced, c + 1, lane);
             bool go = ok && !scan_aborted(ms);
             if (go) go = mbar_wait(&ms.full_mq[s], (c >> 1) & 1, kWaitNs);
             if (!__all_sync(0xffffffffu, go)) {  // the warp decides together
@@ -1035,6 +1054,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) gdn_scan_tc(ChunkParams p) {
                     fence_proxy_async_smem();
                 }
                 tc_fence_before();
+                if (!ok) wait_barrier_step(&ms.synced, c + 1);  // the MMA warp has passed step c
                 named_bar_arrive(kScanBarS, kScanBarCount);
             }
             // ---- outputs of chunk c, overlapping chunk c+1's MMAs
@@ -1117,6 +1137,7 @@ struct LeanMisc {
     uint64_t done;       // every product the MMA warp issued has completed
     uint32_t tmem;
     int abort;           // a party gave up: the others stop waiting and skip their work
+    int synced;          // named-barrier steps the MMA warp has passed
 };
 
 // Byte offset of element (row, col), col < 32, in an MN-major 64B-swizzled tile of 16-bit elements: 64-byte
@@ -1180,6 +1201,7 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gdn_scan_lean_tc(ChunkParams 
         mbar_init(&ms.mma_s, 1);
         mbar_init(&ms.done, 1);
         ms.abort = 0;
+        ms.synced = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -1204,6 +1226,7 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gdn_scan_lean_tc(ChunkParams 
         for (int c = 0; c < NC; ++c) {
             const int s = c & 1;
             named_bar_sync(kLeanBar, kLeanBarCount);  // S_c is in operand tile s
+            mark_barrier_step(&ms.synced, c + 1, lane);
             bool go = ok && !lean_aborted(ms);
             if (go) go = lean_wait(&ms.full_m[s], (c >> 1) & 1, ms);
             if (!__all_sync(0xffffffffu, go)) {
@@ -1320,6 +1343,7 @@ __global__ void __launch_bounds__(kLeanThreads, 2) gdn_scan_lean_tc(ChunkParams 
             }
             if (c + 1 < NC) {
                 tc_fence_before();
+                if (!ok) wait_barrier_step(&ms.synced, c + 1);  // the MMA warp has passed step c
                 named_bar_arrive(kLeanBar, kLeanBarCount);  // every chunk, also after a failure
             }
             if (ok && c + 2 < NC) load_cm<128, 16>(record(c + 2) + kTcB, dk, dv0 + cb, bc);  // bc is free: b_{c+2}
@@ -1401,6 +1425,7 @@ struct BsMisc {
     uint64_t mma;
     uint32_t tmem;
     int abort;
+    int synced;  // named-barrier steps the MMA warp has passed
 };
 
 __device__ __forceinline__ bool bs_aborted(const BsMisc& ms) { return *reinterpret_cast<const volatile int*>(&ms.abort) != 0; }
@@ -1423,6 +1448,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
         }
         mbar_init(&ms.mma, 1);
         ms.abort = 0;
+        ms.synced = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -1443,6 +1469,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
         for (int it = 0; it < NC; ++it) {
             const int s = it & 1;
             named_bar_sync(kBsBar, kBsBarCount);  // dS_{c+1} is in operand tile s
+            mark_barrier_step(&ms.synced, it + 1, lane);
             bool go = ok && !bs_aborted(ms);
             if (go) go = mbar_wait(&ms.full_mq[s], (it >> 1) & 1, kWaitNs);
             if (go) go = mbar_wait(&ms.full_do[s], (it >> 1) & 1, kWaitNs);
@@ -1533,6 +1560,7 @@ __global__ void __launch_bounds__(kBsThreads, 1) gdn_bwd_scan_tc(BwdParams p) {
                 fence_proxy_async_smem();
             }
             tc_fence_before();
+            if (!ok) wait_barrier_step(&ms.synced, it);  // the MMA warp has passed step it - 1
             named_bar_arrive(kBsBar, kBsBarCount);
             // dS_{c+1} (fp32) for the chunk kernels, while the MMAs run: the warp's 32 rows, this CTA's columns
             store_rows_coalesced<kBsCols>(reinterpret_cast<float*>(sm + B_XPOSE) + warp * 32 * (kBsCols + 4), S,
