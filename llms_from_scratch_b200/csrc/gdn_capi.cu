@@ -109,22 +109,20 @@ bool valid_dtype(int d) { return d == GDN_F32 || d == GDN_BF16 || d == GDN_F16; 
 
 // The kernels are compiled for sm_100a only; anything else cannot load them.
 int check_device() {
-    static int major_of[64];
-    static bool known[64];
+    static std::atomic<int> major_plus1[64];  // compute capability major + 1 per device; 0 = not yet read
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     if (dev < 0 || dev >= 64) return fail(GDN_ERR_DEVICE, "device ordinal %d out of range", dev);
-    if (!known[dev]) {
-        int major = 0;
+    int major = major_plus1[dev].load(std::memory_order_relaxed) - 1;
+    if (major < 0) {
         e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
         if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-        major_of[dev] = major;
-        known[dev] = true;
+        major_plus1[dev].store(major + 1, std::memory_order_relaxed);
     }
-    if (major_of[dev] != 10)
+    if (major != 10)
         return fail(GDN_ERR_DEVICE, "device %d has compute capability %d.x; this library is built for sm_100a (B200)",
-                    dev, major_of[dev]);
+                    dev, major);
     return GDN_OK;
 }
 

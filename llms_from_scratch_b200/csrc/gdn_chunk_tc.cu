@@ -2728,16 +2728,17 @@ cudaError_t launch_scan_lean(const ChunkParams& p, cudaStream_t stream) {
 // 32-column chains per SM (the 32-column gdn_scan_tc for packed batches, shard summaries and the backward's
 // recompute).
 cudaError_t launch_chunk_tc_scan(const ChunkParams& p, cudaStream_t stream) {
-    static int nsm[64];
+    static std::atomic<int> nsm_cache[64];  // SM count per device, filled on first use (any host thread)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-    if (!nsm[dev]) {
-        int n = 0;
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        nsm[dev] = n > 0 ? n : 1;
+    int nsm = nsm_cache[dev].load(std::memory_order_relaxed);
+    if (!nsm) {
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        if (nsm <= 0) nsm = 1;
+        nsm_cache[dev].store(nsm, std::memory_order_relaxed);
     }
     const int64_t rows = p.cu_seqlens ? (int64_t)p.N * p.H : (int64_t)p.B * p.H * (p.scan_mode == 1 ? 2 : 1);
-    if (rows * ScanLayout<16>::kSlices <= nsm[dev]) return launch_scan_w<16>(p, stream);
+    if (rows * ScanLayout<16>::kSlices <= nsm) return launch_scan_w<16>(p, stream);
     // more chains than one wave of one-per-SM CTAs: two chains per SM (fixed-length forward)
     if (!p.cu_seqlens && p.scan_mode == 0 && !p.states) return launch_scan_lean(p, stream);
     return launch_scan_w<32>(p, stream);
